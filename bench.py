@@ -1,0 +1,340 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 logits-to-token path on the batched-sampler workload.
+
+Workload: B=32 rows x V=151,936 fp32 logits ~ N(0, 2.5^2) per GPU, per-row
+parameters from a seed (T ~ U[0.3,1.2] with 25% greedy, top-k in {0,20,40,100}, top-p ~
+U[0.7,1.0], repetition penalty ~ U[1.0,1.3], Adaptive mode), histories of 256-8,192 ids. A step is
+one fused sampler launch (sixi_smp_sample) over one batch. Rows are independent, so N GPUs run
+N batches with no collective (weak scaling); the timed region is bracketed by a barrier and
+device synchronisation and its length is the max over ranks of the CUDA-event time.
+
+  value         rows/s over all ranks, inputs resident in HBM (16 rotating batches, 311 MB per
+                GPU > 126 MB L2, so every step reads its logits from HBM)
+  e2e           rows/s through sixi_smp_sample_host: pinned host logits -> device -> tokens back
+  roofline      algorithmic bytes per launch (logits + histories) / CUDA-event time per launch
+  cpu_baseline  the engine's own CPU sampler (oracle/_ref) on all host threads, rank 0 at N=1
+
+`--impl reference` times the engine's CPU sampler alone on the same workload (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+sys.path.insert(0, str(REPO / "sixi-asi_b200"))
+
+METRIC = "sampled rows/s at B=32,V=151,936 fp32; HBM GB/s vs B200 peak; 1/2/4/8 GPU"
+UNIT = "rows/s"
+ROWS = 32
+VOCAB = 151_936
+NBUF = 16
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def dist_env() -> tuple[int, int, int]:
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.tmp = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.tmp.flush()
+        rows = []
+        for line in Path(self.tmp.name).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append(f)
+            except Exception:
+                pass
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def make_batches(seed: int):
+    from sixi_smp import workloads as W
+
+    base = W.config2(rows=ROWS, vocab=VOCAB, seed=seed)
+    rng = np.random.default_rng(seed + 17)
+    logits = [base["logits"]] + [rng.normal(0.0, 2.5, size=(ROWS, VOCAB)).astype(np.float32)
+                                 for _ in range(NBUF - 1)]
+    uniforms = [rng.random(ROWS) for _ in range(NBUF)]
+    return base, logits, uniforms
+
+
+def algorithmic_bytes(base: dict) -> int:
+    return ROWS * VOCAB * 4 + 4 * int(base["hist_off"][-1])
+
+
+def cpu_reference_rows_per_s(base, logits, uniforms, budget_s: float, n_threads: int = 0):
+    """Times the engine's own CPU sampler (or the C restatement when the reference build is absent)
+    on full batches until `budget_s` elapses. Returns (rows/s, kind, threads, sample text)."""
+    from oracle import binding
+
+    orc = binding.reference() or binding.port()
+    threads = n_threads or os.cpu_count() or 1
+    done = 0
+    t0 = time.perf_counter()
+    i = 0
+    while True:
+        orc.sample_batch(logits[i % len(logits)], base["params"], None, base["hist"], base["hist_off"],
+                         uniforms[i % len(uniforms)], n_threads=threads)
+        done += ROWS
+        i += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return done / el, orc.kind, threads, f"{i} batches of {ROWS} rows ({el:.1f} s wall, {threads} threads)"
+
+
+def run_reference(args) -> int:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    base, logits, uniforms = make_batches(1000)
+    from oracle import binding
+
+    orc = binding.reference()
+    kind = "reference"
+    if orc is None:
+        orc = binding.port()
+        kind = "port"
+    threads = os.cpu_count() or 1
+    # size each step so that warmup + K steps stay within about 90 s
+    t0 = time.perf_counter()
+    orc.sample_batch(logits[0], base["params"], None, base["hist"], base["hist_off"], uniforms[0],
+                     n_threads=threads)
+    per_batch = time.perf_counter() - t0
+    total_steps = max(1, args.steps + args.warmup)
+    rows_per_step = ROWS
+    if per_batch * total_steps > 90.0:
+        rows_per_step = max(1, int(ROWS * 90.0 / (per_batch * total_steps)))
+    lg = [np.ascontiguousarray(x[:rows_per_step]) for x in logits]
+    prm = base["params"][:rows_per_step]
+    hoff = base["hist_off"][:rows_per_step + 1]
+    hist = base["hist"][:int(hoff[-1])]
+    for i in range(args.warmup):
+        orc.sample_batch(lg[i % NBUF], prm, None, hist, hoff, uniforms[i % NBUF][:rows_per_step], n_threads=threads)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        orc.sample_batch(lg[i % NBUF], prm, None, hist, hoff, uniforms[i % NBUF][:rows_per_step], n_threads=threads)
+    el = time.perf_counter() - t0
+    value = rows_per_step * args.steps / el
+    sample = f"{rows_per_step} of {ROWS} rows per step, {args.steps} steps, {threads} threads"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / max(1, args.steps),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": "config2 batched sampler", "rows": ROWS, "vocab": VOCAB},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    import sixi_smp as S
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    base, logits, uniforms = make_batches(1000 + rank)
+    d_logits = [torch.from_numpy(x).to(dev) for x in logits]
+    d_u = [torch.from_numpy(u).to(dev) for u in uniforms]
+    d_params = torch.from_numpy(base["params"].view(np.uint8)).to(dev)
+    d_hist = torch.from_numpy(base["hist"]).to(dev)
+    d_hoff = torch.from_numpy(base["hist_off"]).to(dev)
+    smp = S.Sampler(local, 1024, VOCAB)
+    tok = torch.empty(ROWS, dtype=torch.int32, device=dev)
+    sts = torch.empty(ROWS, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(i: int, s) -> None:
+        smp.sample(d_logits[i % NBUF], d_params, hist=d_hist, hist_off=d_hoff, uniforms=d_u[i % NBUF],
+                   out_tokens=tok, out_status=sts, stream=s)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i, stream)
+    stream.synchronize()
+    assert int((sts != 0).sum()) == 0, f"statuses {sts.tolist()}"
+    # the K timed steps are captured once in a CUDA graph (launch-bound otherwise: one ~6 us launch
+    # per step from Python)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(args.steps):
+            step(i, torch.cuda.current_stream())
+    graph.replay()
+    stream.synchronize()
+
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.05)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    e1.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    ms_per_step = ms_max / args.steps
+    value = world * ROWS * args.steps / (ms_max / 1e3)
+
+    # roofline of the fused launch (this rank)
+    bytes_per_launch = algorithmic_bytes(base)
+    achieved = bytes_per_launch / (ms / args.steps / 1e3) / 1e9
+    peak, peak_kind = peaks()
+
+    # end to end through the host entry point: pinned host logits in, tokens out
+    e2e = None
+    if args.e2e_steps > 0:
+        h_logits = torch.from_numpy(logits[0]).pin_memory()
+        h_np = h_logits.numpy()
+        h_params = torch.from_numpy(base["params"].view(np.uint8)).pin_memory().numpy().view(S.PARAMS_DTYPE)
+        h_hist = torch.from_numpy(base["hist"]).pin_memory().numpy()
+        h_hoff = torch.from_numpy(base["hist_off"]).pin_memory().numpy()
+        h_u = torch.from_numpy(uniforms[0]).pin_memory().numpy()
+        h_tok = torch.empty(ROWS, dtype=torch.int32).pin_memory().numpy()
+        h_st = torch.empty(ROWS, dtype=torch.int32).pin_memory().numpy()
+        for _ in range(3):
+            smp.sample_host(h_np, h_params, hist=h_hist, hist_off=h_hoff, uniforms=h_u, out_tokens=h_tok,
+                            out_status=h_st, stream=stream)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            smp.sample_host(h_np, h_params, hist=h_hist, hist_off=h_hoff, uniforms=h_u, out_tokens=h_tok,
+                            out_status=h_st, stream=stream)
+        el = time.perf_counter() - t0
+        el_max = el
+        if world > 1:
+            t = torch.tensor([el], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            el_max = float(t.item())
+        h2d = h_np.nbytes + h_params.nbytes + h_hist.nbytes + h_hoff.nbytes + h_u.nbytes
+        e2e = {"value": world * ROWS * args.e2e_steps / el_max, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(h_tok.nbytes + h_st.nbytes)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, kind, threads, sample = cpu_reference_rows_per_s(base, logits, uniforms, args.cpu_budget)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample}
+
+    if world > 1:
+        del graph
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config2 batched sampler", "rows_per_gpu": ROWS, "vocab": VOCAB,
+                       "parallelism": f"rows partitioned, {world} GPU(s), no collective",
+                       "l2": f"inputs larger than L2: {NBUF} rotating batches, "
+                             f"{NBUF * ROWS * VOCAB * 4 / 1e6:.0f} MB per GPU"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+                         "bytes_per_launch": bytes_per_launch},
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "gpu_launches": args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    smp.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

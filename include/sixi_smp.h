@@ -1,0 +1,215 @@
+/*
+ * sixi_smp.h - C ABI of the B200 logits-to-token path (sampler chain, grammar-mask application,
+ * speculative verifier) of the Sixi-ASI engine.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes, and returns an int32 status
+ * whose values are the engine's `sixi_asi::ErrorCode` integers (include/sixi_asi/common.hpp:40-66
+ * in the engine). Device-side failures of a single row (NaN/Inf logits, all-masked row, bad
+ * draft id) are reported per row in `out_status` and never trap the GPU.
+ *
+ * Unless stated otherwise all array arguments are DEVICE pointers, every call is asynchronous on
+ * the caller's CUDA stream (`stream` is a `cudaStream_t` passed as `void*`, NULL = legacy default
+ * stream) and performs no host synchronisation. The handle owns device workspace only; it is not
+ * thread-safe (one handle per host thread or external serialisation), matching the engine, where
+ * device access is serialised by the batch leader (src/core/core_execution.cpp:1398-1530).
+ */
+#ifndef SIXI_SMP_H
+#define SIXI_SMP_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SIXI_SMP_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define SIXI_SMP_API __attribute__((visibility("default")))
+#else
+#define SIXI_SMP_API
+#endif
+
+/* Status codes: the engine's ErrorCode values (include/sixi_asi/common.hpp:40-66). */
+enum {
+    SIXI_OK = 0,
+    SIXI_INVALID_ARGUMENT = 1,
+    SIXI_OUT_OF_BOUNDS = 2,
+    SIXI_OUT_OF_MEMORY_VRAM = 11,
+    SIXI_NUMERIC_NAN_OR_INF = 16,
+    SIXI_BACKEND_ERROR = 23,
+    SIXI_UNSUPPORTED_HARDWARE = 24
+};
+
+/* Logits element type. */
+enum { SIXI_SMP_F32 = 0, SIXI_SMP_BF16 = 1 };
+
+/* ExecutionMode (include/sixi_asi/common.hpp:133-136): penalties apply only in Adaptive. */
+enum { SIXI_SMP_STRICT_REPLAY = 0, SIXI_SMP_ADAPTIVE = 1 };
+
+/* sixi_smp_params.flags */
+enum {
+    SIXI_SMP_ROW_MASKED = 1u /* apply this row's grammar bitmask (mask_words row) */
+};
+
+/*
+ * Per-row (sampler) or per-stream (verifier) sampling parameters. Mirrors
+ * sixi_asi::core::SamplingParams (include/sixi_asi/core_execution.hpp:136-144); `min_p` and
+ * `frequency_penalty` are extensions that are identity at 0 (they do not exist in the engine).
+ * Uniform draws, when not supplied by the caller, come from Philox4x32-10 with
+ * key = seed and counter = {slot, 0, lo32(counter + step), hi32(counter + step)}.
+ */
+typedef struct sixi_smp_params {
+    float temperature;        /* <= 0: greedy argmax, lowest id wins ties, consumes no uniform */
+    int32_t top_k;            /* <= 0 or >= allowed vocab: no top-k truncation */
+    float top_p;              /* truncation applied when 0 < top_p < 1 (crossing token kept) */
+    float min_p;              /* extension: keep prob >= min_p * max prob; 0 = off */
+    float repetition_penalty; /* 1 = off; v<0 ? v*rep : v/rep once per unique history id */
+    float presence_penalty;   /* 0 = off; subtracted once per unique history id */
+    float frequency_penalty;  /* extension: subtracted once per history occurrence; 0 = off */
+    uint32_t mode;            /* SIXI_SMP_STRICT_REPLAY or SIXI_SMP_ADAPTIVE */
+    uint32_t flags;           /* SIXI_SMP_ROW_MASKED */
+    uint32_t reserved;
+    uint64_t seed;            /* Philox key */
+    uint64_t counter;         /* Philox counter base (e.g. the request's decode step) */
+} sixi_smp_params;
+
+/* A batch of logits rows in device memory: row r starts at data + r * row_stride elements. */
+typedef struct sixi_smp_rows {
+    const void* data;
+    uint32_t dtype;       /* SIXI_SMP_F32 or SIXI_SMP_BF16 */
+    uint32_t n_rows;
+    uint64_t row_stride;  /* in elements, >= vocab */
+} sixi_smp_rows;
+
+typedef struct sixi_smp sixi_smp; /* opaque handle */
+
+/* Creates a handle bound to `device` for rows of `vocab` entries. Replaces the construction of the
+ * engine's sampler state; the engine's DeterministicSampler is stateless
+ * (include/sixi_asi/core_execution.hpp:146-183), so the handle holds only device workspace for
+ * up to `max_rows` rows per call and the launch configuration. */
+SIXI_SMP_API int32_t sixi_smp_create(int32_t device, uint32_t max_rows, uint32_t vocab, sixi_smp** out);
+SIXI_SMP_API int32_t sixi_smp_destroy(sixi_smp* h);
+SIXI_SMP_API uint32_t sixi_smp_vocab(const sixi_smp* h);
+SIXI_SMP_API uint32_t sixi_smp_mask_words(const sixi_smp* h); /* ceil(vocab / 32) */
+SIXI_SMP_API const char* sixi_smp_status_string(int32_t status);
+
+/*
+ * Fused sampler over a batch of rows: grammar mask -> NaN/Inf check -> penalties -> greedy argmax
+ * or top-k -> temperature softmax -> top-p -> min-p -> draw. One token per row.
+ * Replaces DeterministicSampler::sample_token / compute_sampling_candidates /
+ * sample_from_candidates (src/core/core_execution.cpp:449-619).
+ *   params      [n_rows]
+ *   mask_words  [n_rows][sixi_smp_mask_words(h)] or NULL; bit (i % 32) of word (i / 32) set =
+ *               token i allowed; used by rows whose params.flags has SIXI_SMP_ROW_MASKED
+ *   hist_tokens/hist_offsets: CSR token history, row r = hist_tokens[hist_offsets[r] ..
+ *               hist_offsets[r+1]); hist_tokens may be NULL (no history)
+ *   uniforms    [n_rows] in [0,1) or NULL (Philox slot 0); greedy rows consume none
+ *   out_tokens  [n_rows] (-1 on error), out_status [n_rows]
+ */
+SIXI_SMP_API int32_t sixi_smp_sample(sixi_smp* h, const sixi_smp_rows* rows, const sixi_smp_params* params,
+                        const uint32_t* mask_words, const int32_t* hist_tokens,
+                        const int64_t* hist_offsets, const double* uniforms, uint64_t step,
+                        int32_t* out_tokens, int32_t* out_status, void* stream);
+
+/*
+ * Same as sixi_smp_sample with HOST inputs and outputs: copies the logits (pinned host memory
+ * recommended), params, masks, histories and uniforms to handle-owned device staging, samples, and
+ * copies tokens and statuses back, then synchronises `stream`. This is the engine-facing call
+ * shape of DeterministicSampler::sample_token (src/core/core_execution.cpp:603-619), which takes
+ * host logits. The staging buffers grow on demand: the first call with a larger batch allocates.
+ */
+SIXI_SMP_API int32_t sixi_smp_sample_host(sixi_smp* h, const void* host_logits, uint32_t dtype,
+                             uint32_t n_rows, uint64_t row_stride,
+                             const sixi_smp_params* host_params, const uint32_t* host_mask_words,
+                             const int32_t* host_hist_tokens, const int64_t* host_hist_offsets,
+                             const double* host_uniforms, uint64_t step, int32_t* host_out_tokens,
+                             int32_t* host_out_status, void* stream);
+
+/*
+ * Greedy argmax per row on the raw (optionally masked) logits, lowest id on ties; a NaN at index 0
+ * yields 0 and other NaNs never win, exactly as DeterministicSampler::sample_greedy_argmax
+ * (src/core/core_execution.cpp:394-407). Replaces the llama.cpp greedy sampler hook
+ * (set_gpu_greedy_sampling_enabled / forward_sequence_greedy_argmax,
+ * src/core/core_execution.cpp:3067-3104, 3847-3923). `mask_words`, when not NULL, masks every row.
+ */
+SIXI_SMP_API int32_t sixi_smp_greedy_argmax(sixi_smp* h, const sixi_smp_rows* rows, const uint32_t* mask_words,
+                               int32_t* out_tokens, int32_t* out_status, void* stream);
+
+/*
+ * Diagnostic / parity: the sorted candidate list (logit desc, id asc) that a row's draw uses, i.e.
+ * compute_sampling_candidates (src/core/core_execution.cpp:449-584). Writes the first
+ * min(max_out, n) candidates of each row into out_ids/out_probs [n_rows][max_out] and the full
+ * candidate count n into out_count. max_out <= 256.
+ */
+SIXI_SMP_API int32_t sixi_smp_candidates(sixi_smp* h, const sixi_smp_rows* rows, const sixi_smp_params* params,
+                            const uint32_t* mask_words, const int32_t* hist_tokens,
+                            const int64_t* hist_offsets, uint32_t max_out, int32_t* out_ids,
+                            double* out_probs, int32_t* out_count, int32_t* out_status,
+                            void* stream);
+
+/*
+ * Speculative verification of n_streams streams with k drafted tokens each.
+ *   target      n_streams * (k + 1) rows; row s*(k+1)+i is the target distribution that verifies
+ *               draft i (i < k); row s*(k+1)+k draws the bonus token on full acceptance.
+ *   draft_probs [n_streams][k][row_stride] fp32 dense draft distributions q, or NULL for one-hot
+ *               drafts. Dense q follows SpeculativeDecoder::step's verification with draft
+ *               probabilities (src/speculative/speculative.cpp:801-916): accept with
+ *               min(1, p/q), residual max(0, p - q) drawn in vocab-id order. NULL follows the
+ *               fast path (src/speculative/speculative.cpp:589-692): accept with p, residual =
+ *               candidates without the draft, drawn in candidate order.
+ *   drafts      [n_streams][k]; n_drafts [n_streams] or NULL (= k for every stream)
+ *   params      [n_streams]; temperature <= 0 selects greedy match (argmax of raw logits)
+ *   mask_words  [n_streams * (k + 1)][mask words] or NULL; used by streams with
+ *               SIXI_SMP_ROW_MASKED
+ *   hist_*      CSR per-stream base history (the context; for one-hot drafts include the anchor).
+ *               Row i is penalised with base + drafts[0..i-1]; the bonus row with base only for
+ *               dense q (speculative.cpp:908-915) and base + all drafts for one-hot.
+ *   uniforms    [n_streams][k + 1] or NULL (Philox slots 0..k). The uniforms are consumed in
+ *               order exactly like the engine's DeterministicRng: one per examined draft, then one
+ *               for the residual or bonus draw; out_uniforms_used reports how many.
+ *   outputs     out_accepted [S], out_tokens [S][k+1] (committed tokens, -1 padded),
+ *               out_n_tokens [S], out_first_reject [S] (-1 on full accept),
+ *               out_uniforms_used [S], out_status [S]
+ */
+SIXI_SMP_API int32_t sixi_smp_verify(sixi_smp* h, const sixi_smp_rows* target, const float* draft_probs,
+                        const int32_t* drafts, const int32_t* n_drafts, uint32_t n_streams,
+                        uint32_t k, const sixi_smp_params* params, const uint32_t* mask_words,
+                        const int32_t* hist_tokens, const int64_t* hist_offsets,
+                        const double* uniforms, uint64_t step, int32_t* out_accepted,
+                        int32_t* out_tokens, int32_t* out_n_tokens, int32_t* out_first_reject,
+                        int32_t* out_uniforms_used, int32_t* out_status, void* stream);
+
+/*
+ * Vocab-sharded mode (logits produced vocab-parallel; no counterpart in the engine, which runs on
+ * one device). Stage 1 on every rank: for each row of this rank's vocab shard
+ * [vocab_offset, vocab_offset + shard_vocab), apply mask and penalties and emit the shard's best
+ * `top_n` (<= 64) candidates (adjusted logit, global id; sorted logit desc, id asc; padded with
+ * -inf / -1), the shard max, sum of exp((v - max) / T) over the shard and the allowed count.
+ *   mask_words  full-vocabulary masks [n_rows][ceil(full_vocab/32)]; the shard reads its bit range
+ *   out_cand    [n_rows][top_n] of {float logit; int32 id} (8 bytes each)
+ *   out_stats   [n_rows] of {float max; int32 n_allowed; double sum_exp; int32 status; int32 pad}
+ * Stage 2 (after an all-gather of both arrays over the ranks) on every rank: merge n_shards
+ * shards per row into the final token, identically on every rank. Exact for top_k <= top_n; rows
+ * whose top-k or top-p set is not contained in the gathered candidates report
+ * SIXI_OUT_OF_BOUNDS in out_status.
+ */
+SIXI_SMP_API int32_t sixi_smp_shard_candidates(sixi_smp* h, const sixi_smp_rows* shard_rows,
+                                  uint32_t vocab_offset, uint32_t full_vocab,
+                                  const sixi_smp_params* params, const uint32_t* mask_words,
+                                  const int32_t* hist_tokens, const int64_t* hist_offsets,
+                                  uint32_t top_n, void* out_cand, void* out_stats, void* stream);
+SIXI_SMP_API int32_t sixi_smp_merge_shards(sixi_smp* h, uint32_t n_rows, uint32_t n_shards, uint32_t top_n,
+                              const void* gathered_cand, const void* gathered_stats,
+                              const sixi_smp_params* params, const double* uniforms, uint64_t step,
+                              int32_t* out_tokens, int32_t* out_status, void* stream);
+
+/* Philox4x32-10 uniform used when `uniforms` is NULL (host copy of the device function). */
+SIXI_SMP_API double sixi_smp_philox_uniform(uint64_t seed, uint64_t counter, uint32_t slot);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* SIXI_SMP_H */

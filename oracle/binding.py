@@ -1,0 +1,144 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes binding of the CPU oracle (parity checker).
+
+Loads either implementation of oracle/sixi_oracle.h:
+  port()       liboracle.so        - plain-C restatement of the engine's sampler and verifier
+  reference()  _ref/libsixiref.so  - the engine's own DeterministicSampler built from its sources
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this module; the product
+library never calls it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+PORT_PATH = HERE / "liboracle.so"
+REF_PATH = HERE / "_ref" / "libsixiref.so"
+UNSUPPORTED = -2
+
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_U32 = ctypes.c_uint32
+_U64 = ctypes.c_uint64
+
+_SIGS = {
+    "orc_kind": (_I32, []),
+    "orc_philox_uniform": (ctypes.c_double, [_U64, _U64, _U32]),
+    "orc_greedy_argmax": (_I32, [_P, _U64]),
+    "orc_greedy_row": (_I32, [_P, _U32, _U64, _P, _P]),
+    "orc_candidates": (_I32, [_P, _U32, _U64, _P, _P, _U64, _P, _U64, _P, _P, _P]),
+    "orc_sample": (_I32, [_P, _U32, _U64, _P, _P, _U64, _P, ctypes.c_double, _P]),
+    "orc_sample_batch": (_I32, [_P, _U32, _U32, _U64, _U64, _P, _P, _P, _P, _P, _U64, _P, _P, _I32]),
+    "orc_verify": (_I32, [_P, _U32, _U64, _U64, _P, _P, _P, _U32, _U32, _P, _P, _P, _P, _P, _U64,
+                          _P, _P, _P, _P, _P, _P, _I32]),
+}
+
+
+def build() -> None:
+    """Builds liboracle.so and, when the reference sources are present, _ref/libsixiref.so."""
+    subprocess.run(["make", "-s", "-C", str(HERE), "-j8"], check=True)
+
+
+def _p(a) -> int:
+    return 0 if a is None else a.ctypes.data
+
+
+def _dtype_of(a: np.ndarray) -> int:
+    return 1 if a.dtype == np.uint16 else 0
+
+
+class Oracle:
+    def __init__(self, path: Path):
+        self.path = Path(path)
+        self.lib = ctypes.CDLL(str(self.path))
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(self.lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        self.kind = "reference" if self.lib.orc_kind() == 1 else "port"
+
+    def philox_uniform(self, seed: int, counter: int, slot: int) -> float:
+        return float(self.lib.orc_philox_uniform(seed, counter, slot))
+
+    def greedy_argmax(self, x: np.ndarray) -> int:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        return int(self.lib.orc_greedy_argmax(_p(x), x.size))
+
+    def greedy_row(self, row: np.ndarray, mask=None) -> tuple[int, int]:
+        row = np.ascontiguousarray(row)
+        tok = np.zeros(1, dtype=np.int32)
+        st = self.lib.orc_greedy_row(_p(row), _dtype_of(row), row.size, _p(mask), _p(tok))
+        return int(st), int(tok[0])
+
+    def candidates(self, row: np.ndarray, params: np.ndarray, hist=None, mask=None, cap=None):
+        """Returns (status, ids, probs) with the full sorted candidate list (up to cap)."""
+        row = np.ascontiguousarray(row)
+        v = row.size
+        cap = v if cap is None else cap
+        ids = np.zeros(cap, dtype=np.int32)
+        probs = np.zeros(cap, dtype=np.float64)
+        n = np.zeros(1, dtype=np.uint64)
+        h = None if hist is None else np.ascontiguousarray(hist, dtype=np.int32)
+        st = self.lib.orc_candidates(_p(row), _dtype_of(row), v, _p(params), _p(h), 0 if h is None else h.size,
+                                     _p(mask), cap, _p(ids), _p(probs), _p(n))
+        k = int(min(int(n[0]), cap))
+        return int(st), ids[:k].copy(), probs[:k].copy(), int(n[0])
+
+    def sample(self, row: np.ndarray, params: np.ndarray, hist=None, mask=None, u: float = 0.5):
+        row = np.ascontiguousarray(row)
+        tok = np.zeros(1, dtype=np.int32)
+        h = None if hist is None else np.ascontiguousarray(hist, dtype=np.int32)
+        st = self.lib.orc_sample(_p(row), _dtype_of(row), row.size, _p(params), _p(h),
+                                 0 if h is None else h.size, _p(mask), float(u), _p(tok))
+        return int(st), int(tok[0])
+
+    def sample_batch(self, logits: np.ndarray, params: np.ndarray, masks=None, hist=None, hist_off=None,
+                     uniforms=None, step: int = 0, n_threads: int = 0, vocab: int | None = None):
+        logits = np.ascontiguousarray(logits)
+        n, stride = logits.shape
+        vocab = stride if vocab is None else vocab
+        tok = np.zeros(n, dtype=np.int32)
+        sts = np.zeros(n, dtype=np.int32)
+        self.lib.orc_sample_batch(_p(logits), _dtype_of(logits), n, stride, vocab, _p(params), _p(masks),
+                                  _p(hist), _p(hist_off), _p(uniforms), step, _p(tok), _p(sts), n_threads)
+        return tok, sts
+
+    def verify(self, target: np.ndarray, drafts: np.ndarray, params: np.ndarray, q=None, n_drafts=None,
+               masks=None, hist=None, hist_off=None, uniforms=None, step: int = 0, n_threads: int = 0,
+               vocab: int | None = None):
+        target = np.ascontiguousarray(target)
+        S, k = drafts.shape
+        stride = target.shape[-1]
+        vocab = stride if vocab is None else vocab
+        out = dict(accepted=np.zeros(S, np.int32), tokens=np.zeros((S, k + 1), np.int32),
+                   n_tokens=np.zeros(S, np.int32), first_reject=np.zeros(S, np.int32),
+                   uniforms_used=np.zeros(S, np.int32), status=np.zeros(S, np.int32))
+        self.lib.orc_verify(_p(target), _dtype_of(target), stride, vocab, _p(q), _p(drafts), _p(n_drafts), S, k,
+                            _p(params), _p(masks), _p(hist), _p(hist_off), _p(uniforms), step,
+                            _p(out["accepted"]), _p(out["tokens"]), _p(out["n_tokens"]),
+                            _p(out["first_reject"]), _p(out["uniforms_used"]), _p(out["status"]), n_threads)
+        return out
+
+
+_cache: dict[str, Oracle] = {}
+
+
+def port() -> Oracle:
+    if "port" not in _cache:
+        if not PORT_PATH.exists():
+            build()
+        _cache["port"] = Oracle(PORT_PATH)
+    return _cache["port"]
+
+
+def reference() -> Oracle | None:
+    """The engine's own sampler, or None when it was not built (reference sources absent)."""
+    if "ref" not in _cache:
+        if not REF_PATH.exists():
+            return None
+        _cache["ref"] = Oracle(REF_PATH)
+    return _cache["ref"]

@@ -1,0 +1,364 @@
+// smp_abi.cu - extern "C" boundary of the B200 logits-to-token path (include/sixi_smp.h).
+//
+// The entry points validate arguments, pick the launch plan for the handle's vocabulary and
+// enqueue the row-engine kernels on the caller's stream. They never synchronise, except
+// sixi_smp_sample_host, whose contract is the engine's host-side sample_token call shape.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "../../include/sixi_smp.h"
+#include "smp_device.cuh"
+#include "smp_kernels.cuh"
+
+using sixi_b200::LaunchPlan;
+using sixi_b200::RowArgs;
+using sixi_b200::VerifyRowResult;
+
+struct sixi_smp {
+    int32_t device;
+    uint32_t max_rows;
+    uint32_t vocab;
+    uint32_t mask_words;
+    LaunchPlan plan;
+    VerifyRowResult* ws;         // verifier per-row workspace [max_rows]
+    sixi_smp_params* d_default;  // default params (raw argmax entry)
+    // staging of sixi_smp_sample_host
+    void* d_logits;
+    size_t logits_cap;
+    sixi_smp_params* d_params;
+    uint32_t* d_mask;
+    int32_t* d_hist;
+    size_t hist_cap;
+    int64_t* d_hoff;
+    double* d_u;
+    int32_t* d_tok;
+    int32_t* d_status;
+    size_t rows_cap;
+};
+
+namespace {
+
+int32_t from_cuda(cudaError_t e) {
+    if (e == cudaSuccess) return SIXI_OK;
+    if (e == cudaErrorMemoryAllocation) return SIXI_OUT_OF_MEMORY_VRAM;
+    return SIXI_BACKEND_ERROR;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+bool rows_ok(const sixi_smp* h, const sixi_smp_rows* rows) {
+    if (rows == nullptr || (rows->n_rows > 0 && rows->data == nullptr)) return false;
+    if (rows->dtype != SIXI_SMP_F32 && rows->dtype != SIXI_SMP_BF16) return false;
+    if (rows->row_stride < h->vocab) return false;
+    return true;
+}
+
+RowArgs base_args(const sixi_smp* h, const sixi_smp_rows* rows) {
+    RowArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.data = rows->data;
+    a.row_stride = rows->row_stride;
+    a.dtype = rows->dtype;
+    a.vocab = h->vocab;
+    a.n_rows = rows->n_rows;
+    a.chunk = h->plan.chunk;
+    const size_t esz = rows->dtype == SIXI_SMP_BF16 ? 2 : 4;
+    a.use_tma = ((reinterpret_cast<uintptr_t>(rows->data) & 15u) == 0 &&
+                 (rows->row_stride * esz) % 16 == 0)
+                    ? 1u
+                    : 0u;
+    a.mask_words = h->mask_words;
+    return a;
+}
+
+template <typename T>
+cudaError_t grow(T** p, size_t* cap, size_t need) {
+    if (*cap >= need && *p != nullptr) return cudaSuccess;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), need * sizeof(T));
+    if (e == cudaSuccess) *cap = need;
+    return e;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t sixi_smp_create(int32_t device, uint32_t max_rows, uint32_t vocab, sixi_smp** out) {
+    if (out == nullptr) return SIXI_INVALID_ARGUMENT;
+    *out = nullptr;
+    LaunchPlan plan{};
+    if (vocab == 0 || !sixi_b200::plan_for_vocab(vocab, &plan)) return SIXI_INVALID_ARGUMENT;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return SIXI_INVALID_ARGUMENT;
+    DeviceGuard g(device);
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return SIXI_BACKEND_ERROR;
+    if (prop.major < 10) return SIXI_UNSUPPORTED_HARDWARE;
+    sixi_smp* h = new (std::nothrow) sixi_smp;
+    if (h == nullptr) return SIXI_OUT_OF_MEMORY_VRAM;
+    std::memset(h, 0, sizeof(*h));
+    h->device = device;
+    h->max_rows = max_rows;
+    h->vocab = vocab;
+    h->mask_words = (vocab + 31u) / 32u;
+    h->plan = plan;
+    cudaError_t e = cudaSuccess;
+    if (max_rows > 0) e = cudaMalloc(&h->ws, sizeof(VerifyRowResult) * max_rows);
+    if (e == cudaSuccess) e = cudaMalloc(&h->d_default, sizeof(sixi_smp_params));
+    if (e == cudaSuccess) {
+        sixi_smp_params p;
+        std::memset(&p, 0, sizeof(p));
+        p.top_k = 0;
+        p.top_p = 1.0f;
+        p.repetition_penalty = 1.0f;
+        e = cudaMemcpy(h->d_default, &p, sizeof(p), cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess) e = sixi_b200::prepare_kernels(device);
+    if (e != cudaSuccess) {
+        sixi_smp_destroy(h);
+        return from_cuda(e);
+    }
+    *out = h;
+    return SIXI_OK;
+}
+
+int32_t sixi_smp_destroy(sixi_smp* h) {
+    if (h == nullptr) return SIXI_OK;
+    DeviceGuard g(h->device);
+    cudaFree(h->ws);
+    cudaFree(h->d_default);
+    cudaFree(h->d_logits);
+    cudaFree(h->d_params);
+    cudaFree(h->d_mask);
+    cudaFree(h->d_hist);
+    cudaFree(h->d_hoff);
+    cudaFree(h->d_u);
+    cudaFree(h->d_tok);
+    cudaFree(h->d_status);
+    delete h;
+    return SIXI_OK;
+}
+
+uint32_t sixi_smp_vocab(const sixi_smp* h) { return h ? h->vocab : 0u; }
+uint32_t sixi_smp_mask_words(const sixi_smp* h) { return h ? h->mask_words : 0u; }
+
+const char* sixi_smp_status_string(int32_t status) {
+    switch (status) {
+        case SIXI_OK: return "Ok";
+        case SIXI_INVALID_ARGUMENT: return "InvalidArgument";
+        case SIXI_OUT_OF_BOUNDS: return "OutOfBounds";
+        case SIXI_OUT_OF_MEMORY_VRAM: return "OutOfMemoryVRAM";
+        case SIXI_NUMERIC_NAN_OR_INF: return "NumericNaNOrInf";
+        case SIXI_BACKEND_ERROR: return "BackendError";
+        case SIXI_UNSUPPORTED_HARDWARE: return "UnsupportedHardware";
+        default: return "Unknown";
+    }
+}
+
+double sixi_smp_philox_uniform(uint64_t seed, uint64_t counter, uint32_t slot) {
+    return sixi_b200::philox_uniform(seed, counter, slot);
+}
+
+int32_t sixi_smp_sample(sixi_smp* h, const sixi_smp_rows* rows, const sixi_smp_params* params,
+                        const uint32_t* mask_words, const int32_t* hist_tokens,
+                        const int64_t* hist_offsets, const double* uniforms, uint64_t step,
+                        int32_t* out_tokens, int32_t* out_status, void* stream) {
+    if (h == nullptr || !rows_ok(h, rows) || params == nullptr || out_tokens == nullptr ||
+        out_status == nullptr || (hist_tokens != nullptr && hist_offsets == nullptr))
+        return SIXI_INVALID_ARGUMENT;
+    if (rows->n_rows == 0) return SIXI_OK;
+    DeviceGuard g(h->device);
+    RowArgs a = base_args(h, rows);
+    a.params = params;
+    a.mask = mask_words;
+    a.hist = hist_tokens;
+    a.hist_off = hist_tokens ? hist_offsets : nullptr;
+    a.uniforms = uniforms;
+    a.step = step;
+    a.out_tok = out_tokens;
+    a.out_status = out_status;
+    return from_cuda(sixi_b200::launch_rows(sixi_b200::kModeSample, a, h->plan,
+                                            static_cast<cudaStream_t>(stream)));
+}
+
+int32_t sixi_smp_sample_host(sixi_smp* h, const void* host_logits, uint32_t dtype,
+                             uint32_t n_rows, uint64_t row_stride,
+                             const sixi_smp_params* host_params, const uint32_t* host_mask_words,
+                             const int32_t* host_hist_tokens, const int64_t* host_hist_offsets,
+                             const double* host_uniforms, uint64_t step, int32_t* host_out_tokens,
+                             int32_t* host_out_status, void* stream) {
+    if (h == nullptr || host_logits == nullptr || host_params == nullptr ||
+        host_out_tokens == nullptr || host_out_status == nullptr || row_stride < h->vocab ||
+        (dtype != SIXI_SMP_F32 && dtype != SIXI_SMP_BF16) ||
+        (host_hist_tokens != nullptr && host_hist_offsets == nullptr))
+        return SIXI_INVALID_ARGUMENT;
+    if (n_rows == 0) return SIXI_OK;
+    DeviceGuard g(h->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t esz = dtype == SIXI_SMP_BF16 ? 2 : 4;
+    const size_t lbytes = static_cast<size_t>(n_rows) * row_stride * esz;
+    size_t cap_bytes = h->logits_cap;
+    cudaError_t e = grow(reinterpret_cast<uint8_t**>(&h->d_logits), &cap_bytes, lbytes);
+    h->logits_cap = cap_bytes;
+    // params, tokens, status, uniforms, masks sized by n_rows (re-allocated when a call needs more)
+    if (e == cudaSuccess && (h->d_params == nullptr || h->rows_cap < n_rows)) {
+        cudaFree(h->d_params);
+        cudaFree(h->d_u);
+        cudaFree(h->d_tok);
+        cudaFree(h->d_status);
+        cudaFree(h->d_mask);
+        cudaFree(h->d_hoff);
+        h->d_params = nullptr;
+        h->d_u = nullptr;
+        h->d_tok = nullptr;
+        h->d_status = nullptr;
+        h->d_mask = nullptr;
+        h->d_hoff = nullptr;
+        e = cudaMalloc(&h->d_params, sizeof(sixi_smp_params) * n_rows);
+        if (e == cudaSuccess) e = cudaMalloc(&h->d_u, sizeof(double) * n_rows);
+        if (e == cudaSuccess) e = cudaMalloc(&h->d_tok, sizeof(int32_t) * n_rows);
+        if (e == cudaSuccess) e = cudaMalloc(&h->d_status, sizeof(int32_t) * n_rows);
+        if (e == cudaSuccess) e = cudaMalloc(&h->d_mask, sizeof(uint32_t) * h->mask_words * n_rows);
+        if (e == cudaSuccess) e = cudaMalloc(&h->d_hoff, sizeof(int64_t) * (n_rows + 1));
+        h->rows_cap = (e == cudaSuccess) ? n_rows : 0;
+    }
+    int64_t nh = 0;
+    if (host_hist_tokens != nullptr) nh = host_hist_offsets[n_rows];
+    if (e == cudaSuccess && nh > 0) e = grow(&h->d_hist, &h->hist_cap, static_cast<size_t>(nh));
+    if (e != cudaSuccess) return from_cuda(e);
+    e = cudaMemcpyAsync(h->d_logits, host_logits, lbytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(h->d_params, host_params, sizeof(sixi_smp_params) * n_rows, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && host_mask_words)
+        e = cudaMemcpyAsync(h->d_mask, host_mask_words, sizeof(uint32_t) * h->mask_words * n_rows,
+                            cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && nh > 0) {
+        e = cudaMemcpyAsync(h->d_hist, host_hist_tokens, sizeof(int32_t) * static_cast<size_t>(nh),
+                            cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(h->d_hoff, host_hist_offsets, sizeof(int64_t) * (n_rows + 1),
+                                cudaMemcpyHostToDevice, s);
+    }
+    if (e == cudaSuccess && host_uniforms)
+        e = cudaMemcpyAsync(h->d_u, host_uniforms, sizeof(double) * n_rows, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return from_cuda(e);
+    sixi_smp_rows rows{h->d_logits, dtype, n_rows, row_stride};
+    const int32_t st = sixi_smp_sample(h, &rows, h->d_params, host_mask_words ? h->d_mask : nullptr,
+                                       nh > 0 ? h->d_hist : nullptr, nh > 0 ? h->d_hoff : nullptr,
+                                       host_uniforms ? h->d_u : nullptr, step, h->d_tok, h->d_status,
+                                       stream);
+    if (st != SIXI_OK) return st;
+    e = cudaMemcpyAsync(host_out_tokens, h->d_tok, sizeof(int32_t) * n_rows, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(host_out_status, h->d_status, sizeof(int32_t) * n_rows, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return from_cuda(e);
+}
+
+int32_t sixi_smp_greedy_argmax(sixi_smp* h, const sixi_smp_rows* rows, const uint32_t* mask_words,
+                               int32_t* out_tokens, int32_t* out_status, void* stream) {
+    if (h == nullptr || !rows_ok(h, rows) || out_tokens == nullptr || out_status == nullptr)
+        return SIXI_INVALID_ARGUMENT;
+    if (rows->n_rows == 0) return SIXI_OK;
+    DeviceGuard g(h->device);
+    RowArgs a = base_args(h, rows);
+    a.params = h->d_default;
+    a.mask = mask_words;
+    a.out_tok = out_tokens;
+    a.out_status = out_status;
+    return from_cuda(sixi_b200::launch_rows(sixi_b200::kModeGreedy, a, h->plan,
+                                            static_cast<cudaStream_t>(stream)));
+}
+
+int32_t sixi_smp_candidates(sixi_smp* h, const sixi_smp_rows* rows, const sixi_smp_params* params,
+                            const uint32_t* mask_words, const int32_t* hist_tokens,
+                            const int64_t* hist_offsets, uint32_t max_out, int32_t* out_ids,
+                            double* out_probs, int32_t* out_count, int32_t* out_status,
+                            void* stream) {
+    if (h == nullptr || !rows_ok(h, rows) || params == nullptr || max_out == 0 || max_out > 256 ||
+        out_ids == nullptr || out_probs == nullptr || out_count == nullptr || out_status == nullptr ||
+        (hist_tokens != nullptr && hist_offsets == nullptr))
+        return SIXI_INVALID_ARGUMENT;
+    if (rows->n_rows == 0) return SIXI_OK;
+    DeviceGuard g(h->device);
+    RowArgs a = base_args(h, rows);
+    a.params = params;
+    a.mask = mask_words;
+    a.hist = hist_tokens;
+    a.hist_off = hist_tokens ? hist_offsets : nullptr;
+    a.max_out = max_out;
+    a.out_ids = out_ids;
+    a.out_probs = out_probs;
+    a.out_count = out_count;
+    a.out_status = out_status;
+    return from_cuda(sixi_b200::launch_rows(sixi_b200::kModeCandidates, a, h->plan,
+                                            static_cast<cudaStream_t>(stream)));
+}
+
+int32_t sixi_smp_verify(sixi_smp* h, const sixi_smp_rows* target, const float* draft_probs,
+                        const int32_t* drafts, const int32_t* n_drafts, uint32_t n_streams,
+                        uint32_t k, const sixi_smp_params* params, const uint32_t* mask_words,
+                        const int32_t* hist_tokens, const int64_t* hist_offsets,
+                        const double* uniforms, uint64_t step, int32_t* out_accepted,
+                        int32_t* out_tokens, int32_t* out_n_tokens, int32_t* out_first_reject,
+                        int32_t* out_uniforms_used, int32_t* out_status, void* stream) {
+    if (h == nullptr || !rows_ok(h, target) || params == nullptr || drafts == nullptr ||
+        out_accepted == nullptr || out_tokens == nullptr || out_n_tokens == nullptr ||
+        out_first_reject == nullptr || out_uniforms_used == nullptr || out_status == nullptr ||
+        (hist_tokens != nullptr && hist_offsets == nullptr) || k == 0)
+        return SIXI_INVALID_ARGUMENT;
+    if (static_cast<uint64_t>(n_streams) * (k + 1) != target->n_rows) return SIXI_INVALID_ARGUMENT;
+    if (target->n_rows > h->max_rows) return SIXI_INVALID_ARGUMENT;
+    if (n_streams == 0) return SIXI_OK;
+    if (draft_probs != nullptr && (reinterpret_cast<uintptr_t>(draft_probs) & 3u) != 0)
+        return SIXI_INVALID_ARGUMENT;
+    DeviceGuard g(h->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    RowArgs a = base_args(h, target);
+    a.params = params;
+    a.mask = mask_words;
+    a.hist = hist_tokens;
+    a.hist_off = hist_tokens ? hist_offsets : nullptr;
+    a.uniforms = uniforms;
+    a.step = step;
+    a.q = draft_probs;
+    a.drafts = drafts;
+    a.n_drafts = n_drafts;
+    a.k = k;
+    a.ws = h->ws;
+    cudaError_t e = sixi_b200::launch_rows(sixi_b200::kModeVerify, a, h->plan, s);
+    if (e == cudaSuccess)
+        e = sixi_b200::launch_verify_finalize(a, n_streams, out_accepted, out_tokens, out_n_tokens,
+                                              out_first_reject, out_uniforms_used, out_status, s);
+    return from_cuda(e);
+}
+
+int32_t sixi_smp_shard_candidates(sixi_smp*, const sixi_smp_rows*, uint32_t, uint32_t,
+                                  const sixi_smp_params*, const uint32_t*, const int32_t*,
+                                  const int64_t*, uint32_t, void*, void*, void*) {
+    return SIXI_UNSUPPORTED_HARDWARE;
+}
+
+int32_t sixi_smp_merge_shards(sixi_smp*, uint32_t, uint32_t, uint32_t, const void*, const void*,
+                              const sixi_smp_params*, const double*, uint64_t, int32_t*, int32_t*,
+                              void*) {
+    return SIXI_UNSUPPORTED_HARDWARE;
+}
+
+}  // extern "C"

@@ -1,0 +1,278 @@
+"""Python binding of libsixi_smp.so, the C ABI of the B200 logits-to-token path.
+
+The library is the product; this module only declares its entry points for ctypes and offers a
+thin convenience layer over torch CUDA tensors (torch supplies device memory and streams). There
+is no fallback: importing fails loudly when the library has not been built.
+
+Entry points mirror the engine's sampler/verifier interface (include/sixi_smp.h):
+  sample           DeterministicSampler::sample_token          src/core/core_execution.cpp:603-619
+  candidates       DeterministicSampler::compute_sampling_candidates  (:449-584)
+  greedy_argmax    DeterministicSampler::sample_greedy_argmax  (:394-407)
+  verify           SpeculativeDecoder::step verification       src/speculative/speculative.cpp:589-916
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+_PKG = Path(__file__).resolve().parent.parent
+LIB_PATH = Path(os.environ.get("SIXI_SMP_LIB", _PKG / "lib" / "libsixi_smp.so"))
+
+# status codes (ErrorCode values of the engine)
+OK = 0
+INVALID_ARGUMENT = 1
+OUT_OF_BOUNDS = 2
+OUT_OF_MEMORY_VRAM = 11
+NUMERIC_NAN_OR_INF = 16
+BACKEND_ERROR = 23
+UNSUPPORTED_HARDWARE = 24
+
+F32 = 0
+BF16 = 1
+STRICT_REPLAY = 0
+ADAPTIVE = 1
+ROW_MASKED = 1
+
+PARAMS_DTYPE = np.dtype(
+    [
+        ("temperature", "<f4"),
+        ("top_k", "<i4"),
+        ("top_p", "<f4"),
+        ("min_p", "<f4"),
+        ("repetition_penalty", "<f4"),
+        ("presence_penalty", "<f4"),
+        ("frequency_penalty", "<f4"),
+        ("mode", "<u4"),
+        ("flags", "<u4"),
+        ("reserved", "<u4"),
+        ("seed", "<u8"),
+        ("counter", "<u8"),
+    ],
+    align=True,
+)
+assert PARAMS_DTYPE.itemsize == 56
+
+
+class Rows(ctypes.Structure):
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("dtype", ctypes.c_uint32),
+        ("n_rows", ctypes.c_uint32),
+        ("row_stride", ctypes.c_uint64),
+    ]
+
+
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_U32 = ctypes.c_uint32
+_U64 = ctypes.c_uint64
+
+# name -> (restype, argtypes); every symbol declared in include/sixi_smp.h
+SIGNATURES = {
+    "sixi_smp_create": (_I32, [_I32, _U32, _U32, ctypes.POINTER(_P)]),
+    "sixi_smp_destroy": (_I32, [_P]),
+    "sixi_smp_vocab": (_U32, [_P]),
+    "sixi_smp_mask_words": (_U32, [_P]),
+    "sixi_smp_status_string": (ctypes.c_char_p, [_I32]),
+    "sixi_smp_sample": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _P, _P, _U64, _P, _P, _P]),
+    "sixi_smp_sample_host": (_I32, [_P, _P, _U32, _U32, _U64, _P, _P, _P, _P, _P, _U64, _P, _P, _P]),
+    "sixi_smp_greedy_argmax": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _P]),
+    "sixi_smp_candidates": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _P, _U32, _P, _P, _P, _P, _P]),
+    "sixi_smp_verify": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32, _P, _P, _P, _P, _P,
+                               _U64, _P, _P, _P, _P, _P, _P, _P]),
+    "sixi_smp_shard_candidates": (_I32, [_P, ctypes.POINTER(Rows), _U32, _U32, _P, _P, _P, _P, _U32,
+                                         _P, _P, _P]),
+    "sixi_smp_merge_shards": (_I32, [_P, _U32, _U32, _U32, _P, _P, _P, _P, _U64, _P, _P, _P]),
+    "sixi_smp_philox_uniform": (ctypes.c_double, [_U64, _U64, _U32]),
+}
+
+
+def load(path: Path | str = LIB_PATH) -> ctypes.CDLL:
+    path = Path(path)
+    if not path.exists():
+        raise ImportError(
+            f"{path} is missing: build it with `python sixi-asi_b200/build_lib.py` "
+            "(there is no CPU fallback)")
+    lib = ctypes.CDLL(str(path))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+_LIB = None
+
+
+def _lib() -> ctypes.CDLL:
+    """The loaded library (loaded on first use; raises ImportError when it is not built)."""
+    global _LIB
+    if _LIB is None:
+        _LIB = load()
+    return _LIB
+
+
+def status_string(st: int) -> str:
+    return _lib().sixi_smp_status_string(int(st)).decode()
+
+
+def philox_uniform(seed: int, counter: int, slot: int) -> float:
+    return float(_lib().sixi_smp_philox_uniform(seed, counter, slot))
+
+
+class SixiError(RuntimeError):
+    def __init__(self, where: str, status: int):
+        super().__init__(f"{where}: {status_string(status)} ({status})")
+        self.status = status
+
+
+def _check(where: str, st: int) -> None:
+    if st != OK:
+        raise SixiError(where, st)
+
+
+def make_params(n: int, **fields) -> np.ndarray:
+    """Array of n parameter records; scalars or per-row arrays for any field."""
+    p = np.zeros(n, dtype=PARAMS_DTYPE)
+    p["top_p"] = 1.0
+    p["repetition_penalty"] = 1.0
+    p["mode"] = ADAPTIVE
+    for k, v in fields.items():
+        p[k] = v
+    return p
+
+
+def _ptr(t) -> int:
+    """Device pointer of a torch tensor, or 0 for None."""
+    return 0 if t is None else int(t.data_ptr())
+
+
+class Sampler:
+    """A handle bound to one device and vocabulary (sixi_smp_create)."""
+
+    def __init__(self, device: int, max_rows: int, vocab: int):
+        h = _P()
+        _check("sixi_smp_create", _lib().sixi_smp_create(device, max_rows, vocab, ctypes.byref(h)))
+        self.h = h
+        self.device = device
+        self.vocab = vocab
+        self.max_rows = max_rows
+        self.mask_words = int(_lib().sixi_smp_mask_words(h))
+
+    def close(self) -> None:
+        if self.h:
+            _lib().sixi_smp_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- device-pointer entry points (torch tensors on this device) ---------------------------
+    @staticmethod
+    def _rows(logits) -> Rows:
+        import torch
+
+        dt = {torch.float32: F32, torch.bfloat16: BF16}[logits.dtype]
+        assert logits.dim() == 2 and logits.stride(1) == 1
+        return Rows(logits.data_ptr(), dt, logits.shape[0], logits.stride(0))
+
+    @staticmethod
+    def _stream(stream) -> int:
+        import torch
+
+        s = stream if stream is not None else torch.cuda.current_stream()
+        return int(s.cuda_stream)
+
+    def sample(self, logits, params, masks=None, hist=None, hist_off=None, uniforms=None, step=0,
+               out_tokens=None, out_status=None, stream=None):
+        import torch
+
+        n = logits.shape[0]
+        dev = logits.device
+        if out_tokens is None:
+            out_tokens = torch.empty(n, dtype=torch.int32, device=dev)
+        if out_status is None:
+            out_status = torch.empty(n, dtype=torch.int32, device=dev)
+        rows = self._rows(logits)
+        st = _lib().sixi_smp_sample(self.h, ctypes.byref(rows), _ptr(params), _ptr(masks), _ptr(hist),
+                                 _ptr(hist_off), _ptr(uniforms), step, _ptr(out_tokens),
+                                 _ptr(out_status), self._stream(stream))
+        _check("sixi_smp_sample", st)
+        return out_tokens, out_status
+
+    def greedy_argmax(self, logits, masks=None, stream=None):
+        import torch
+
+        n = logits.shape[0]
+        tok = torch.empty(n, dtype=torch.int32, device=logits.device)
+        sts = torch.empty(n, dtype=torch.int32, device=logits.device)
+        rows = self._rows(logits)
+        st = _lib().sixi_smp_greedy_argmax(self.h, ctypes.byref(rows), _ptr(masks), _ptr(tok), _ptr(sts),
+                                        self._stream(stream))
+        _check("sixi_smp_greedy_argmax", st)
+        return tok, sts
+
+    def candidates(self, logits, params, max_out=256, masks=None, hist=None, hist_off=None,
+                   stream=None):
+        import torch
+
+        n = logits.shape[0]
+        dev = logits.device
+        ids = torch.full((n, max_out), -1, dtype=torch.int32, device=dev)
+        probs = torch.zeros((n, max_out), dtype=torch.float64, device=dev)
+        cnt = torch.zeros(n, dtype=torch.int32, device=dev)
+        sts = torch.empty(n, dtype=torch.int32, device=dev)
+        rows = self._rows(logits)
+        st = _lib().sixi_smp_candidates(self.h, ctypes.byref(rows), _ptr(params), _ptr(masks), _ptr(hist),
+                                     _ptr(hist_off), max_out, _ptr(ids), _ptr(probs), _ptr(cnt),
+                                     _ptr(sts), self._stream(stream))
+        _check("sixi_smp_candidates", st)
+        return ids, probs, cnt, sts
+
+    def verify(self, target, drafts, params, draft_probs=None, n_drafts=None, masks=None, hist=None,
+               hist_off=None, uniforms=None, step=0, stream=None):
+        import torch
+
+        S, k = drafts.shape
+        dev = target.device
+        acc = torch.empty(S, dtype=torch.int32, device=dev)
+        toks = torch.empty((S, k + 1), dtype=torch.int32, device=dev)
+        ntok = torch.empty(S, dtype=torch.int32, device=dev)
+        frej = torch.empty(S, dtype=torch.int32, device=dev)
+        used = torch.empty(S, dtype=torch.int32, device=dev)
+        sts = torch.empty(S, dtype=torch.int32, device=dev)
+        rows = self._rows(target)
+        st = _lib().sixi_smp_verify(self.h, ctypes.byref(rows), _ptr(draft_probs), _ptr(drafts),
+                                 _ptr(n_drafts), S, k, _ptr(params), _ptr(masks), _ptr(hist),
+                                 _ptr(hist_off), _ptr(uniforms), step, _ptr(acc), _ptr(toks), _ptr(ntok),
+                                 _ptr(frej), _ptr(used), _ptr(sts), self._stream(stream))
+        _check("sixi_smp_verify", st)
+        return dict(accepted=acc, tokens=toks, n_tokens=ntok, first_reject=frej, uniforms_used=used,
+                    status=sts)
+
+    # -- host-buffer entry point ---------------------------------------------------------------
+    def sample_host(self, logits: np.ndarray, params: np.ndarray, masks=None, hist=None, hist_off=None,
+                    uniforms=None, step=0, out_tokens=None, out_status=None, stream=None):
+        """logits: host array [n, stride] (float32, or uint16 holding bf16)."""
+        n = logits.shape[0]
+        dt = BF16 if logits.dtype == np.uint16 else F32
+        if out_tokens is None:
+            out_tokens = np.empty(n, dtype=np.int32)
+        if out_status is None:
+            out_status = np.empty(n, dtype=np.int32)
+
+        def hp(a):
+            return 0 if a is None else a.ctypes.data
+
+        st = _lib().sixi_smp_sample_host(self.h, hp(logits), dt, n, logits.shape[1], hp(params), hp(masks),
+                                      hp(hist), hp(hist_off), hp(uniforms), step, hp(out_tokens),
+                                      hp(out_status), self._stream(stream) if stream is not None else 0)
+        _check("sixi_smp_sample_host", st)
+        return out_tokens, out_status

@@ -1,0 +1,230 @@
+"""GPU parity of the fused sampler kernels against the CPU oracle (calls through the C ABI).
+
+Bars: greedy tokens, candidate id sets/order, masked sets and statuses bit-exact; sampled ids
+exact except where the uniform is within 1e-6 of a reference CDF boundary; probabilities within
+1e-5 relative (conftest.BOUNDARY_EPS / PROB_RTOL).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import PROB_RTOL, has_gpu, near_boundary
+
+pytestmark = pytest.mark.gpu
+
+if not has_gpu():  # collected on CPU boxes, skipped there
+    pytest.skip("no CUDA device", allow_module_level=True)
+
+import torch  # noqa: E402
+
+import sixi_smp as S  # noqa: E402
+from sixi_smp import workloads as W  # noqa: E402
+
+DEV = torch.device("cuda:0")
+
+
+def dev(a: np.ndarray | None):
+    if a is None:
+        return None
+    if a.dtype.names is not None:  # params records
+        return torch.from_numpy(np.ascontiguousarray(a).view(np.uint8)).to(DEV)
+    if a.dtype == np.uint32:
+        return torch.from_numpy(a.view(np.int32)).to(DEV)
+    if a.dtype == np.uint16:
+        return torch.from_numpy(a.view(np.int16)).to(DEV).view(torch.bfloat16)
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+_samplers: dict[int, S.Sampler] = {}
+
+
+def sampler(vocab: int) -> S.Sampler:
+    if vocab not in _samplers:
+        _samplers[vocab] = S.Sampler(0, 1024, vocab)
+    return _samplers[vocab]
+
+
+def run_sample(d: dict, uniforms: np.ndarray | None, step: int = 0):
+    logits = d["logits"]
+    vocab = d.get("vocab", logits.shape[1])
+    smp = sampler(vocab)
+    tok, st = smp.sample(dev(logits), dev(d["params"]), masks=dev(d.get("masks")), hist=dev(d.get("hist")),
+                         hist_off=dev(d.get("hist_off")) if d.get("hist") is not None else None,
+                         uniforms=dev(uniforms), step=step)
+    torch.cuda.synchronize()
+    return tok.cpu().numpy(), st.cpu().numpy()
+
+
+def check_against_oracle(port, d: dict, uniforms: np.ndarray, tok, st, step: int = 0):
+    logits = d["logits"]
+    vocab = d.get("vocab", logits.shape[1])
+    if uniforms is None:
+        uniforms = np.array([port.philox_uniform(int(p["seed"]), int(p["counter"]) + step, 0) for p in d["params"]])
+    otok, ost = port.sample_batch(logits, d["params"], d.get("masks"), d.get("hist"), d.get("hist_off"),
+                                  uniforms, step=step, vocab=vocab)
+    assert np.array_equal(st, ost), f"status mismatch gpu={st} oracle={ost}"
+    bad = np.nonzero(tok != otok)[0]
+    excused = 0
+    for r in bad:
+        h = None
+        if d.get("hist") is not None:
+            h = d["hist"][d["hist_off"][r]:d["hist_off"][r + 1]]
+        m = None
+        if d.get("masks") is not None and (d["params"]["flags"][r] & S.ROW_MASKED):
+            m = d["masks"][r]
+        row = logits[r, :vocab]
+        if near_boundary(port, row, d["params"][r:r + 1], h, m, uniforms[r]):
+            excused += 1
+            continue
+        raise AssertionError(f"row {r}: gpu token {tok[r]} oracle {otok[r]} params {d['params'][r]}")
+    return excused
+
+
+@pytest.mark.parametrize("seed", [11, 12, 13])
+def test_config2_batched_sampler(port, seed):
+    d = W.config2(rows=32, seed=seed)
+    u = np.random.default_rng(seed).random(32)
+    tok, st = run_sample(d, u)
+    check_against_oracle(port, d, u, tok, st)
+
+
+@pytest.mark.parametrize("seed", [21, 22])
+def test_config3_grammar_masked(port, seed):
+    d = W.config3(rows=32, seed=seed)
+    u = np.random.default_rng(seed).random(32)
+    tok, st = run_sample(d, u)
+    check_against_oracle(port, d, u, tok, st)
+    # every sampled token is allowed by its row's mask
+    allowed = W.unpack_mask(d["masks"], d["logits"].shape[1])
+    for r in range(32):
+        assert st[r] == 0 and allowed[r, tok[r]]
+
+
+def test_config1_single_row_philox(port):
+    for greedy in (False, True):
+        d = W.config1(greedy=greedy)
+        for step in range(4):
+            tok, st = run_sample(d, None, step=step)
+            check_against_oracle(port, d, None, tok, st, step=step)
+
+
+def rand_small_case(rng: np.random.Generator, vocab: int, rows: int, dtype: str):
+    kind = rng.integers(0, 3)
+    if kind == 0:
+        logits = rng.normal(0.0, 2.5, size=(rows, vocab)).astype(np.float32)
+    elif kind == 1:  # heavy ties
+        logits = rng.integers(-3, 4, size=(rows, vocab)).astype(np.float32)
+    else:
+        logits = (rng.standard_cauchy(size=(rows, vocab)) * 0.5).astype(np.float32)
+    if dtype == "bf16":
+        bits = W.f32_to_bf16_bits(logits)
+        logits_in = bits
+    else:
+        logits_in = logits
+    t = rng.choice(np.array([0.0, 0.3, 0.7, 1.0, 1.5, 4.0], np.float32), size=rows)
+    topk = rng.choice(np.array([0, 1, 2, 5, 20, 100, 256, 257, 300, 1000, vocab], np.int64), size=rows)
+    topp = rng.choice(np.array([1.0, 0.95, 0.8, 0.5, 0.1], np.float32), size=rows)
+    minp = np.where(rng.random(rows) < 0.2, rng.choice(np.array([0.01, 0.1, 0.5], np.float32), size=rows), 0.0)
+    rep = rng.choice(np.array([1.0, 1.1, 1.3, 0.8], np.float32), size=rows)
+    pres = np.where(rng.random(rows) < 0.3, 0.5, 0.0).astype(np.float32)
+    freq = np.where(rng.random(rows) < 0.2, 0.25, 0.0).astype(np.float32)
+    mode = np.where(rng.random(rows) < 0.8, S.ADAPTIVE, S.STRICT_REPLAY)
+    params = S.make_params(rows, temperature=t, top_k=topk.astype(np.int32), top_p=topp, min_p=minp,
+                           repetition_penalty=rep, presence_penalty=pres, frequency_penalty=freq, mode=mode)
+    masks = None
+    if rng.random() < 0.5:
+        allowed = np.stack([W.run_mask(rng, vocab, float(rng.choice([0.05, 0.3, 0.9])), mean_run=4.0)
+                            for _ in range(rows)])
+        masks = W.pack_mask(allowed)
+        params["flags"] = np.where(rng.random(rows) < 0.7, S.ROW_MASKED, 0)
+    lens = rng.integers(0, 3 * vocab + 2, size=rows)
+    off = np.zeros(rows + 1, dtype=np.int64)
+    off[1:] = np.cumsum(lens)
+    hist = rng.integers(-2, vocab + 2, size=int(off[-1]), dtype=np.int32)  # includes out-of-range ids
+    return dict(logits=logits_in, params=params, masks=masks, hist=hist if off[-1] > 0 else None,
+                hist_off=off if off[-1] > 0 else None, vocab=vocab)
+
+
+@pytest.mark.parametrize("vocab", [1, 7, 31, 32, 33, 100, 513, 4097, 5000, 40000])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_small_vocab_random_params(port, vocab, dtype):
+    rng = np.random.default_rng(vocab * 7 + (dtype == "bf16"))
+    for it in range(3):
+        d = rand_small_case(rng, vocab, 24, dtype)
+        u = rng.random(24)
+        tok, st = run_sample(d, u)
+        check_against_oracle(port, d, u, tok, st)
+
+
+def test_statuses_nan_inf_all_masked(port):
+    vocab = 5000
+    rng = np.random.default_rng(5)
+    logits = rng.normal(0, 1, size=(6, vocab)).astype(np.float32)
+    logits[0, 17] = np.nan
+    logits[1, 4999] = np.inf
+    logits[2, 0] = -np.inf
+    allowed = np.ones((6, vocab), dtype=bool)
+    allowed[3] = False                      # all masked
+    allowed[4] = False
+    allowed[4, 17] = True                   # single allowed token
+    logits[5, 10] = np.nan
+    allowed[5, 10] = False                  # NaN only on a masked token: fine
+    params = S.make_params(6, temperature=0.8, top_k=0, top_p=0.9, flags=S.ROW_MASKED)
+    d = dict(logits=logits, params=params, masks=W.pack_mask(allowed))
+    u = rng.random(6)
+    tok, st = run_sample(d, u)
+    assert list(st) == [16, 16, 16, 1, 0, 0]
+    assert tok[3] == -1 and tok[4] == 17
+    check_against_oracle(port, d, u, tok, st)
+
+
+def test_greedy_argmax_raw(port):
+    vocab = 151_936
+    rng = np.random.default_rng(3)
+    x = rng.normal(0, 2.5, size=(8, vocab)).astype(np.float32)
+    x[1, :] = 0.0                            # all tied -> 0
+    x[2, 5] = x[2, 77] = x[2, 151_000] = 50.0  # tie -> 5
+    x[3, 0] = np.nan                         # engine quirk: NaN at index 0 -> 0
+    x[4, 100] = np.nan                       # other NaNs never win
+    x[5, 151_935] = 1e30
+    x[6, 3] = -0.0
+    x[6, :] = np.minimum(x[6, :], -1.0)
+    x[6, 3] = 0.0
+    x[6, 2] = -0.0                           # -0 and +0 tie -> lower id
+    smp = sampler(vocab)
+    tok, st = smp.greedy_argmax(dev(x))
+    tok = tok.cpu().numpy()
+    st = st.cpu().numpy()
+    for r in range(8):
+        ost, otok = port.greedy_row(x[r])
+        assert tok[r] == otok, (r, tok[r], otok)
+        assert st[r] == ost
+    assert tok[1] == 0 and tok[2] == 5 and tok[3] == 0 and tok[6] == 2
+
+
+@pytest.mark.parametrize("seed", [31, 32])
+def test_candidates_full_vocab(port, seed):
+    d = W.config2(rows=16, seed=seed)
+    d["params"]["temperature"] = np.where(d["params"]["temperature"] <= 0, 0.9, d["params"]["temperature"])
+    smp = sampler(d["logits"].shape[1])
+    ids, probs, cnt, st = smp.candidates(dev(d["logits"]), dev(d["params"]), max_out=256, hist=dev(d["hist"]),
+                                         hist_off=dev(d["hist_off"]))
+    ids, probs, cnt, st = (t.cpu().numpy() for t in (ids, probs, cnt, st))
+    for r in range(16):
+        h = d["hist"][d["hist_off"][r]:d["hist_off"][r + 1]]
+        ost, oids, oprobs, on = port.candidates(d["logits"][r], d["params"][r:r + 1], h)
+        assert st[r] == ost == 0
+        assert cnt[r] == on, (r, cnt[r], on, d["params"][r])
+        m = min(on, 256)
+        assert np.array_equal(ids[r, :m], oids[:m]), r
+        np.testing.assert_allclose(probs[r, :m], oprobs[:m], rtol=PROB_RTOL, atol=1e-300)
+
+
+def test_philox_matches_host():
+    vals = [S.philox_uniform(123, 7, s) for s in range(4)]
+    from oracle import binding
+
+    p = binding.port()
+    assert vals == [p.philox_uniform(123, 7, s) for s in range(4)]

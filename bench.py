@@ -241,7 +241,9 @@ def main() -> int:
     with torch.cuda.graph(graph, stream=stream):
         for i in range(args.steps):
             step(i, torch.cuda.current_stream())
-    graph.replay()
+    # CUDAGraph.replay() launches on the current stream: replay and time inside `stream`
+    with torch.cuda.stream(stream):
+        graph.replay()
     stream.synchronize()
 
     clocks = ClockSampler(local)
@@ -252,9 +254,10 @@ def main() -> int:
     time.sleep(0.05)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    graph.replay()
-    e1.record(stream)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
     e1.synchronize()
     torch.cuda.synchronize()
     if world > 1:

@@ -22,7 +22,6 @@ struct sixi_smp {
     uint32_t max_rows;
     uint32_t vocab;
     uint32_t mask_words;
-    LaunchPlan plan;
     VerifyRowResult* ws;         // verifier per-row workspace [max_rows]
     sixi_smp_params* d_default;  // default params (raw argmax entry)
     // staging of sixi_smp_sample_host
@@ -66,15 +65,16 @@ bool rows_ok(const sixi_smp* h, const sixi_smp_rows* rows) {
     return true;
 }
 
-RowArgs base_args(const sixi_smp* h, const sixi_smp_rows* rows) {
+RowArgs base_args(const sixi_smp* h, const sixi_smp_rows* rows, LaunchPlan* plan) {
     RowArgs a;
     std::memset(&a, 0, sizeof(a));
+    sixi_b200::plan_rows(h->vocab, rows->n_rows, plan);
     a.data = rows->data;
     a.row_stride = rows->row_stride;
     a.dtype = rows->dtype;
     a.vocab = h->vocab;
     a.n_rows = rows->n_rows;
-    a.chunk = h->plan.chunk;
+    a.chunk = plan->chunk;
     const size_t esz = rows->dtype == SIXI_SMP_BF16 ? 2 : 4;
     a.use_tma = ((reinterpret_cast<uintptr_t>(rows->data) & 15u) == 0 &&
                  (rows->row_stride * esz) % 16 == 0)
@@ -103,7 +103,7 @@ int32_t sixi_smp_create(int32_t device, uint32_t max_rows, uint32_t vocab, sixi_
     if (out == nullptr) return SIXI_INVALID_ARGUMENT;
     *out = nullptr;
     LaunchPlan plan{};
-    if (vocab == 0 || !sixi_b200::plan_for_vocab(vocab, &plan)) return SIXI_INVALID_ARGUMENT;
+    if (vocab == 0 || !sixi_b200::plan_rows(vocab, 1, &plan)) return SIXI_INVALID_ARGUMENT;
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return SIXI_INVALID_ARGUMENT;
     DeviceGuard g(device);
@@ -117,7 +117,6 @@ int32_t sixi_smp_create(int32_t device, uint32_t max_rows, uint32_t vocab, sixi_
     h->max_rows = max_rows;
     h->vocab = vocab;
     h->mask_words = (vocab + 31u) / 32u;
-    h->plan = plan;
     cudaError_t e = cudaSuccess;
     if (max_rows > 0) e = cudaMalloc(&h->ws, sizeof(VerifyRowResult) * max_rows);
     if (e == cudaSuccess) e = cudaMalloc(&h->d_default, sizeof(sixi_smp_params));
@@ -184,7 +183,8 @@ int32_t sixi_smp_sample(sixi_smp* h, const sixi_smp_rows* rows, const sixi_smp_p
         return SIXI_INVALID_ARGUMENT;
     if (rows->n_rows == 0) return SIXI_OK;
     DeviceGuard g(h->device);
-    RowArgs a = base_args(h, rows);
+    LaunchPlan plan{};
+    RowArgs a = base_args(h, rows, &plan);
     a.params = params;
     a.mask = mask_words;
     a.hist = hist_tokens;
@@ -193,7 +193,7 @@ int32_t sixi_smp_sample(sixi_smp* h, const sixi_smp_rows* rows, const sixi_smp_p
     a.step = step;
     a.out_tok = out_tokens;
     a.out_status = out_status;
-    return from_cuda(sixi_b200::launch_rows(sixi_b200::kModeSample, a, h->plan,
+    return from_cuda(sixi_b200::launch_rows(sixi_b200::kModeSample, a, plan,
                                             static_cast<cudaStream_t>(stream)));
 }
 
@@ -277,12 +277,13 @@ int32_t sixi_smp_greedy_argmax(sixi_smp* h, const sixi_smp_rows* rows, const uin
         return SIXI_INVALID_ARGUMENT;
     if (rows->n_rows == 0) return SIXI_OK;
     DeviceGuard g(h->device);
-    RowArgs a = base_args(h, rows);
+    LaunchPlan plan{};
+    RowArgs a = base_args(h, rows, &plan);
     a.params = h->d_default;
     a.mask = mask_words;
     a.out_tok = out_tokens;
     a.out_status = out_status;
-    return from_cuda(sixi_b200::launch_rows(sixi_b200::kModeGreedy, a, h->plan,
+    return from_cuda(sixi_b200::launch_rows(sixi_b200::kModeGreedy, a, plan,
                                             static_cast<cudaStream_t>(stream)));
 }
 
@@ -297,7 +298,8 @@ int32_t sixi_smp_candidates(sixi_smp* h, const sixi_smp_rows* rows, const sixi_s
         return SIXI_INVALID_ARGUMENT;
     if (rows->n_rows == 0) return SIXI_OK;
     DeviceGuard g(h->device);
-    RowArgs a = base_args(h, rows);
+    LaunchPlan plan{};
+    RowArgs a = base_args(h, rows, &plan);
     a.params = params;
     a.mask = mask_words;
     a.hist = hist_tokens;
@@ -307,7 +309,7 @@ int32_t sixi_smp_candidates(sixi_smp* h, const sixi_smp_rows* rows, const sixi_s
     a.out_probs = out_probs;
     a.out_count = out_count;
     a.out_status = out_status;
-    return from_cuda(sixi_b200::launch_rows(sixi_b200::kModeCandidates, a, h->plan,
+    return from_cuda(sixi_b200::launch_rows(sixi_b200::kModeCandidates, a, plan,
                                             static_cast<cudaStream_t>(stream)));
 }
 
@@ -330,7 +332,8 @@ int32_t sixi_smp_verify(sixi_smp* h, const sixi_smp_rows* target, const float* d
         return SIXI_INVALID_ARGUMENT;
     DeviceGuard g(h->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    RowArgs a = base_args(h, target);
+    LaunchPlan plan{};
+    RowArgs a = base_args(h, target, &plan);
     a.params = params;
     a.mask = mask_words;
     a.hist = hist_tokens;
@@ -342,7 +345,7 @@ int32_t sixi_smp_verify(sixi_smp* h, const sixi_smp_rows* target, const float* d
     a.n_drafts = n_drafts;
     a.k = k;
     a.ws = h->ws;
-    cudaError_t e = sixi_b200::launch_rows(sixi_b200::kModeVerify, a, h->plan, s);
+    cudaError_t e = sixi_b200::launch_rows(sixi_b200::kModeVerify, a, plan, s);
     if (e == cudaSuccess)
         e = sixi_b200::launch_verify_finalize(a, n_streams, out_accepted, out_tokens, out_n_tokens,
                                               out_first_reject, out_uniforms_used, out_status, s);

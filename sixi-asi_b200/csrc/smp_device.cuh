@@ -7,7 +7,8 @@
 //     composite (key << 32) | (0xFFFFFFFF - id), larger = better, unique per row.
 //   * The probability mass of a candidate, for the selections that run over the whole vocabulary
 //     (top_k = 0 or large k), is an unsigned 64-bit fixed-point weight
-//     w = round(exp((x - max) / T) * 2^43). Integer sums are exact and order-independent, so
+//     w ~ round(exp((x - max) / T) * 2^43) (see weight_of). Integer sums are exact and
+//     order-independent, so
 //     every CTA of a cluster derives identical cumulative masses and the selection is
 //     deterministic. The exponent is computed with hi/lo-split constants so that the only
 //     rounding is one fp32 rounding of the exponent and the ex2 approximation (relative error
@@ -110,11 +111,22 @@ __device__ __forceinline__ float fast_ex2(float x) {
     return y;
 }
 
+// Fixed-point weight round(2^t * 2^43) of t = neg_log2w(x) <= 0, built from the exponent and
+// mantissa of the fp32 power with integer operations (round half up on the dropped bits).
 __device__ __forceinline__ uint64_t weight_of(float x, const WeightCtx& w) {
     float t = neg_log2w(x, w);
     t = fminf(t, 0.0f);
-    const float e = fast_ex2(t);
-    return __float2ull_rn(e * 8796093022208.0f);
+    const float e = fast_ex2(t);  // in [0, 1]; flushed to 0 below the normal range
+    const uint32_t b = __float_as_uint(e);
+    const int ex = static_cast<int>(b >> 23);
+    const uint32_t m = (b & 0x7FFFFFu) | 0x800000u;
+    const int sh = ex - 107;  // value = m * 2^(ex - 127 - 23) * 2^43
+    const uint32_t r = static_cast<uint32_t>(sh < 0 ? -sh : 0);
+    const uint32_t l = static_cast<uint32_t>(sh > 0 ? sh : 0);
+    const uint32_t rr = r < 31u ? r : 31u;
+    const uint32_t mr = (m + ((1u << rr) >> 1)) >> rr;
+    const uint64_t v = static_cast<uint64_t>(mr) << l;
+    return (ex == 0 || r >= 25u) ? 0ull : v;
 }
 
 // histogram bin of a candidate (0 = most likely); monotone non-increasing in x

@@ -13,12 +13,11 @@
 
 namespace sixi_b200 {
 
-template <int EPT, int DT, int MODE>
+template <int DT, int MODE>
 static cudaError_t launch_one(const RowArgs& a, const LaunchPlan& plan, cudaStream_t stream) {
-    auto kfn = row_kernel<EPT, DT, MODE>;
-    // The dynamic shared-memory opt-in is set once per device (never inside a stream capture
-    // after the first launch on that device). Every plan of this instance needs at most
-    // max_smem bytes, so the attribute is raised to that bound.
+    auto kfn = row_kernel<DT, MODE>;
+    // The shared-memory opt-in (and non-portable cluster sizes) are set once per device, so later
+    // launches issue no attribute call (they may be inside a stream capture).
     static std::atomic<uint64_t> ready{0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -26,18 +25,19 @@ static cudaError_t launch_one(const RowArgs& a, const LaunchPlan& plan, cudaStre
     const uint64_t bit = 1ull << (dev & 63);
     if (!(ready.load(std::memory_order_acquire) & bit)) {
         e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
         ready.fetch_or(bit, std::memory_order_acq_rel);
     }
     if (plan.smem > static_cast<size_t>(kMaxSmem)) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.n_rows * kC, 1, 1);
+    cfg.gridDim = dim3(a.n_rows * plan.cluster, 1, 1);
     cfg.blockDim = dim3(kNT, 1, 1);
     cfg.dynamicSmemBytes = plan.smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kC;
+    attr[0].val.clusterDim.x = plan.cluster;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
@@ -48,13 +48,7 @@ static cudaError_t launch_one(const RowArgs& a, const LaunchPlan& plan, cudaStre
 template <>
 cudaError_t launch_mode_dt<SIXI_INST_MODE, SIXI_INST_DT>(const RowArgs& a, const LaunchPlan& plan,
                                                          cudaStream_t stream) {
-    switch (plan.ept) {
-        case 8: return launch_one<8, SIXI_INST_DT, SIXI_INST_MODE>(a, plan, stream);
-        case 16: return launch_one<16, SIXI_INST_DT, SIXI_INST_MODE>(a, plan, stream);
-        case 80: return launch_one<80, SIXI_INST_DT, SIXI_INST_MODE>(a, plan, stream);
-        case 128: return launch_one<128, SIXI_INST_DT, SIXI_INST_MODE>(a, plan, stream);
-        default: return cudaErrorInvalidValue;
-    }
+    return launch_one<SIXI_INST_DT, SIXI_INST_MODE>(a, plan, stream);
 }
 
 }  // namespace sixi_b200

@@ -56,12 +56,14 @@ struct RowArgs {
 
 // Launch configuration chosen by the host for a vocabulary size.
 struct LaunchPlan {
-    int ept;        // elements per thread (template instance)
-    uint32_t chunk;  // elements per CTA
-    size_t smem;    // dynamic shared memory bytes
+    uint32_t cluster;  // CTAs per row
+    uint32_t chunk;    // elements per CTA (multiple of 8)
+    size_t smem;       // dynamic shared memory bytes
 };
 
-bool plan_for_vocab(uint32_t vocab, LaunchPlan* plan);
+// Launch plan for a vocabulary and batch: the smallest cluster whose chunk fits shared memory,
+// widened (up to 8 CTAs) while the batch leaves SMs idle.
+bool plan_rows(uint32_t vocab, uint32_t n_rows, LaunchPlan* plan);
 cudaError_t launch_rows(int mode, const RowArgs& a, const LaunchPlan& plan, cudaStream_t stream);
 cudaError_t launch_verify_finalize(const RowArgs& a, uint32_t n_streams, int32_t* out_accepted,
                                    int32_t* out_tokens, int32_t* out_n_tokens,

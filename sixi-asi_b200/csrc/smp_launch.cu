@@ -3,24 +3,22 @@
 
 namespace sixi_b200 {
 
-int pick_ept(uint32_t chunk) {
-    const uint32_t per = (chunk + kNT - 1) / kNT;
-    if (per <= 8) return 8;
-    if (per <= 16) return 16;
-    if (per <= 80) return 80;
-    if (per <= 128) return 128;
-    return 0;
+static uint32_t chunk_for(uint32_t vocab, uint32_t c) {
+    uint32_t chunk = (vocab + c - 1) / c;
+    return (chunk + 7u) / 8u * 8u;
 }
 
-bool plan_for_vocab(uint32_t vocab, LaunchPlan* plan) {
+bool plan_rows(uint32_t vocab, uint32_t n_rows, LaunchPlan* plan) {
     if (vocab == 0) return false;
-    uint32_t chunk = (vocab + kC - 1) / kC;
-    chunk = (chunk + 7u) / 8u * 8u;
-    const int ept = pick_ept(chunk);
-    if (ept == 0) return false;
-    plan->ept = ept;
-    plan->chunk = chunk;
-    plan->smem = make_layout(chunk).total;
+    uint32_t c = 1;
+    while (c <= 16 && chunk_for(vocab, c) > kMaxChunk) c *= 2;
+    if (c > 16) return false;
+    // widen the cluster while the batch would leave more than half of the SMs idle
+    const uint32_t sms = 148;
+    while (c < 8 && n_rows > 0 && static_cast<uint64_t>(n_rows) * c * 2 <= sms && chunk_for(vocab, 2 * c) >= 2048) c *= 2;
+    plan->cluster = c;
+    plan->chunk = chunk_for(vocab, c);
+    plan->smem = make_layout(plan->chunk, c).total;
     return plan->smem <= static_cast<size_t>(kMaxSmem);
 }
 

@@ -2,13 +2,14 @@
 // smp_row.cuh - the B200 (sm_100a) row engine behind sixi_smp_sample / _candidates /
 // _greedy_argmax / _verify.
 //
-// One cluster of kC CTAs owns one logits row. CTA c bulk-copies (TMA, cp.async.bulk) its
-// contiguous chunk of the row from HBM into shared memory once, converts it to 32-bit monotone
-// keys held in registers while applying the grammar mask, the NaN/Inf check and the
-// repetition/presence penalties, and from then on every step (argmax, top-k, softmax mass,
-// top-p / min-p crossing, the draw, the verifier's accept test and residual) runs on the
-// register-resident row with block reductions and DSMEM exchanges inside the cluster. HBM is read
-// exactly once per row: the path is bandwidth-bound and uses no tensor cores.
+// One cluster of C CTAs (C = 1..16, chosen per vocabulary and batch) owns one logits row. CTA c
+// bulk-copies (TMA, cp.async.bulk) its contiguous chunk of the row from HBM into shared memory in
+// kStages pipelined stages and converts each stage in place into 32-bit monotone keys while the
+// next stages are still in flight, applying the grammar mask, the NaN/Inf check and the
+// repetition/presence penalties on the way. From then on every step (argmax, top-k, softmax mass,
+// top-p / min-p crossing, the draw, the verifier's accept test and residual) runs over the
+// shared-memory-resident keys with compact loops, block reductions and DSMEM exchanges inside the
+// cluster. HBM is read exactly once per row: the path is bandwidth-bound and uses no tensor cores.
 //
 // Reference semantics (Sixi-ASI engine):
 //   DeterministicSampler::sample_greedy_argmax        src/core/core_execution.cpp:394-407
@@ -26,13 +27,14 @@
 //   * mass path (top_k = 0 or k > kKS): an exp-domain histogram of fixed-point weights is reduced
 //     over the cluster, then the crossing bin of each selection (k boundary, top-p, draw,
 //     residual) is gathered into every CTA and resolved exactly by a radix select over the unique
-//     (key, id) composites. Integer masses make every CTA reach identical decisions.
+//     (key, id) composites; bins too full to gather are refined by key digits across the cluster.
+//     Integer masses make every CTA reach identical decisions.
 //
 // Cluster barriers: every cluster.sync() sits at the top level of the kernel, and whether a CTA
 // reaches the next one depends only on data every CTA of the cluster holds identically (the
 // exchanged row statistics, the assembled histograms, gathered sets and pushed partial results),
-// so all CTAs of a cluster take the same barriers. The only wait the kernel spins on (the
-// mbarrier of its own bulk copy) is bounded and reports SIXI_BACKEND_ERROR on expiry.
+// so all CTAs of a cluster take the same barriers. The only waits the kernel spins on (the
+// mbarriers of its own bulk copies) are bounded and report SIXI_BACKEND_ERROR on expiry.
 #include <cooperative_groups.h>
 
 #include <cfloat>
@@ -45,48 +47,51 @@ namespace cg = cooperative_groups;
 
 namespace sixi_b200 {
 
-constexpr int kC = 8;          // CTAs per row (cluster size)
-constexpr int kNT = 256;       // threads per CTA
-constexpr int kNW = kNT / 32;  // warps per CTA
-constexpr int kKS = 256;       // max candidates of the list path
-constexpr int kLCap = 1024;    // local candidate superset capacity
-constexpr int kGCap = 1024;    // gathered-bin capacity
-constexpr int kSeg = kABins / kC;
-constexpr int kMaxRounds = 48; // bound on the mass path's exchange rounds (normally 2-5)
+constexpr int kNT = 512;        // threads per CTA
+constexpr int kNW = kNT / 32;   // warps per CTA
+constexpr int kCMax = 16;       // largest cluster
+constexpr int kKS = 256;        // max candidates of the list path
+constexpr int kLCap = 1536;     // local candidate superset capacity
+constexpr int kGCap = 1536;     // gathered-bin capacity
+constexpr int kTB = 2048;       // bins of the per-thread-maximum histogram
+constexpr int kStages = 4;      // bulk-copy pipeline stages per chunk
+constexpr int kVecMax = 5;      // 16-byte vectors per thread per stage (bound, see plan)
+constexpr int kMaxRounds = 48;  // bound on the mass path's exchange rounds (normally 2-5)
 constexpr uint32_t kWaitIters = 1u << 24;
 constexpr uint32_t kNoList = 0xFFFFFFFFu;
-constexpr int kMaxSmem = 227 * 1024;  // per-block opt-in limit of sm_100
+constexpr int kMaxSmem = 227 * 1024;       // per-block opt-in limit of sm_100
+constexpr uint32_t kMaxChunk = 37984;      // keys per CTA (148,352 bytes)
 
-static_assert(kNT == 256 && kNW == 8, "block primitives assume 8 warps");
 static_assert(kKS <= kNT, "list path assumes one candidate per thread");
+static_assert((kMaxChunk * 4 / 16 + kStages * kNT - 1) / (kStages * kNT) <= kVecMax, "stage vectors");
 
 // ---------------------------------------------------------------------------------------------
 // shared memory layout
 
 struct RowStat {
-    unsigned long long best;   // max composite (key, id) over valid entries; 0 if none
-    unsigned long long first;  // (first allowed id << 1) | raw-NaN flag; ~0 if none
-    unsigned long long dkey;   // (1 << 32) | key of the draft token if it lies in this chunk
-    unsigned int min_key;      // min key over valid entries
-    unsigned int n_allowed;    // allowed in-range entries
-    unsigned int bad;          // bit 0: an allowed entry was NaN/Inf; bit 1: copy wait expired
-    unsigned int pad;
+    unsigned long long best;  // max composite (key, id) over valid entries; 0 if none
+    unsigned int min_key;     // min key over valid entries
+    unsigned int n_allowed;   // allowed in-range entries
+    unsigned int first;       // first allowed id (0xFFFFFFFF if none)
+    unsigned int flags;       // bit 0: allowed entry NaN/Inf; bit 1: copy wait expired;
+                              // bit 2: the first allowed entry is NaN (raw-argmax modes)
+    unsigned int dkey;        // key of the draft token when it lies in this chunk
+    unsigned int dhas;        // 1 when the draft token lies in this chunk
 };
 
 struct ClusterShared {  // written by remote CTAs of the cluster
-    RowStat xs[kC];
-    unsigned long long z[kC];     // partial weight sums
-    unsigned long long wmin[kC];  // partial min-p prefix weight
-    unsigned long long segw[kC];  // reduced segment weight totals (unused beyond checks)
-    unsigned long long cnt[kC];   // partial counts
-    double rsum[kC];              // dense residual partial sums
-    double psum[kC];              // dense fallback (p_target) partial sums
-    unsigned long long mm[kC];    // refine: (min key << 32) | max key of the bin's entries
-    unsigned long long rcnt[kC];  // refine: tie counts
-    unsigned long long rsel;      // refine: composite of the crossing tie (from its owner)
-    unsigned int lcnt[kC];        // list path: list lengths pushed to CTA 0
-    unsigned int gcnt[2];         // gather buffer counters
-    int result;                   // token sent to CTA 0 by the dense-residual owner
+    RowStat xs[kCMax];
+    unsigned long long z[kCMax];     // partial weight sums
+    unsigned long long wmin[kCMax];  // partial min-p prefix weight
+    unsigned long long cnt[kCMax];   // partial counts
+    unsigned long long mm[kCMax];    // refine: (min key << 32) | max key of the bin's entries
+    unsigned long long rcnt[kCMax];  // refine: tie counts
+    double rsum[kCMax];              // dense residual partial sums
+    double psum[kCMax];              // dense fallback (p_target) partial sums
+    unsigned long long rsel;         // refine: composite of the crossing tie (from its owner)
+    unsigned int lcnt[kCMax];        // list path: list lengths pushed to CTA 0
+    unsigned int gcnt[2];            // gather buffer counters
+    int result;                      // token sent to CTA 0 by the dense-residual owner
     int pad;
 };
 
@@ -95,55 +100,57 @@ struct LocalShared {
     unsigned int red32[kNW];
     unsigned long long bc[16];  // broadcast scalars
     double bcd[kNW];
-    uint64_t mbar[1];
+    unsigned int lcount;        // local list fill counter
+    unsigned int pad;
+    uint64_t mbar[kStages];
 };
 
 struct Layout {
-    uint32_t off_ls, off_hb, off_mw, off_dyn;
-    // work area (relative to off_dyn)
-    uint32_t off_h, off_hc, off_r, off_rc, off_cg, off_cgc, off_g0, off_g1, off_bh, off_bw;
-    uint32_t off_ll, off_ma, off_fl, off_fp, off_fq;
+    uint32_t off_ls, off_dyn;
+    // relative to off_dyn
+    uint32_t off_k, off_x, off_y, off_z, off_r, off_f;
+    uint32_t seg;  // histogram bins reduced by each CTA
     uint32_t dyn_bytes, total;
 };
 
 __host__ __device__ inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+__host__ __device__ inline uint32_t umax(uint32_t a, uint32_t b) { return a > b ? a : b; }
 
-__host__ __device__ inline Layout make_layout(uint32_t chunk) {
+// Regions (lifetimes):
+//   K  keys (staging area of the bulk copies, then the keys of the chunk; live throughout)
+//   X  list path: MA, CTA 0's merge area (remote writes before CS1, read in phase B);
+//      mass path: H/HC local histograms (remote reads between CS2 and CS3), then CG/CGC
+//   Y  phase A: history bitmap + mask words (until P0 ends), then the local list LL;
+//      mass path: the two gather buffers
+//   Z  phase A: per-thread-maximum histogram; later the block-select digit histograms BH/BW
+//   R  reduced histogram segment (remote reads right after CS3), then the refine rounds
+//      double-buffered digit histograms (remote reads, first written two rounds after CS3)
+//   F  FL/FP/FQ: CTA 0's sorted candidates, probabilities and scratch
+__host__ __device__ inline Layout make_layout(uint32_t chunk, uint32_t C) {
     Layout L{};
     uint32_t o = align_up(static_cast<uint32_t>(sizeof(ClusterShared)), 16);
     L.off_ls = o;
     o = align_up(o + static_cast<uint32_t>(sizeof(LocalShared)), 16);
-    L.off_hb = o;
-    o = align_up(o + 4u * (chunk / 32u + 2u), 16);
-    L.off_mw = o;
-    o = align_up(o + 4u * (chunk / 32u + 4u), 128);
-    L.off_dyn = o;
-    // Work area. Lifetimes: the thread-maximum histogram (u32) aliases H and the local list LL
-    // aliases CG (both die before the first cluster barrier); the list-path merge area MA aliases
-    // the two gather buffers (MA dies before the first gather).
+    L.off_dyn = align_up(o, 128);
+    L.seg = kABins / C;
     uint32_t w = 0;
-    L.off_h = w;   w += 8u * kABins;
-    L.off_hc = w;  w += 4u * kABins;
-    L.off_r = w;   w += 8u * kSeg;
-    L.off_rc = w;  w += 4u * kSeg;
-    L.off_cg = w;  w += 8u * kABins;
-    L.off_cgc = w; w += 4u * kABins;
-    L.off_ll = L.off_cg;
-    L.off_g0 = w;  w += 8u * kGCap;
-    L.off_g1 = w;  w += 8u * kGCap;
-    L.off_ma = L.off_g0;
-    L.off_bh = w;  w += 4u * 256u;
-    L.off_bw = w;  w += 8u * 256u;
-    L.off_fl = w;  w += 8u * kKS;
-    L.off_fp = w;  w += 8u * kKS;
-    L.off_fq = w;  w += 8u * kKS;
-    const uint32_t stg = 4u * chunk;
-    L.dyn_bytes = w > stg ? w : stg;
-    L.total = L.off_dyn + L.dyn_bytes;
+    L.off_k = w;
+    w += align_up(4u * chunk, 128);
+    L.off_x = w;
+    w += align_up(umax(8u * C * kKS, 12u * kABins), 128);
+    L.off_y = w;
+    const uint32_t bitwords = 4u * (chunk / 32u + 2u) + 4u * (chunk / 32u + 4u);
+    w += align_up(umax(umax(8u * kLCap, 16u * kGCap), bitwords), 128);
+    L.off_z = w;
+    w += align_up(umax(4u * kTB, 4u * 256u + 8u * 256u), 128);
+    L.off_r = w;
+    w += align_up(umax(12u * L.seg, 6144u), 128);
+    L.off_f = w;
+    w += 3u * 8u * kKS;
+    L.dyn_bytes = w;
+    L.total = L.off_dyn + w;
     return L;
 }
-static_assert(8 * kC * kKS <= 2 * 8 * kGCap, "MA must fit in the gather buffers");
-static_assert(8 * kLCap <= 8 * kABins, "LL must fit in CG");
 
 // ---------------------------------------------------------------------------------------------
 // per-row context
@@ -245,11 +252,6 @@ __device__ __forceinline__ float penalize(float v, const sixi_smp_params* p) {
     return __fsub_rn(v, p->presence_penalty);
 }
 
-template <int SW>
-__device__ __forceinline__ int elem_of(int j, int i) {
-    return SW * (static_cast<int>(threadIdx.x) + kNT * j) + i;
-}
-
 // block-wide helpers (all threads call) -------------------------------------------------------
 
 __device__ __forceinline__ double block_sum_f64(double v, LocalShared* ls) {
@@ -282,9 +284,19 @@ __device__ __forceinline__ double block_incl_f64(double v, LocalShared* ls, doub
     return before + inc;
 }
 
-// smallest value over the block of v (u64), all threads get it
 __device__ __forceinline__ unsigned long long block_min_bc(unsigned long long v, LocalShared* ls) {
     return block_min_u64<kNT>(v, ls->red);
+}
+
+// warp-aggregated reservation of `n` slots (per lane) in a counter; returns the lane's first slot
+__device__ __forceinline__ uint32_t warp_reserve(uint32_t n, unsigned int* counter) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t incl = warp_incl_u32(n);
+    const uint32_t total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+    uint32_t base = 0;
+    if (lane == 31 && total > 0) base = atomicAdd(counter, total);
+    base = __shfl_sync(0xFFFFFFFFu, base, 31);
+    return base + incl - n;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -293,10 +305,10 @@ __device__ __forceinline__ unsigned long long block_min_bc(unsigned long long v,
 // which the running sum (count, or weight when wc != nullptr) reaches `target` (>= 1) and returns
 // it; *cum_through receives the running sum through it. Returns 0 when the target is not reached.
 inline __device__ unsigned long long block_select(const unsigned long long* g, uint32_t n,
-                                           unsigned long long target, const WeightCtx* wc,
-                                           unsigned long long lowb, unsigned long long excl,
-                                           uint32_t* bh, unsigned long long* bw, LocalShared* ls,
-                                           unsigned long long* cum_through) {
+                                                  unsigned long long target, const WeightCtx* wc,
+                                                  unsigned long long lowb, unsigned long long excl,
+                                                  uint32_t* bh, unsigned long long* bw,
+                                                  LocalShared* ls, unsigned long long* cum_through) {
     const int tid = threadIdx.x;
     unsigned long long andv = ~0ull, orv = 0ull;
     uint32_t cnt_l = 0;
@@ -359,7 +371,7 @@ inline __device__ unsigned long long block_select(const unsigned long long* g, u
             if (c < lowb || c == excl || (c & pmask) != prefix) continue;
             const unsigned int d = static_cast<unsigned int>(c >> shift) & (nd - 1u);
             atomicAdd(&bh[d], 1u);
-            if (wc) atomicAdd(&bw[d], weight_of(kval(comp_key(c)), *wc));
+            if (wc) atomicAdd(&bw[d], static_cast<unsigned long long>(weight_of(kval(comp_key(c)), *wc)));
         }
         __syncthreads();
         if (tid < 32) {
@@ -429,23 +441,72 @@ inline __device__ unsigned long long block_select(const unsigned long long* g, u
 }
 
 // ---------------------------------------------------------------------------------------------
-// mass-path state machine stages
+// warp-level scans over kKS candidates held kPL per lane (candidate order = lane-major)
+
+constexpr int kPL = kKS / 32;
+
+// first candidate index whose inclusive cumulative is >= t (0xFFFFFFFF if none below n)
+__device__ __forceinline__ uint32_t lane_first_cum_ge(const double (&v)[kPL], double t, uint32_t n, int lane) {
+    double run = 0.0;
+#pragma unroll
+    for (int j = 0; j < kPL; ++j) run += v[j];
+    double acc = warp_incl_f64(run) - run;
+    uint32_t mine = 0xFFFFFFFFu;
+#pragma unroll
+    for (int j = 0; j < kPL; ++j) {
+        acc += v[j];
+        const uint32_t idx = lane * kPL + j;
+        if (mine == 0xFFFFFFFFu && idx < n && acc >= t) mine = idx;
+    }
+    return __reduce_min_sync(0xFFFFFFFFu, mine);
+}
+
+// first candidate index whose inclusive cumulative is > u (the CDF draw `u < cdf`)
+__device__ __forceinline__ uint32_t lane_first_cum_gt(const double (&v)[kPL], double u, uint32_t n, int lane) {
+    double run = 0.0;
+#pragma unroll
+    for (int j = 0; j < kPL; ++j) run += v[j];
+    double acc = warp_incl_f64(run) - run;
+    uint32_t mine = 0xFFFFFFFFu;
+#pragma unroll
+    for (int j = 0; j < kPL; ++j) {
+        acc += v[j];
+        const uint32_t idx = lane * kPL + j;
+        if (mine == 0xFFFFFFFFu && idx < n && u < acc) mine = idx;
+    }
+    return __reduce_min_sync(0xFFFFFFFFu, mine);
+}
+
+// renormalise the first `keep` candidates to sum 1
+__device__ __forceinline__ void lane_renorm(double (&v)[kPL], uint32_t keep, int lane) {
+    double s = 0.0;
+#pragma unroll
+    for (int j = 0; j < kPL; ++j) s += (lane * kPL + j < keep) ? v[j] : 0.0;
+    const double r = warp_sum_f64(s);
+    if (r > 0.0) {
+#pragma unroll
+        for (int j = 0; j < kPL; ++j) v[j] /= r;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// mass-path state machine
+
 enum Stage : int {
-    kStKBound = 0,   // find the k-th candidate (count select)
-    kStTopP = 1,     // top-p crossing (weight select)
-    kStKept = 2,     // min-p, then the verifier's accept test
-    kStDraw = 3,     // the draw (weight select)
-    kStResid = 4,    // one-hot residual draw without the draft (weight select)
-    kStDSum = 5,     // dense residual: partial sums pushed
-    kStDFind = 6,    // dense residual: owner CTA finds the token, sends it to CTA 0
-    kStDWait = 7,    // dense residual: CTA 0 reads the token
-    kStCount = 8,    // candidates: kept count partials pushed
-    kStDone = 9
+    kStKBound = 0,  // find the k-th candidate (count select)
+    kStTopP = 1,    // top-p crossing (weight select)
+    kStKept = 2,    // min-p, then the verifier's accept test
+    kStDraw = 3,    // the draw (weight select)
+    kStResid = 4,   // one-hot residual draw without the draft (weight select)
+    kStDSum = 5,    // dense residual: partial sums pushed
+    kStDWait = 6,   // dense residual: CTA 0 reads the token
+    kStCount = 7,   // candidates: kept count partials pushed
+    kStDone = 8
 };
 
 struct LState {
     int stage;
-    int pending_bin;  // bin gathered this round (-1 none)
+    int pending_bin;  // bin of the pending selection (-1 none)
     int pending_kind; // 0 none, 1 gather, 2 exchange, 3 refine
     unsigned long long target;
     unsigned long long zk, zkept, kbound, xcross, excl, wexcl;
@@ -467,76 +528,96 @@ struct Refine {
     int top, shift, width;
     unsigned long long above_c, above_w, tie_w;
     int buf;
+    uint32_t klo, khi;  // key interval of the bin
 };
 
 // ---------------------------------------------------------------------------------------------
 
-template <int EPT, int DT, int MODE>
-__global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const RowArgs a) {
-    constexpr int SW = (DT == SIXI_SMP_BF16) ? 8 : 4;
-    constexpr int NV = EPT / SW;
+template <int DT, int MODE>
+__global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     constexpr int ESZ = (DT == SIXI_SMP_BF16) ? 2 : 4;
-    static_assert(EPT % 8 == 0, "EPT must be a multiple of 8");
+    constexpr int EPV = 16 / ESZ;  // input elements per 16-byte vector
 
     extern __shared__ __align__(128) uint8_t smem[];
     cg::cluster_group cluster = cg::this_cluster();
+    const uint32_t C = cluster.num_blocks();
     const uint32_t crank = cluster.block_rank();
-    const uint32_t row = blockIdx.x / kC;
+    const uint32_t row = blockIdx.x / C;
     const int tid = threadIdx.x;
-    const Layout lay = make_layout(a.chunk);
+    const int lane = tid & 31;
+    const Layout lay = make_layout(a.chunk, C);
 
     ClusterShared* cs = reinterpret_cast<ClusterShared*>(smem);
     LocalShared* ls = reinterpret_cast<LocalShared*>(smem + lay.off_ls);
-    uint32_t* hb = reinterpret_cast<uint32_t*>(smem + lay.off_hb);
-    uint32_t* mw = reinterpret_cast<uint32_t*>(smem + lay.off_mw);
     uint8_t* dyn = smem + lay.off_dyn;
-    float* stg = reinterpret_cast<float*>(dyn);
-    unsigned long long* H = reinterpret_cast<unsigned long long*>(dyn + lay.off_h);
-    uint32_t* H32 = reinterpret_cast<uint32_t*>(dyn + lay.off_h);
-    uint32_t* HC = reinterpret_cast<uint32_t*>(dyn + lay.off_hc);
+    uint32_t* K = reinterpret_cast<uint32_t*>(dyn + lay.off_k);
+    float* KF = reinterpret_cast<float*>(dyn + lay.off_k);
+    // X
+    unsigned long long* MA = reinterpret_cast<unsigned long long*>(dyn + lay.off_x);
+    unsigned long long* H = reinterpret_cast<unsigned long long*>(dyn + lay.off_x);
+    uint32_t* HC = reinterpret_cast<uint32_t*>(dyn + lay.off_x + 8u * kABins);
+    unsigned long long* CG = H;    // H is dead once the segments are reduced
+    uint32_t* CGC = HC;
+    // Y
+    uint32_t* hb = reinterpret_cast<uint32_t*>(dyn + lay.off_y);
+    uint32_t* mw = hb + (a.chunk / 32u + 2u);
+    unsigned long long* LL = reinterpret_cast<unsigned long long*>(dyn + lay.off_y);
+    unsigned long long* G0 = reinterpret_cast<unsigned long long*>(dyn + lay.off_y);
+    unsigned long long* G1 = G0 + kGCap;
+    // Z
+    uint32_t* H32 = reinterpret_cast<uint32_t*>(dyn + lay.off_z);
+    uint32_t* BH = reinterpret_cast<uint32_t*>(dyn + lay.off_z);
+    unsigned long long* BW = reinterpret_cast<unsigned long long*>(dyn + lay.off_z + 1024u);
+    // R
     unsigned long long* R = reinterpret_cast<unsigned long long*>(dyn + lay.off_r);
-    uint32_t* RC = reinterpret_cast<uint32_t*>(dyn + lay.off_rc);
-    unsigned long long* CG = reinterpret_cast<unsigned long long*>(dyn + lay.off_cg);
-    uint32_t* CGC = reinterpret_cast<uint32_t*>(dyn + lay.off_cgc);
-    unsigned long long* LL = reinterpret_cast<unsigned long long*>(dyn + lay.off_ll);
-    unsigned long long* G0 = reinterpret_cast<unsigned long long*>(dyn + lay.off_g0);
-    unsigned long long* G1 = reinterpret_cast<unsigned long long*>(dyn + lay.off_g1);
-    uint32_t* BH = reinterpret_cast<uint32_t*>(dyn + lay.off_bh);
-    unsigned long long* BW = reinterpret_cast<unsigned long long*>(dyn + lay.off_bw);
-    unsigned long long* MA = reinterpret_cast<unsigned long long*>(dyn + lay.off_ma);
-    unsigned long long* FL = reinterpret_cast<unsigned long long*>(dyn + lay.off_fl);
-    double* FP = reinterpret_cast<double*>(dyn + lay.off_fp);
-    double* FQ = reinterpret_cast<double*>(dyn + lay.off_fq);
+    uint32_t* RC = reinterpret_cast<uint32_t*>(dyn + lay.off_r + 8u * lay.seg);
+    // F
+    unsigned long long* FL = reinterpret_cast<unsigned long long*>(dyn + lay.off_f);
+    double* FP = reinterpret_cast<double*>(dyn + lay.off_f + 8u * kKS);
+    double* FQ = reinterpret_cast<double*>(dyn + lay.off_f + 16u * kKS);
 
-    const RowCtx rc = make_row_ctx<MODE>(a, row);
-    const sixi_smp_params* P = rc.p;
     const int32_t c0 = static_cast<int32_t>(crank * a.chunk);
-    int32_t len = static_cast<int32_t>(a.vocab) - c0;
-    if (len < 0) len = 0;
-    if (len > static_cast<int32_t>(a.chunk)) len = static_cast<int32_t>(a.chunk);
-    if (!rc.active) len = 0;
-    const uint8_t* gchunk = rc.row + static_cast<size_t>(c0) * ESZ;
+    int32_t len_load = static_cast<int32_t>(a.vocab) - c0;
+    if (len_load < 0) len_load = 0;
+    if (len_load > static_cast<int32_t>(a.chunk)) len_load = static_cast<int32_t>(a.chunk);
+    const uint8_t* gchunk = static_cast<const uint8_t*>(a.data) +
+                            (static_cast<size_t>(row) * a.row_stride + static_cast<size_t>(c0)) * ESZ;
 
     // ======================================================================== phase A
-    // bulk copy of the chunk (fp32 at the start of the staging area, bf16 in its upper half)
-    const int32_t tma_bytes = a.use_tma ? (len * ESZ) / 16 * 16 : 0;
+    // The bulk copies go out first (they need only the row address); the parameters, mask words
+    // and history are read while they are in flight.
+    const int32_t tma_bytes = a.use_tma ? (len_load * ESZ) / 16 * 16 : 0;
     const int32_t len_t = tma_bytes / ESZ;
-    uint8_t* stg_dst = (DT == SIXI_SMP_BF16) ? dyn + 2u * a.chunk : dyn;
+    const int32_t nvec = tma_bytes / 16;
+    uint8_t* stg = (DT == SIXI_SMP_BF16) ? dyn + lay.off_k + 2u * a.chunk : dyn + lay.off_k;
+    auto stage_vec = [&](int s) { return static_cast<int32_t>((static_cast<int64_t>(nvec) * s) / kStages); };
     if (tid == 0) {
-        mbar_init(&ls->mbar[0], 1);
+#pragma unroll
+        for (int s = 0; s < kStages; ++s) mbar_init(&ls->mbar[s], 1);
         fence_mbar_init();
-        if (tma_bytes > 0) {
-            mbar_arrive_expect_tx(&ls->mbar[0], static_cast<uint32_t>(tma_bytes));
-            for (int32_t off = 0; off < tma_bytes; off += 32768) {
-                const int32_t nb = (tma_bytes - off) < 32768 ? (tma_bytes - off) : 32768;
-                bulk_g2s(stg_dst + off, gchunk + off, static_cast<uint32_t>(nb), &ls->mbar[0]);
+        for (int s = 0; s < kStages; ++s) {
+            const int32_t b0 = stage_vec(s) * 16, b1 = stage_vec(s + 1) * 16;
+            if (b1 <= b0) continue;
+            mbar_arrive_expect_tx(&ls->mbar[s], static_cast<uint32_t>(b1 - b0));
+            for (int32_t off = b0; off < b1; off += 32768) {
+                const int32_t nb = (b1 - off) < 32768 ? (b1 - off) : 32768;
+                bulk_g2s(stg + off, gchunk + off, static_cast<uint32_t>(nb), &ls->mbar[s]);
             }
         }
         cs->gcnt[0] = 0;
         cs->gcnt[1] = 0;
         cs->result = -1;
+        cs->rsel = 0ull;
         ls->bc[15] = 0;
+        ls->lcount = 0;
     }
+
+    const RowCtx rc = make_row_ctx<MODE>(a, row);
+    const sixi_smp_params* P = rc.p;
+    const int32_t len = rc.active ? len_load : 0;
+    const int nq = (len + 3) >> 2;  // 4-key groups of this chunk
+    const int nq_iter = (nq + kNT - 1) / kNT;
+
     const int nbw = static_cast<int>(a.chunk / 32u + 2u);
     for (int i = tid; i < nbw; i += kNT) hb[i] = 0u;
     const uint32_t wbase = static_cast<uint32_t>(c0) >> 5;
@@ -554,179 +635,280 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
     };
     const int64_t nht = rc.nh + rc.n_extra;
     const bool pen_smem = rc.pen && P->frequency_penalty != 0.0f;
-    // unique history ids of this chunk -> bitmap (overlaps the bulk copy)
+    // unique history ids of this chunk -> bitmap (overlaps the bulk copy; 4 loads in flight)
     if (rc.pen && len > 0) {
-        for (int64_t j = tid; j < nht; j += kNT) {
-            const int32_t t = hist_at(rc, j);
-            if (t < c0 || t >= c0 + len || !allowed(t)) continue;
-            const int32_t e = t - c0;
-            atomicOr(&hb[e >> 5], 1u << (e & 31));
+        for (int64_t j0 = tid; j0 < nht; j0 += 4 * kNT) {
+            int32_t t4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t j = j0 + u * kNT;
+                t4[u] = j < nht ? hist_at(rc, j) : -1;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int32_t t = t4[u];
+                if (t < c0 || t >= c0 + len || !allowed(t)) continue;
+                const int32_t e = t - c0;
+                atomicOr(&hb[e >> 5], 1u << (e & 31));
+            }
         }
     }
-    if (tma_bytes > 0) {
-        if (!mbar_wait(&ls->mbar[0], 0, kWaitIters)) ls->bc[15] = 1;
+    // allowed count and first allowed id of this chunk (from the mask words, not per element)
+    uint32_t t_cnt = 0, t_first = 0xFFFFFFFFu;
+    if (rc.mask == nullptr) {
+        if (tid == 0 && len > 0) {
+            t_cnt = static_cast<uint32_t>(len);
+            t_first = static_cast<uint32_t>(c0);
+        }
+    } else {
+        const int32_t w_lo = 0, w_hi = (len > 0) ? static_cast<int32_t>(((c0 + len - 1) >> 5) - wbase) : -1;
+        for (int32_t i = w_lo + tid; i <= w_hi; i += kNT) {
+            uint32_t w = mw[i];
+            const int32_t g0 = static_cast<int32_t>((wbase + i) << 5);
+            if (g0 < c0) w &= ~0u << (c0 - g0);
+            if (g0 + 32 > c0 + len) w &= (c0 + len - g0) >= 32 ? ~0u : ((1u << (c0 + len - g0)) - 1u);
+            t_cnt += __popc(w);
+            if (w && t_first == 0xFFFFFFFFu) t_first = static_cast<uint32_t>(g0 + __ffs(w) - 1);
+        }
     }
     __syncthreads();
-    if (pen_smem && len > 0) {
-        // frequency-penalty rows: materialise the chunk as fp32 in shared memory, apply the
-        // per-unique penalty, then the per-occurrence frequency penalty (identical addends, so the
-        // order of the atomic updates does not change the result)
+
+    auto load_global = [&](int32_t e) -> float {
         if (DT == SIXI_SMP_BF16) {
-            const uint16_t* src = reinterpret_cast<const uint16_t*>(dyn + 2u * a.chunk);
-            for (int32_t t0 = 0; t0 < len; t0 += kNT * 8) {
-                float v[8];
+            const uint16_t b = reinterpret_cast<const uint16_t*>(gchunk)[e];
+            return __uint_as_float(static_cast<uint32_t>(b) << 16);
+        }
+        return reinterpret_cast<const float*>(gchunk)[e];
+    };
+    // P0: staged input -> keys, in place. Per entry: mask bit, |bits| for the NaN/Inf check,
+    // -0 -> +0, monotone key, running max (first occurrence) and min. Entries in the penalty
+    // bitmap are excluded from the running statistics here and fixed up sparsely afterwards.
+    // (Straight-line code with register accumulators: no lambda captures of mutable state.)
+    constexpr bool kRaw = (MODE == kModeGreedy) || (MODE == kModeVerify);
+    const bool has_mask = rc.mask != nullptr;
+    const bool use_pbits = rc.pen && !pen_smem;
+    uint32_t t_mk = 0u, t_mi = 0u, t_mn = 0xFFFFFFFFu, t_amax = 0u;
+#define SIXI_ADMIT(E, XV, MBIT, PBIT, KOUT)                                                   \
+    {                                                                                        \
+        float x_ = (XV);                                                                     \
+        const bool ok_ = (MBIT) && (E) < len;                                                \
+        const uint32_t raw_ = __float_as_uint(x_) & 0x7FFFFFFFu;                             \
+        t_amax = (ok_ && raw_ > t_amax) ? raw_ : t_amax;                                     \
+        x_ = __fadd_rn(x_, 0.0f);                                                            \
+        const uint32_t b_ = __float_as_uint(x_);                                             \
+        uint32_t k_ = b_ ^ (static_cast<uint32_t>(static_cast<int32_t>(b_) >> 31) | 0x80000000u); \
+        if (kRaw && x_ != x_) k_ = 0u;                                                       \
+        k_ = ok_ ? k_ : 0u;                                                                  \
+        const uint32_t ks_ = (PBIT) ? 0u : k_;                                               \
+        if (ks_ > t_mk) {                                                                    \
+            t_mk = ks_;                                                                      \
+            t_mi = static_cast<uint32_t>(E);                                                 \
+        }                                                                                    \
+        t_mn = (ks_ != 0u && ks_ < t_mn) ? ks_ : t_mn;                                       \
+        (KOUT) = k_;                                                                         \
+    }
+    if (!pen_smem) {
+        for (int s = 0; s < kStages; ++s) {
+            const int32_t v0 = stage_vec(s), v1 = stage_vec(s + 1);
+            if (v1 > v0) {
+                if (!mbar_wait(&ls->mbar[s], 0, kWaitIters)) ls->bc[15] = 1;
+            }
+            if (DT == SIXI_SMP_BF16) {
+                // keys overwrite the bf16 sources in place: read the whole stage first
+                uint4 raw4[kVecMax];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int32_t e = t0 + tid * 8 + i;
-                    uint16_t b = 0;
-                    if (e < len_t) b = src[e];
-                    else if (e < len) b = reinterpret_cast<const uint16_t*>(gchunk)[e];
-                    v[i] = __uint_as_float(static_cast<uint32_t>(b) << 16);
+                for (int m = 0; m < kVecMax; ++m) {
+                    const int32_t v = v0 + tid + m * kNT;
+                    if (v < v1) raw4[m] = *reinterpret_cast<const uint4*>(stg + 16u * v);
                 }
                 __syncthreads();
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int32_t e = t0 + tid * 8 + i;
-                    if (e < len) stg[e] = v[i];
+                for (int m = 0; m < kVecMax; ++m) {
+                    const int32_t v = v0 + tid + m * kNT;
+                    if (v < v1) {
+                        const int32_t e0 = v * 8;
+                        const uint32_t g = static_cast<uint32_t>(c0 + e0);
+                        const uint32_t mb = has_mask ? (mw[(g >> 5) - wbase] >> (g & 31)) & 0xFFu : 0xFFu;
+                        const uint32_t pb = use_pbits ? (hb[e0 >> 5] >> (e0 & 31)) & 0xFFu : 0u;
+                        const uint32_t w4[4] = {raw4[m].x, raw4[m].y, raw4[m].z, raw4[m].w};
+                        uint32_t k8[8];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            SIXI_ADMIT(e0 + 2 * i, __uint_as_float(w4[i] << 16), (mb >> (2 * i)) & 1u,
+                                       (pb >> (2 * i)) & 1u, k8[2 * i]);
+                            SIXI_ADMIT(e0 + 2 * i + 1, __uint_as_float(w4[i] & 0xFFFF0000u), (mb >> (2 * i + 1)) & 1u,
+                                       (pb >> (2 * i + 1)) & 1u, k8[2 * i + 1]);
+                        }
+                        *reinterpret_cast<uint4*>(K + e0) = make_uint4(k8[0], k8[1], k8[2], k8[3]);
+                        *reinterpret_cast<uint4*>(K + e0 + 4) = make_uint4(k8[4], k8[5], k8[6], k8[7]);
+                    }
+                }
+                __syncthreads();
+            } else {
+#pragma unroll
+                for (int m = 0; m < kVecMax; ++m) {
+                    const int32_t v = v0 + tid + m * kNT;
+                    if (v < v1) {
+                        const float4 f = *reinterpret_cast<const float4*>(stg + 16u * v);
+                        const int32_t e0 = v * 4;
+                        const uint32_t g = static_cast<uint32_t>(c0 + e0);
+                        const uint32_t mb = has_mask ? (mw[(g >> 5) - wbase] >> (g & 31)) & 0xFu : 0xFu;
+                        const uint32_t pb = use_pbits ? (hb[e0 >> 5] >> (e0 & 31)) & 0xFu : 0u;
+                        uint32_t k0, k1, k2, k3;
+                        SIXI_ADMIT(e0 + 0, f.x, mb & 1u, pb & 1u, k0);
+                        SIXI_ADMIT(e0 + 1, f.y, (mb >> 1) & 1u, (pb >> 1) & 1u, k1);
+                        SIXI_ADMIT(e0 + 2, f.z, (mb >> 2) & 1u, (pb >> 2) & 1u, k2);
+                        SIXI_ADMIT(e0 + 3, f.w, (mb >> 3) & 1u, (pb >> 3) & 1u, k3);
+                        *reinterpret_cast<uint4*>(K + e0) = make_uint4(k0, k1, k2, k3);
+                    }
+                }
+            }
+        }
+        for (int32_t e = len_t + tid; e < len; e += kNT) {  // ragged tail: plain loads
+            float x;
+            if (DT == SIXI_SMP_BF16) {
+                x = __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(gchunk)[e]) << 16);
+            } else {
+                x = reinterpret_cast<const float*>(gchunk)[e];
+            }
+            const uint32_t mb = allowed(c0 + e) ? 1u : 0u;
+            const uint32_t pb = use_pbits ? (hb[e >> 5] >> (e & 31)) & 1u : 0u;
+            uint32_t k;
+            SIXI_ADMIT(e, x, mb, pb, k);
+            K[e] = k;
+        }
+        if (use_pbits) {
+            // sparse penalty fix-up: each penalised id once (test-and-clear on the bitmap)
+            __syncthreads();
+            const float rep = P->repetition_penalty, pres = P->presence_penalty;
+            for (int64_t j = tid; j < nht; j += kNT) {
+                const int32_t t = hist_at(rc, j);
+                if (t < c0 || t >= c0 + len) continue;
+                const int32_t e = t - c0;
+                const uint32_t bit = 1u << (e & 31);
+                if (!(hb[e >> 5] & bit)) continue;
+                const uint32_t old = atomicAnd(&hb[e >> 5], ~bit);
+                if (!(old & bit)) continue;
+                float v = kval(K[e]);
+                if (rep != 1.0f && rep > 0.0f) v = (v < 0.0f) ? __fmul_rn(v, rep) : __fdiv_rn(v, rep);
+                v = __fsub_rn(v, pres);
+                v = __fadd_rn(v, 0.0f);
+                const uint32_t b = __float_as_uint(v);
+                uint32_t k = b ^ (static_cast<uint32_t>(static_cast<int32_t>(b) >> 31) | 0x80000000u);
+                K[e] = k;
+                if (k > t_mk || (k == t_mk && static_cast<uint32_t>(e) < t_mi)) {
+                    t_mk = k;
+                    t_mi = static_cast<uint32_t>(e);
+                }
+                t_mn = (k != 0u && k < t_mn) ? k : t_mn;
+            }
+        }
+    } else {
+        // frequency-penalty rows: fp32 values first, then the per-unique penalty, then the
+        // per-occurrence frequency penalty (identical addends, so the order of the atomic updates
+        // does not change the result), then keys
+        for (int s = 0; s < kStages; ++s) {
+            const int32_t v0 = stage_vec(s), v1 = stage_vec(s + 1);
+            if (v1 > v0) {
+                if (!mbar_wait(&ls->mbar[s], 0, kWaitIters)) ls->bc[15] = 1;
+            }
+            if (DT == SIXI_SMP_BF16) {
+                uint4 raw4[kVecMax];
+#pragma unroll
+                for (int m = 0; m < kVecMax; ++m) {
+                    const int32_t v = v0 + tid + m * kNT;
+                    if (v < v1) raw4[m] = *reinterpret_cast<const uint4*>(stg + 16u * v);
+                }
+                __syncthreads();
+#pragma unroll
+                for (int m = 0; m < kVecMax; ++m) {
+                    const int32_t v = v0 + tid + m * kNT;
+                    if (v < v1) {
+                        const uint32_t w4[4] = {raw4[m].x, raw4[m].y, raw4[m].z, raw4[m].w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            KF[v * 8 + 2 * i] = __uint_as_float(w4[i] << 16);
+                            KF[v * 8 + 2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
+                        }
+                    }
                 }
                 __syncthreads();
             }
-        } else {
-            for (int32_t e = len_t + tid; e < len; e += kNT) stg[e] = reinterpret_cast<const float*>(gchunk)[e];
-            __syncthreads();
         }
+        for (int32_t e = len_t + tid; e < len; e += kNT) KF[e] = load_global(e);
+        __syncthreads();
         for (int64_t j = tid; j < nht; j += kNT) {
             const int32_t t = hist_at(rc, j);
             if (t < c0 || t >= c0 + len || !allowed(t)) continue;
             const int32_t e = t - c0;
             const uint32_t bit = 1u << (e & 31);
             const uint32_t old = atomicAnd(&hb[e >> 5], ~bit);
-            if (old & bit) stg[e] = penalize(stg[e], P);
+            if (old & bit) KF[e] = penalize(KF[e], P);
         }
         __syncthreads();
         for (int64_t j = tid; j < nht; j += kNT) {
             const int32_t t = hist_at(rc, j);
             if (t < c0 || t >= c0 + len || !allowed(t)) continue;
-            atomicAdd(&stg[t - c0], -P->frequency_penalty);
+            atomicAdd(&KF[t - c0], -P->frequency_penalty);
         }
         __syncthreads();
+        for (int32_t e = tid; e < len; e += kNT) {
+            uint32_t k;
+            SIXI_ADMIT(e, KF[e], allowed(c0 + e) ? 1u : 0u, 0u, k);
+            K[e] = k;
+        }
     }
+#undef SIXI_ADMIT
+    // keys past the chunk end (up to a multiple of 4) are invalid
+    if (tid < 4 && len + tid < nq * 4) K[len + tid] = 0u;
+    __syncthreads();
 
-    // P0: shared / global -> register keys, with mask, NaN/Inf check and penalties
-    uint32_t keys[EPT];
-    unsigned long long t_best = 0ull, t_first = ~0ull, t_dkey = 0ull;
-    uint32_t t_min = 0xFFFFFFFFu, t_n = 0u, t_bad = 0u;
-#pragma unroll
-    for (int j = 0; j < NV; ++j) {
-        const int e0 = SW * (tid + kNT * j);
-        float xv[SW];
-        if (pen_smem) {
-#pragma unroll
-            for (int i = 0; i < SW; ++i) xv[i] = (e0 + i < len) ? stg[e0 + i] : 0.0f;
-        } else if (e0 + SW <= len_t) {
-            if (DT == SIXI_SMP_BF16) {
-                const uint4 v = *reinterpret_cast<const uint4*>(dyn + 2u * a.chunk + 2u * e0);
-                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    xv[2 * i] = __uint_as_float(w4[i] << 16);
-                    xv[2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
-                }
-            } else {
-                const float4 v = *reinterpret_cast<const float4*>(stg + e0);
-                xv[0] = v.x;
-                xv[1] = v.y;
-                xv[2] = v.z;
-                xv[3] = v.w;
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < SW; ++i) {
-                const int e = e0 + i;
-                float x = 0.0f;
-                if (e < len) {
-                    if (DT == SIXI_SMP_BF16) {
-                        const uint16_t b = reinterpret_cast<const uint16_t*>(gchunk)[e];
-                        x = __uint_as_float(static_cast<uint32_t>(b) << 16);
-                    } else {
-                        x = reinterpret_cast<const float*>(gchunk)[e];
-                    }
-                }
-                xv[i] = x;
-            }
-        }
-        uint32_t mbits = (1u << SW) - 1u;
-        if (rc.mask != nullptr && e0 < len) {
-            const uint32_t g = static_cast<uint32_t>(c0 + e0);
-            mbits = (mw[(g >> 5) - wbase] >> (g & 31)) & ((1u << SW) - 1u);
-        }
-        uint32_t pbits = 0;
-        if (rc.pen && !pen_smem && e0 < len) pbits = (hb[e0 >> 5] >> (e0 & 31)) & ((1u << SW) - 1u);
-#pragma unroll
-        for (int i = 0; i < SW; ++i) {
-            const int e = e0 + i;
-            const bool ok = (e < len) && ((mbits >> i) & 1u);
-            float x = xv[i];
-            uint32_t k = 0u;
-            if (ok) {
-                const bool nan = isnan(x);
-                if (!isfinite(x)) t_bad = 1u;
-                const unsigned long long f = (static_cast<unsigned long long>(c0 + e) << 1) | (nan ? 1ull : 0ull);
-                t_first = f < t_first ? f : t_first;
-                ++t_n;
-                if ((pbits >> i) & 1u) x = penalize(x, P);
-                if (!isnan(x)) {
-                    k = fkey(x);
-                    const unsigned long long cp = comp_of(k, static_cast<uint32_t>(c0 + e));
-                    t_best = cp > t_best ? cp : t_best;
-                    t_min = k < t_min ? k : t_min;
-                }
-            }
-            if (e < len && c0 + e == rc.draft) t_dkey = (1ull << 32) | k;
-            keys[j * SW + i] = k;
-        }
-    }
     // block reduction of the row statistics; the result is pushed to every CTA of the cluster
     unsigned long long l_best;
     uint32_t l_n;
     {
-        const unsigned long long v0 = warp_max_u64(t_best), v1 = warp_min_u64(t_first),
-                                 v2 = warp_max_u64(t_dkey), v3 = warp_min_u64(t_min);
-        const uint32_t v4 = warp_sum_u32(t_n);
-        const uint32_t v5 = __reduce_or_sync(0xFFFFFFFFu, t_bad);
         const int w = tid >> 5;
-        if ((tid & 31) == 0) {
-            ls->red[w * 8 + 0] = v0;
-            ls->red[w * 8 + 1] = v1;
-            ls->red[w * 8 + 2] = v2;
-            ls->red[w * 8 + 3] = v3;
-            ls->red[w * 8 + 4] = v4;
-            ls->red[w * 8 + 5] = v5;
+        const uint32_t wmk = __reduce_max_sync(0xFFFFFFFFu, t_mk);
+        const uint32_t wmi = __reduce_min_sync(0xFFFFFFFFu, (t_mk == wmk && wmk != 0u) ? t_mi : 0xFFFFFFFFu);
+        const uint32_t wmn = __reduce_min_sync(0xFFFFFFFFu, t_mn);
+        const uint32_t wam = __reduce_max_sync(0xFFFFFFFFu, t_amax);
+        const uint32_t wcn = __reduce_add_sync(0xFFFFFFFFu, t_cnt);
+        const uint32_t wfi = __reduce_min_sync(0xFFFFFFFFu, t_first);
+        if (lane == 0) {
+            ls->red[w * 8 + 0] = (static_cast<unsigned long long>(wmk) << 32) | wmi;
+            ls->red[w * 8 + 1] = wmn;
+            ls->red[w * 8 + 2] = wam;
+            ls->red[w * 8 + 3] = wcn;
+            ls->red[w * 8 + 4] = wfi;
         }
         __syncthreads();
-        RowStat st;
-        st.best = 0ull;
-        st.first = ~0ull;
-        st.dkey = 0ull;
-        unsigned long long mn = ~0ull;
-        uint32_t n = 0, bad = 0;
+        uint32_t mk = 0u, mi = 0xFFFFFFFFu, mn = 0xFFFFFFFFu, am = 0u, cn = 0u, fi = 0xFFFFFFFFu;
 #pragma unroll
         for (int q = 0; q < kNW; ++q) {
-            st.best = ls->red[q * 8 + 0] > st.best ? ls->red[q * 8 + 0] : st.best;
-            st.first = ls->red[q * 8 + 1] < st.first ? ls->red[q * 8 + 1] : st.first;
-            st.dkey = ls->red[q * 8 + 2] > st.dkey ? ls->red[q * 8 + 2] : st.dkey;
-            mn = ls->red[q * 8 + 3] < mn ? ls->red[q * 8 + 3] : mn;
-            n += static_cast<uint32_t>(ls->red[q * 8 + 4]);
-            bad |= static_cast<uint32_t>(ls->red[q * 8 + 5]);
+            const uint32_t k = static_cast<uint32_t>(ls->red[q * 8 + 0] >> 32);
+            const uint32_t i = static_cast<uint32_t>(ls->red[q * 8 + 0]);
+            if (k > mk || (k == mk && i < mi)) {
+                mk = k;
+                mi = i;
+            }
+            mn = static_cast<uint32_t>(ls->red[q * 8 + 1]) < mn ? static_cast<uint32_t>(ls->red[q * 8 + 1]) : mn;
+            am = static_cast<uint32_t>(ls->red[q * 8 + 2]) > am ? static_cast<uint32_t>(ls->red[q * 8 + 2]) : am;
+            cn += static_cast<uint32_t>(ls->red[q * 8 + 3]);
+            fi = static_cast<uint32_t>(ls->red[q * 8 + 4]) < fi ? static_cast<uint32_t>(ls->red[q * 8 + 4]) : fi;
         }
-        st.min_key = static_cast<uint32_t>(mn);
-        st.n_allowed = n;
-        st.bad = bad | (ls->bc[15] ? 2u : 0u);
-        st.pad = 0;
+        RowStat st;
+        st.best = (mk != 0u) ? comp_of(mk, static_cast<uint32_t>(c0) + mi) : 0ull;
+        st.min_key = mn;
+        st.n_allowed = cn;
+        st.first = fi;
+        st.flags = (am >= 0x7F800000u ? 1u : 0u) | (ls->bc[15] ? 2u : 0u);
+        if (kRaw && fi != 0xFFFFFFFFu && K[fi - static_cast<uint32_t>(c0)] == 0u) st.flags |= 4u;
+        st.dhas = (rc.draft >= c0 && rc.draft < c0 + len) ? 1u : 0u;
+        st.dkey = st.dhas ? K[rc.draft - c0] : 0u;
         l_best = st.best;
-        l_n = n;
-        if (tid < kC) cluster.map_shared_rank(cs, tid)->xs[crank] = st;
-        __syncthreads();
+        l_n = cn;
+        if (tid < static_cast<int>(C)) cluster.map_shared_rank(cs, tid)->xs[crank] = st;
+        __syncthreads();  // also: the history bitmap / mask words (region Y) are dead from here
     }
 
     // list-path local selection (before the first cluster barrier). A row takes the list path
@@ -752,36 +934,29 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
         }
         const uint32_t kl = ksel < l_n ? ksel : l_n;
         if (push && kl > 0) {
-            // histogram of the per-thread maxima over exp-domain bins relative to the local max
+            // Key threshold from the per-thread maxima: the bin (exp domain, relative to the local
+            // max) where their cumulative count reaches kl; every key >= the smallest of those
+            // maxima is a candidate, which is a superset of the local top-kl.
             const float lmax = kval(comp_key(l_best));
             const float bscale = static_cast<float>(
-                (kABins - 1) / (46.0 * 0.6931471805599453 * static_cast<double>(P->temperature)));
+                (kTB - 1) / (46.0 * 0.6931471805599453 * static_cast<double>(P->temperature)));
             auto xbin = [&](uint32_t key) -> int {
                 const float d = (lmax - kval(key)) * bscale;
                 int b = d > 0.0f ? static_cast<int>(d) : 0;
-                return b < kABins - 1 ? b : kABins - 1;
+                return b < kTB - 1 ? b : kTB - 1;
             };
-            unsigned long long tmax = 0ull;
-#pragma unroll
-            for (int q = 0; q < EPT; ++q) {
-                if (keys[q] == 0u) continue;
-                const unsigned long long cp = comp_of(keys[q], static_cast<uint32_t>(c0 + elem_of<SW>(q / SW, q % SW)));
-                tmax = cp > tmax ? cp : tmax;
-            }
-            for (int i = tid; i < kABins; i += kNT) H32[i] = 0u;
+            for (int i = tid; i < kTB; i += kNT) H32[i] = 0u;
             __syncthreads();
-            if (tmax != 0ull) atomicAdd(&H32[xbin(comp_key(tmax))], 1u);
+            if (t_mk != 0u) atomicAdd(&H32[xbin(t_mk)], 1u);
             __syncthreads();
-            // b1 = first bin where the cumulative count of per-thread maxima reaches kl; then at
-            // least kl entries lie in bins <= b1
-            constexpr int PER = kABins / kNT;
+            constexpr int PER = kTB / kNT;
             const int b0 = tid * PER;
             uint32_t s8 = 0;
 #pragma unroll
             for (int q = 0; q < PER; ++q) s8 += H32[b0 + q];
             uint32_t tot = 0;
             const uint32_t ex = block_excl_u32<kNT>(s8, ls->red32, &tot);
-            if (tid == 0) ls->bc[4] = kABins - 1;
+            if (tid == 0) ls->bc[4] = kTB - 1;
             __syncthreads();
             if (ex < kl && ex + s8 >= kl) {
                 uint32_t run = ex;
@@ -795,22 +970,38 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
             }
             __syncthreads();
             const int b1 = static_cast<int>(ls->bc[4]);
-            uint32_t mine = 0;
+            // fewer than kl threads hold a valid entry: every valid entry is a candidate
+            const uint32_t kthr = (tot < kl) ? 1u : static_cast<uint32_t>(
+                block_min_bc((t_mk != 0u && xbin(t_mk) <= b1) ? t_mk : 0xFFFFFFFFull, ls));
+            // collect the superset into LL (unordered)
+            for (int m = 0; m < nq_iter; ++m) {
+                const int q = tid + m * kNT;
+                uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                if (q < nq) v = reinterpret_cast<const uint4*>(K)[q];
+                const uint32_t k4[4] = {v.x, v.y, v.z, v.w};
+                uint32_t c = 0;
 #pragma unroll
-            for (int q = 0; q < EPT; ++q)
-                if (keys[q] != 0u && xbin(keys[q]) <= b1) ++mine;
-            uint32_t ncand = 0;
-            uint32_t off = block_excl_u32<kNT>(mine, ls->red32, &ncand);
-            unsigned long long thr = 0ull;
+                for (int i = 0; i < 4; ++i) c += (k4[i] >= kthr) ? 1u : 0u;
+                if (__ballot_sync(0xFFFFFFFFu, c != 0u) == 0u) continue;
+                uint32_t slot = warp_reserve(c, &ls->lcount);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (k4[i] >= kthr) {
+                        if (slot < static_cast<uint32_t>(kLCap)) LL[slot] = comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i));
+                        ++slot;
+                    }
+                }
+            }
+            __syncthreads();
+            uint32_t ncand = ls->lcount;
             if (ncand > static_cast<uint32_t>(kLCap)) {
-                // too many: exact kl-th largest composite by a radix select over the registers
+                // too many: exact kl-th largest composite by a radix select over the keys
                 uint32_t prefix = 0, pmask = 0, above = 0;
                 for (int shift = 24; shift >= 0; shift -= 8) {
                     for (int i = tid; i < 256; i += kNT) BH[i] = 0u;
                     __syncthreads();
-#pragma unroll
-                    for (int q = 0; q < EPT; ++q) {
-                        const uint32_t k = keys[q];
+                    for (int e = tid; e < len; e += kNT) {
+                        const uint32_t k = K[e];
                         if (k == 0u || (k & pmask) != prefix) continue;
                         atomicAdd(&BH[(k >> shift) & 255u], 1u);
                     }
@@ -837,39 +1028,49 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                 // entries with key == prefix are ties: the (kl - above)-th lowest id closes the set
                 const uint32_t need = kl - above;
                 uint32_t taken = 0;
-                for (int j = 0; j < NV; ++j) {
+                for (int m = 0; m < nq_iter; ++m) {
+                    const int q = tid + m * kNT;
                     uint32_t t = 0;
+                    if (q < nq) {
 #pragma unroll
-                    for (int i = 0; i < SW; ++i) t += (keys[j * SW + i] == prefix) ? 1u : 0u;
+                        for (int i = 0; i < 4; ++i) t += (K[4 * q + i] == prefix) ? 1u : 0u;
+                    }
                     uint32_t tot2 = 0;
                     const uint32_t ex2 = block_excl_u32<kNT>(t, ls->red32, &tot2);
                     uint32_t run = taken + ex2;
+                    if (q < nq) {
 #pragma unroll
-                    for (int i = 0; i < SW; ++i) {
-                        if (keys[j * SW + i] != prefix) continue;
-                        ++run;
-                        if (run == need) ls->bc[7] = comp_of(prefix, static_cast<uint32_t>(c0 + elem_of<SW>(j, i)));
+                        for (int i = 0; i < 4; ++i) {
+                            if (K[4 * q + i] != prefix) continue;
+                            ++run;
+                            if (run == need) ls->bc[7] = comp_of(prefix, static_cast<uint32_t>(c0 + 4 * q + i));
+                        }
                     }
                     taken += tot2;
                 }
                 __syncthreads();
-                thr = ls->bc[7];
-                mine = 0;
+                const unsigned long long thr = ls->bc[7];
+                if (tid == 0) ls->lcount = 0;
+                __syncthreads();
+                for (int m = 0; m < nq_iter; ++m) {
+                    const int q = tid + m * kNT;
+                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                    if (q < nq) v = reinterpret_cast<const uint4*>(K)[q];
+                    const uint32_t k4[4] = {v.x, v.y, v.z, v.w};
+                    uint32_t c = 0;
 #pragma unroll
-                for (int q = 0; q < EPT; ++q) {
-                    if (keys[q] == 0u) continue;
-                    if (comp_of(keys[q], static_cast<uint32_t>(c0 + elem_of<SW>(q / SW, q % SW))) >= thr) ++mine;
+                    for (int i = 0; i < 4; ++i)
+                        c += (k4[i] != 0u && comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i)) >= thr) ? 1u : 0u;
+                    uint32_t slot = warp_reserve(c, &ls->lcount);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const unsigned long long cp = comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i));
+                        if (k4[i] != 0u && cp >= thr) LL[slot++] = cp;
+                    }
                 }
-                off = block_excl_u32<kNT>(mine, ls->red32, &ncand);
+                __syncthreads();
+                ncand = ls->lcount;
             }
-#pragma unroll
-            for (int q = 0; q < EPT; ++q) {
-                if (keys[q] == 0u) continue;
-                const unsigned long long cp = comp_of(keys[q], static_cast<uint32_t>(c0 + elem_of<SW>(q / SW, q % SW)));
-                const bool take = thr ? (cp >= thr) : (xbin(keys[q]) <= b1);
-                if (take) LL[off++] = cp;
-            }
-            __syncthreads();
             // rank sort; the best kl go to CTA 0's merge area at their rank
             unsigned long long* ma0 = cluster.map_shared_rank(MA, 0);
             for (uint32_t i = tid; i < ncand; i += kNT) {
@@ -886,17 +1087,23 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
     cluster.sync();  // ======================================================== CS1
 
     // ======================================================================== phase B
-    unsigned long long best = 0ull, first = ~0ull, dkey = 0ull;
+    unsigned long long best = 0ull;
+    uint32_t first = 0xFFFFFFFFu, first_nan = 0u, dkey = 0u, dhas = 0u;
     uint32_t min_key = 0xFFFFFFFFu, n_allowed = 0, bad = 0;
-#pragma unroll
-    for (int q = 0; q < kC; ++q) {
+    for (uint32_t q = 0; q < C; ++q) {
         const RowStat& s = cs->xs[q];
         best = s.best > best ? s.best : best;
-        first = s.first < first ? s.first : first;
-        dkey = s.dkey > dkey ? s.dkey : dkey;
+        if (s.first < first) {
+            first = s.first;
+            first_nan = (s.flags >> 2) & 1u;
+        }
+        if (s.dhas) {
+            dhas = 1u;
+            dkey = s.dkey;
+        }
         min_key = s.min_key < min_key ? s.min_key : min_key;
         n_allowed += s.n_allowed;
-        bad |= s.bad;
+        bad |= s.flags & 3u;
     }
     const bool raw_argmax = (MODE == kModeGreedy) || (MODE == kModeVerify && rc.greedy);
     int32_t status = SIXI_OK;
@@ -919,8 +1126,7 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
     int32_t res_token = -1;
     int32_t res_accept = 0;
     if (rc.active && status == SIXI_OK && rc.greedy) {
-        const bool first_nan = (first != ~0ull) && (first & 1ull);
-        res_token = (raw_argmax && (first_nan || best == 0ull)) ? static_cast<int32_t>(first >> 1)
+        res_token = (raw_argmax && (first_nan || best == 0ull)) ? static_cast<int32_t>(first)
                                                               : static_cast<int32_t>(comp_id(best));
         if (raw_argmax && (bad & 1u)) res_status = SIXI_NUMERIC_NAN_OR_INF;
     }
@@ -928,9 +1134,9 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
     const double invT = 1.0 / static_cast<double>(P->temperature);
     const float M = kval(comp_key(best));
     const double maxs = static_cast<double>(M) * invT;
-    const bool dvalid = (dkey >> 32) != 0ull && static_cast<uint32_t>(dkey) != 0u;
-    const float xd = dvalid ? kval(static_cast<uint32_t>(dkey)) : 0.0f;
-    const unsigned long long dcomp = dvalid ? comp_of(static_cast<uint32_t>(dkey), static_cast<uint32_t>(rc.draft)) : 0ull;
+    const bool dvalid = dhas != 0u && dkey != 0u;
+    const float xd = dvalid ? kval(dkey) : 0.0f;
+    const unsigned long long dcomp = dvalid ? comp_of(dkey, static_cast<uint32_t>(rc.draft)) : 0ull;
 
     // merge of the pushed lists at CTA 0 into FL (sorted). Used by the list path and by the
     // candidates entry on the mass path.
@@ -939,8 +1145,7 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
     if (want_lists) {
         uint32_t total = 0;
         bool ok = true;
-#pragma unroll
-        for (int q = 0; q < kC; ++q) {
+        for (uint32_t q = 0; q < C; ++q) {
             if (cs->lcnt[q] == kNoList) ok = false;
             else total += cs->lcnt[q];
         }
@@ -951,90 +1156,102 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
             path = (path == 1) ? 0 : path;
             fl_n = 0;
         }
-        for (int q = 0; q < kC && fl_n > 0; ++q) {
-            const uint32_t nq = cs->lcnt[q];
-            for (uint32_t pidx = tid; pidx < nq; pidx += kNT) {
-                const unsigned long long v = MA[q * kKS + pidx];
-                uint32_t rank = pidx;
-#pragma unroll
-                for (int o = 0; o < kC; ++o) {
-                    if (o == q) continue;
-                    uint32_t lo = 0, hi = cs->lcnt[o];
-                    const unsigned long long* lp = MA + o * kKS;
-                    while (lo < hi) {
-                        const uint32_t mid = (lo + hi) >> 1;
-                        if (lp[mid] > v) lo = mid + 1;
-                        else hi = mid;
-                    }
-                    rank += lo;
+        // merge: rank of every pushed entry = its position + entries greater in the other lists
+        for (uint32_t x = tid; fl_n > 0 && x < C * kKS; x += kNT) {
+            const uint32_t q = x / kKS, pidx = x % kKS;
+            if (pidx >= cs->lcnt[q]) continue;
+            const unsigned long long v = MA[q * kKS + pidx];
+            uint32_t rank = pidx;
+            for (uint32_t o = 0; o < C; ++o) {
+                if (o == q) continue;
+                uint32_t lo = 0, hi = cs->lcnt[o];
+                const unsigned long long* lp = MA + o * kKS;
+                while (lo < hi) {
+                    const uint32_t mid = (lo + hi) >> 1;
+                    if (lp[mid] > v) lo = mid + 1;
+                    else hi = mid;
                 }
-                if (rank < fl_n) FL[rank] = v;
+                rank += lo;
             }
+            if (rank < fl_n) FL[rank] = v;
         }
         __syncthreads();
     }
-    // CTA-uniform for CTA 0 only; other CTAs skip the list path entirely
+    // list path: CTA 0 (softmax terms by all threads, then warp 0 with 8 candidates per lane,
+    // candidate order = lane-major); the other CTAs of such rows are finished
     if (crank == 0 && path == 1) {
-        // fp64 softmax over the k candidates (core_execution.cpp:538-549)
         const uint32_t n = fl_n;
-        const bool act = static_cast<uint32_t>(tid) < n;
-        double e = 0.0;
-        if (act) e = exp(static_cast<double>(kval(comp_key(FL[tid]))) * invT - maxs);
-        const double sum_exp = block_sum_f64(e, ls);
-        double prob = (sum_exp > 0.0) ? e / sum_exp : e;
-        // top-p: keep through the first index with cumulative >= top_p (core_execution.cpp:551-575)
-        uint32_t keep = n;
-        double tot = 0.0;
-        if (P->top_p > 0.0f && P->top_p < 1.0f) {
-            const double cum = block_incl_f64(act ? prob : 0.0, ls, &tot);
-            const bool hit = act && cum >= static_cast<double>(P->top_p);
-            const unsigned long long first_hit = block_min_bc(hit ? static_cast<unsigned long long>(tid) : ~0ull, ls);
-            keep = (first_hit == ~0ull) ? n : static_cast<uint32_t>(first_hit) + 1u;
-            if (keep < n) {
-                const double renorm = block_sum_f64(static_cast<uint32_t>(tid) < keep ? prob : 0.0, ls);
-                if (renorm > 0.0) prob = prob / renorm;
-            }
-        }
-        // min-p extension: keep prob >= min_p * max prob, renormalise
-        if (P->min_p > 0.0f) {
-            if (tid == 0) ls->bcd[0] = prob;
-            __syncthreads();
-            const double thr = static_cast<double>(P->min_p) * ls->bcd[0];
-            __syncthreads();
-            const bool drop = static_cast<uint32_t>(tid) < keep && prob < thr;
-            const unsigned long long fd = block_min_bc(drop ? static_cast<unsigned long long>(tid) : ~0ull, ls);
-            if (fd != ~0ull && fd >= 1ull && static_cast<uint32_t>(fd) < keep) {
-                keep = static_cast<uint32_t>(fd);
-                const double renorm = block_sum_f64(static_cast<uint32_t>(tid) < keep ? prob : 0.0, ls);
-                if (renorm > 0.0) prob = prob / renorm;
-            }
-        }
-        if (tid < kKS) FP[tid] = static_cast<uint32_t>(tid) < keep ? prob : 0.0;
+        // fp64 softmax terms over the k candidates (core_execution.cpp:538-549)
+        if (static_cast<uint32_t>(tid) < n) FP[tid] = exp(static_cast<double>(kval(comp_key(FL[tid]))) * invT - maxs);
         __syncthreads();
-        // CDF draw in candidate order over FL/`pr` (core_execution.cpp:586-601)
-        auto draw_list = [&](double u, const double* pr, const unsigned long long* ids, uint32_t nk) -> int32_t {
-            double t2 = 0.0;
-            const double v = static_cast<uint32_t>(tid) < nk ? pr[tid] : 0.0;
-            const double cdf = block_incl_f64(v, ls, &t2);
-            const bool hit = static_cast<uint32_t>(tid) < nk && u < cdf;
-            const unsigned long long j = block_min_bc(hit ? static_cast<unsigned long long>(tid) : ~0ull, ls);
-            const uint32_t jj = (j == ~0ull) ? nk - 1u : static_cast<uint32_t>(j);
-            return static_cast<int32_t>(comp_id(ids[jj]));
-        };
-        if (MODE == kModeSample || (MODE == kModeVerify && rc.vrole == 1)) {
-            res_token = draw_list(rc.u_draw, FP, FL, keep);
-        } else if (MODE == kModeCandidates) {
-            if (static_cast<uint32_t>(tid) < keep && static_cast<uint32_t>(tid) < a.max_out) {
-                a.out_ids[static_cast<size_t>(row) * a.max_out + tid] = static_cast<int32_t>(comp_id(FL[tid]));
-                a.out_probs[static_cast<size_t>(row) * a.max_out + tid] = FP[tid];
+    }
+    if (crank == 0 && path == 1 && tid < 32) {
+        const uint32_t n = fl_n;
+        double pr[kPL];
+        double lsum = 0.0;
+#pragma unroll
+        for (int j = 0; j < kPL; ++j) {
+            const uint32_t idx = lane * kPL + j;
+            pr[j] = idx < n ? FP[idx] : 0.0;
+            lsum += pr[j];
+        }
+        const double sum_exp = warp_sum_f64(lsum);
+        if (sum_exp > 0.0) {
+#pragma unroll
+            for (int j = 0; j < kPL; ++j) pr[j] /= sum_exp;
+        }
+        uint32_t keep = n;
+        if (P->top_p > 0.0f && P->top_p < 1.0f) {
+            // top-p: keep through the first index with cumulative >= top_p (core_execution.cpp:551-575)
+            const uint32_t f = lane_first_cum_ge(pr, static_cast<double>(P->top_p), n, lane);
+            keep = (f == 0xFFFFFFFFu) ? n : f + 1u;
+            if (keep < n) lane_renorm(pr, keep, lane);
+        }
+        if (P->min_p > 0.0f) {
+            // min-p extension: keep prob >= min_p * max prob, renormalise
+            const double thr = static_cast<double>(P->min_p) * __shfl_sync(0xFFFFFFFFu, pr[0], 0);
+            uint32_t mine = 0xFFFFFFFFu;
+#pragma unroll
+            for (int j = kPL - 1; j >= 0; --j) {
+                const uint32_t idx = lane * kPL + j;
+                if (idx >= 1 && idx < keep && pr[j] < thr) mine = idx;
             }
-            if (tid == 0) a.out_count[row] = static_cast<int32_t>(keep);
+            const uint32_t f = __reduce_min_sync(0xFFFFFFFFu, mine);
+            if (f != 0xFFFFFFFFu && f < keep) {
+                keep = f;
+                lane_renorm(pr, keep, lane);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kPL; ++j) {
+            if (lane * kPL + j >= keep) pr[j] = 0.0;
+            FP[lane * kPL + j] = pr[j];
+        }
+        __syncwarp();
+        if (MODE == kModeSample || (MODE == kModeVerify && rc.vrole == 1)) {
+            // CDF draw in candidate order (core_execution.cpp:586-601)
+            const uint32_t f = lane_first_cum_gt(pr, rc.u_draw, keep, lane);
+            res_token = static_cast<int32_t>(comp_id(FL[f == 0xFFFFFFFFu ? keep - 1u : f]));
+        } else if (MODE == kModeCandidates) {
+#pragma unroll
+            for (int j = 0; j < kPL; ++j) {
+                const uint32_t idx = lane * kPL + j;
+                if (idx < keep && idx < a.max_out) {
+                    a.out_ids[static_cast<size_t>(row) * a.max_out + idx] = static_cast<int32_t>(comp_id(FL[idx]));
+                    a.out_probs[static_cast<size_t>(row) * a.max_out + idx] = pr[j];
+                }
+            }
+            if (lane == 0) a.out_count[row] = static_cast<int32_t>(keep);
         } else if (MODE == kModeVerify) {
             const int32_t d = rc.draft;
-            const bool kact = static_cast<uint32_t>(tid) < keep;
-            const bool isd = kact && static_cast<int32_t>(comp_id(FL[tid])) == d;
-            const unsigned long long dpos = block_min_bc(isd ? static_cast<unsigned long long>(tid) : ~0ull, ls);
-            const double pd = (dpos == ~0ull) ? 0.0 : FP[dpos];
+            uint32_t mine = 0xFFFFFFFFu;
+#pragma unroll
+            for (int j = kPL - 1; j >= 0; --j) {
+                const uint32_t idx = lane * kPL + j;
+                if (idx < keep && static_cast<int32_t>(comp_id(FL[idx])) == d) mine = idx;
+            }
+            const uint32_t dpos = __reduce_min_sync(0xFFFFFFFFu, mine);
+            const double pd = (dpos == 0xFFFFFFFFu) ? 0.0 : FP[dpos];
             const bool in_range = d >= 0 && static_cast<uint32_t>(d) < a.vocab;
             if (a.q != nullptr) {
                 // dense draft probabilities (speculative.cpp:823-903)
@@ -1045,48 +1262,62 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                     : fmin(1.0, static_cast<double>(p_d) / fmax(1e-12, static_cast<double>(q_d)));
                 res_accept = rc.u_accept < accept_prob ? 1 : 0;
                 if (!res_accept) {
-                    // residual max(0, p - q) is non-zero only on the kept candidates; walk them in
-                    // vocabulary-id order
-                    const uint32_t myid = kact ? comp_id(FL[tid]) : 0xFFFFFFFFu;
-                    const float pf = kact ? static_cast<float>(FP[tid]) : 0.0f;
-                    const double res = kact ? fmax(0.0, static_cast<double>(pf) - static_cast<double>(qrow[myid])) : 0.0;
-                    uint32_t idr = 0;
-                    if (kact) {
-                        for (uint32_t j = 0; j < keep; ++j) idr += (comp_id(FL[j]) < myid) ? 1u : 0u;
+                    // residual max(0, p - q) is non-zero only on the kept candidates: walk them in
+                    // vocabulary-id order (rank of each id among the kept ids)
+                    double res[kPL];
+                    double rs = 0.0;
+#pragma unroll
+                    for (int j = 0; j < kPL; ++j) {
+                        const uint32_t idx = lane * kPL + j;
+                        res[j] = 0.0;
+                        if (idx < keep) {
+                            const uint32_t id = comp_id(FL[idx]);
+                            res[j] = fmax(0.0, static_cast<double>(static_cast<float>(pr[j])) - static_cast<double>(qrow[id]));
+                        }
+                        rs += res[j];
                     }
-                    const double res_sum = block_sum_f64(res, ls);
-                    if (kact) {
-                        FQ[idr] = (res_sum > 1e-12) ? res / res_sum : static_cast<double>(pf);
-                        BH[idr] = myid;
+                    const double res_sum = warp_sum_f64(rs);
+#pragma unroll
+                    for (int j = 0; j < kPL; ++j) {
+                        const uint32_t idx = lane * kPL + j;
+                        if (idx < keep) {
+                            const uint32_t id = comp_id(FL[idx]);
+                            uint32_t r = 0;
+                            for (uint32_t o = 0; o < keep; ++o) r += comp_id(FL[o]) < id ? 1u : 0u;
+                            FQ[r] = res_sum > 1e-12 ? res[j] / res_sum : static_cast<double>(static_cast<float>(pr[j]));
+                            BH[r] = id;
+                        }
                     }
-                    __syncthreads();
-                    double t3 = 0.0;
-                    const double v = kact ? FQ[tid] : 0.0;
-                    const double cdf = block_incl_f64(v, ls, &t3);
-                    const bool hit = kact && rc.u_draw < cdf;
-                    const unsigned long long j = block_min_bc(hit ? static_cast<unsigned long long>(tid) : ~0ull, ls);
-                    res_token = (j == ~0ull) ? static_cast<int32_t>(a.vocab - 1) : static_cast<int32_t>(BH[j]);
+                    __syncwarp();
+                    double v[kPL];
+#pragma unroll
+                    for (int j = 0; j < kPL; ++j) v[j] = (lane * kPL + j < keep) ? FQ[lane * kPL + j] : 0.0;
+                    const uint32_t f = lane_first_cum_gt(v, rc.u_draw, keep, lane);
+                    res_token = (f == 0xFFFFFFFFu) ? static_cast<int32_t>(a.vocab - 1) : static_cast<int32_t>(BH[f]);
                 }
             } else {
-                // one-hot drafts (speculative.cpp:638-681)
+                // one-hot drafts (speculative.cpp:638-681): residual = the kept candidates without
+                // the draft, renormalised, drawn in candidate order
                 res_accept = rc.u_accept < pd ? 1 : 0;
                 if (!res_accept) {
-                    const bool has_d = dpos != ~0ull;
-                    const double res_sum = block_sum_f64((kact && !isd) ? FP[tid] : 0.0, ls);
-                    const uint32_t m = keep - (has_d ? 1u : 0u);
+                    double v[kPL];
+                    double rs = 0.0;
+#pragma unroll
+                    for (int j = 0; j < kPL; ++j) {
+                        v[j] = (lane * kPL + j == dpos) ? 0.0 : pr[j];
+                        rs += v[j];
+                    }
+                    const double res_sum = warp_sum_f64(rs);
+                    const uint32_t m = keep - (dpos != 0xFFFFFFFFu ? 1u : 0u);
                     if (m > 0 && res_sum > 0.0) {
-                        const uint32_t pos = static_cast<uint32_t>(tid) - ((has_d && static_cast<unsigned long long>(tid) > dpos) ? 1u : 0u);
-                        const double pv = (kact && !isd) ? FP[tid] / res_sum : 0.0;
-                        const unsigned long long fv = (kact && !isd) ? FL[tid] : 0ull;
-                        __syncthreads();
-                        if (kact && !isd) {
-                            FQ[pos] = pv;
-                            LL[pos] = fv;
-                        }
-                        __syncthreads();
-                        res_token = draw_list(rc.u_draw, FQ, LL, m);
+#pragma unroll
+                        for (int j = 0; j < kPL; ++j) v[j] /= res_sum;
+                        const uint32_t last = (dpos == keep - 1u) ? keep - 2u : keep - 1u;
+                        const uint32_t f = lane_first_cum_gt(v, rc.u_draw, keep, lane);
+                        res_token = static_cast<int32_t>(comp_id(FL[f == 0xFFFFFFFFu ? last : f]));
                     } else {
-                        res_token = draw_list(rc.u_draw, FP, FL, keep);
+                        const uint32_t f = lane_first_cum_gt(pr, rc.u_draw, keep, lane);
+                        res_token = static_cast<int32_t>(comp_id(FL[f == 0xFFFFFFFFu ? keep - 1u : f]));
                     }
                 }
             }
@@ -1133,6 +1364,11 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
     unsigned long long Z = 0ull, Wmin = 0ull;
     float x_minp = -FLT_MAX;
     const bool need_counts = k_eff < n_allowed;
+    auto xbin_g = [&](uint32_t key) -> int {
+        const float dd = (M - kval(key)) * wc.bin_scale;
+        int b = dd > 0.0f ? static_cast<int>(dd) : 0;
+        return b < kABins - 1 ? b : kABins - 1;
+    };
     {
         const float m = kval(min_key);
         double range = static_cast<double>(M) - static_cast<double>(m);
@@ -1150,25 +1386,32 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
         }
         __syncthreads();
         unsigned long long zp = 0ull, wp = 0ull;
+        for (int m = 0; m < nq_iter; ++m) {  // 4 keys per iteration: independent chains
+            const int q = tid + m * kNT;
+            if (q >= nq) break;
+            const uint4 v = reinterpret_cast<const uint4*>(K)[q];
+            const uint32_t k4[4] = {v.x, v.y, v.z, v.w};
+            unsigned long long w4[4];
+            int b4[4];
 #pragma unroll
-        for (int q = 0; q < EPT; ++q) {
-            const uint32_t k = keys[q];
-            if (k == 0u) continue;
-            const float x = kval(k);
-            const unsigned long long w = weight_of(x, wc);
-            zp += w;
-            if (x >= x_minp) wp += w;
-            if (w || need_counts) {
-                const float dd = (M - x) * wc.bin_scale;
-                int b = dd > 0.0f ? static_cast<int>(dd) : 0;
-                b = b < kABins - 1 ? b : kABins - 1;
-                if (w) atomicAdd(&H[b], w);
-                if (need_counts) atomicAdd(&HC[b], 1u);
+            for (int i = 0; i < 4; ++i) {  // branch-free part: weights, bins, sums
+                const uint32_t k = k4[i];
+                const float x = kval(k);
+                const unsigned long long w = (k != 0u) ? weight_of(x, wc) : 0ull;
+                w4[i] = w;
+                b4[i] = xbin_g(k);
+                zp += w;
+                wp += (x >= x_minp) ? w : 0ull;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (w4[i]) atomicAdd(&H[b4[i]], w4[i]);
+                if (need_counts && k4[i] != 0u) atomicAdd(&HC[b4[i]], 1u);
             }
         }
         zp = block_sum_u64<kNT>(zp, ls->red);
         wp = block_sum_u64<kNT>(wp, ls->red);
-        if (tid < kC) {
+        if (tid < static_cast<int>(C)) {
             ClusterShared* dst = cluster.map_shared_rank(cs, tid);
             dst->z[crank] = zp;
             dst->wmin[crank] = wp;
@@ -1178,32 +1421,41 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
     cluster.sync();  // ======================================================== CS2
 
     // reduce histogram segment `crank` over all CTAs of the cluster
-    for (int i = tid; i < kSeg; i += kNT) {
+    for (uint32_t i = tid; i < lay.seg; i += kNT) {
         unsigned long long s = 0ull;
         uint32_t sc = 0;
-#pragma unroll
-        for (int q = 0; q < kC; ++q) {
-            s += cluster.map_shared_rank(H, q)[crank * kSeg + i];
-            if (need_counts) sc += cluster.map_shared_rank(HC, q)[crank * kSeg + i];
+        for (uint32_t q = 0; q < C; ++q) {
+            s += cluster.map_shared_rank(H, q)[crank * lay.seg + i];
+            if (need_counts) sc += cluster.map_shared_rank(HC, q)[crank * lay.seg + i];
         }
         R[i] = s;
         RC[i] = sc;
     }
-#pragma unroll
-    for (int q = 0; q < kC; ++q) {
+    for (uint32_t q = 0; q < C; ++q) {
         Z += cs->z[q];
         Wmin += cs->wmin[q];
     }
 
     cluster.sync();  // ======================================================== CS3
 
-    auto xbin_g = [&](uint32_t key) -> int {
-        const float dd = (M - kval(key)) * wc.bin_scale;
-        int b = dd > 0.0f ? static_cast<int>(dd) : 0;
-        return b < kABins - 1 ? b : kABins - 1;
-    };
-    auto comp_at = [&](int q) -> unsigned long long {
-        return comp_of(keys[q], static_cast<uint32_t>(c0 + elem_of<SW>(q / SW, q % SW)));
+    // keys of bin b form the interval [lo, hi] (the bin index is non-increasing in the key);
+    // found by binary search over the valid keys [min_key, max key]
+    const uint32_t kmax_valid = comp_key(best);
+    auto bin_key_range = [&](int b, uint32_t* lo_out, uint32_t* hi_out) {
+        uint32_t lo = min_key, hi = kmax_valid;  // smallest key with bin <= b
+        while (lo < hi) {
+            const uint32_t mid = lo + ((hi - lo) >> 1);
+            if (xbin_g(mid) <= b) hi = mid;
+            else lo = mid + 1;
+        }
+        *lo_out = lo;
+        uint32_t lo2 = min_key, hi2 = kmax_valid;  // largest key with bin >= b
+        while (lo2 < hi2) {
+            const uint32_t mid = lo2 + ((hi2 - lo2 + 1) >> 1);
+            if (xbin_g(mid) >= b) lo2 = mid;
+            else hi2 = mid - 1;
+        }
+        *hi_out = lo2;
     };
     auto bin_of_target = [&](unsigned long long t) -> int {  // first bin with CG >= t
         int lo = 0, hi = kABins - 1;
@@ -1217,33 +1469,38 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
     // push my entries of bin b (composite >= lowb) into gather buffer gbuf of every CTA
     auto gather = [&](int b, int gbuf, unsigned long long lowb) {
         unsigned long long* gb = gbuf ? G1 : G0;
-        const int lane = tid & 31;
+        uint32_t klo, khi;
+        bin_key_range(b, &klo, &khi);
+        for (int m = 0; m < nq_iter; ++m) {  // warp-uniform trip count
+            const int q = tid + m * kNT;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (q < nq) v = reinterpret_cast<const uint4*>(K)[q];
+            const uint32_t k4[4] = {v.x, v.y, v.z, v.w};
+            uint32_t c = 0;
 #pragma unroll
-        for (int q = 0; q < EPT; ++q) {
-            const uint32_t k = keys[q];
-            const unsigned long long cp = comp_at(q);
-            const bool mine = k != 0u && xbin_g(k) == b && cp >= lowb;
-            const unsigned ball = __ballot_sync(0xFFFFFFFFu, mine);
-            if (ball == 0u) continue;
-            const int leader = __ffs(ball) - 1;
-            const uint32_t cnt = __popc(ball);
-            const uint32_t rk = __popc(ball & ((1u << lane) - 1u));
-#pragma unroll 1
-            for (int dst = 0; dst < kC; ++dst) {
+            for (int i = 0; i < 4; ++i)
+                c += (k4[i] >= klo && k4[i] <= khi && comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i)) >= lowb) ? 1u : 0u;
+            if (__ballot_sync(0xFFFFFFFFu, c != 0u) == 0u) continue;
+            const uint32_t incl = warp_incl_u32(c);
+            const uint32_t total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+            for (uint32_t dst = 0; dst < C; ++dst) {
                 uint32_t basei = 0;
-                if (lane == leader) basei = atomicAdd(&cluster.map_shared_rank(cs, dst)->gcnt[gbuf], cnt);
-                basei = __shfl_sync(0xFFFFFFFFu, basei, leader);
-                if (mine && basei + rk < static_cast<uint32_t>(kGCap)) cluster.map_shared_rank(gb, dst)[basei + rk] = cp;
+                if (lane == 31) basei = atomicAdd(&cluster.map_shared_rank(cs, dst)->gcnt[gbuf], total);
+                basei = __shfl_sync(0xFFFFFFFFu, basei, 31) + incl - c;
+                unsigned long long* rg = cluster.map_shared_rank(gb, dst);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const unsigned long long cp = comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i));
+                    if (k4[i] >= klo && k4[i] <= khi && cp >= lowb) {
+                        if (basei < static_cast<uint32_t>(kGCap)) rg[basei] = cp;
+                        ++basei;
+                    }
+                }
             }
         }
     };
 
-    // every CTA assembles the same global cumulative histograms
-    for (int i = tid; i < kABins; i += kNT) {
-        CG[i] = cluster.map_shared_rank(R, i / kSeg)[i % kSeg];
-        CGC[i] = need_counts ? cluster.map_shared_rank(RC, i / kSeg)[i % kSeg] : 0u;
-    }
-    __syncthreads();
+    // every CTA assembles the same global cumulative histograms (CG/CGC overwrite H/HC)
     {
         constexpr int PER = kABins / kNT;
         unsigned long long v[PER];
@@ -1252,14 +1509,15 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
         uint32_t sc = 0;
 #pragma unroll
         for (int q = 0; q < PER; ++q) {
-            v[q] = CG[tid * PER + q];
-            vc[q] = CGC[tid * PER + q];
+            const uint32_t i = tid * PER + q;
+            v[q] = cluster.map_shared_rank(R, i / lay.seg)[i % lay.seg];
+            vc[q] = need_counts ? cluster.map_shared_rank(RC, i / lay.seg)[i % lay.seg] : 0u;
             s += v[q];
             sc += vc[q];
         }
         const unsigned long long inc = warp_incl_u64(s);
         const uint32_t incc = warp_incl_u32(sc);
-        if ((tid & 31) == 31) {
+        if (lane == 31) {
             ls->red[tid >> 5] = inc;
             ls->red[kNW + (tid >> 5)] = incc;
         }
@@ -1297,16 +1555,14 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
     st.excl = 0ull;
     st.wexcl = 0ull;
     Refine rf{};
-    uint32_t* RH[2] = {reinterpret_cast<uint32_t*>(dyn + lay.off_h),
-                       reinterpret_cast<uint32_t*>(dyn + lay.off_h) + 256};
-    unsigned long long* RW[2] = {reinterpret_cast<unsigned long long*>(dyn + lay.off_h + 2048u),
-                                 reinterpret_cast<unsigned long long*>(dyn + lay.off_h + 2048u) + 256};
+    // refine digit histograms (double-buffered) in region R: the reduced segments there are last
+    // read remotely in the assembly above, at least one barrier before the first refine level
+    uint32_t* RH[2] = {reinterpret_cast<uint32_t*>(R), reinterpret_cast<uint32_t*>(R) + 256};
+    unsigned long long* RW[2] = {R + 256, R + 512};
 
-    // entries of the selection `rf` describes (bin, lower bound, exclusion, key prefix)
-    auto rf_match = [&](int q) -> bool {
-        const uint32_t k = keys[q];
-        if (k == 0u || (k & rf.pmask) != rf.prefix || xbin_g(k) != rf.bin) return false;
-        const unsigned long long cp = comp_at(q);
+    auto rf_match = [&](int e, uint32_t k) -> bool {
+        if (k < rf.klo || k > rf.khi || (k & rf.pmask) != rf.prefix) return false;
+        const unsigned long long cp = comp_of(k, static_cast<uint32_t>(c0 + e));
         return cp >= rf.lowb && cp != rf.excl;
     };
     auto rf_build = [&](int buf) {  // local digit histogram of the refine level
@@ -1315,12 +1571,12 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
             RW[buf][i] = 0ull;
         }
         __syncthreads();
-#pragma unroll
-        for (int q = 0; q < EPT; ++q) {
-            if (!rf_match(q)) continue;
-            const uint32_t d = (keys[q] >> rf.shift) & ((1u << rf.width) - 1u);
+        for (int e = tid; e < len; e += kNT) {
+            const uint32_t k = K[e];
+            if (!rf_match(e, k)) continue;
+            const uint32_t d = (k >> rf.shift) & ((1u << rf.width) - 1u);
             atomicAdd(&RH[buf][d], 1u);
-            atomicAdd(&RW[buf][d], static_cast<unsigned long long>(weight_of(kval(keys[q]), wc)));
+            atomicAdd(&RW[buf][d], static_cast<unsigned long long>(weight_of(kval(k), wc)));
         }
         __syncthreads();
     };
@@ -1330,9 +1586,6 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
         rf.width = top - rf.shift + 1;
     };
 
-    const double zero_d = 0.0;
-    (void)zero_d;
-
 #pragma unroll 1
     for (int round = 0; round < kMaxRounds; ++round) {
         if (st.stage == kStDone || st.err) break;
@@ -1340,7 +1593,7 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
         const int prev = cur ^ 1;
         bool have_sel = false;
         unsigned long long sel = 0ull, cum_sel = 0ull, wthrough = 0ull;
-        int sel_bin = st.pending_bin;
+        const int sel_bin = st.pending_bin;
         // ------------------------------------------------ resolve what the previous round started
         if (st.pending_kind == 1) {
             const uint32_t n = cs->gcnt[prev];
@@ -1361,16 +1614,17 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                 rf.above_c = 0ull;
                 rf.above_w = 0ull;
                 rf.buf = 0;
+                bin_key_range(rf.bin, &rf.klo, &rf.khi);
                 uint32_t lo = 0xFFFFFFFFu, hi = 0u;
-#pragma unroll
-                for (int q = 0; q < EPT; ++q) {
-                    if (!rf_match(q)) continue;
-                    lo = keys[q] < lo ? keys[q] : lo;
-                    hi = keys[q] > hi ? keys[q] : hi;
+                for (int e = tid; e < len; e += kNT) {
+                    const uint32_t k = K[e];
+                    if (!rf_match(e, k)) continue;
+                    lo = k < lo ? k : lo;
+                    hi = k > hi ? k : hi;
                 }
                 const unsigned long long l2 = block_min_u64<kNT>(lo, ls->red);
                 const unsigned long long h2 = block_max_u64<kNT>(hi, ls->red);
-                if (tid < kC) cluster.map_shared_rank(cs, tid)->mm[crank] = (l2 << 32) | h2;
+                if (tid < static_cast<int>(C)) cluster.map_shared_rank(cs, tid)->mm[crank] = (l2 << 32) | h2;
                 st.pending_kind = 3;
             } else {
                 const unsigned long long* gp = prev ? G1 : G0;
@@ -1395,8 +1649,7 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
         } else if (st.pending_kind == 3) {
             if (rf.phase == 0) {
                 uint32_t klo = 0xFFFFFFFFu, khi = 0u;
-#pragma unroll
-                for (int q = 0; q < kC; ++q) {
+                for (uint32_t q = 0; q < C; ++q) {
                     const unsigned long long v = cs->mm[q];
                     const uint32_t l = static_cast<uint32_t>(v >> 32), h = static_cast<uint32_t>(v);
                     klo = l < klo ? l : klo;
@@ -1417,15 +1670,15 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                 }
             } else if (rf.phase == 1) {
                 // combine the digit histograms of all CTAs, choose the digit of the crossing
-                const int d = tid;  // kNT == 256 digits
-                unsigned long long sc = 0ull, sw = 0ull;
-#pragma unroll
-                for (int q = 0; q < kC; ++q) {
-                    sc += cluster.map_shared_rank(RH[rf.buf], q)[d];
-                    sw += cluster.map_shared_rank(RW[rf.buf], q)[d];
+                if (tid < 256) {
+                    unsigned long long sc = 0ull, sw = 0ull;
+                    for (uint32_t q = 0; q < C; ++q) {
+                        sc += cluster.map_shared_rank(RH[rf.buf], q)[tid];
+                        sw += cluster.map_shared_rank(RW[rf.buf], q)[tid];
+                    }
+                    BH[tid] = static_cast<uint32_t>(sc);
+                    BW[tid] = sw;
                 }
-                BH[d] = static_cast<uint32_t>(sc);
-                BW[d] = sw;
                 __syncthreads();
                 if (tid < 32) {
                     const unsigned int nd = 1u << rf.width;
@@ -1501,10 +1754,10 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                     const unsigned long long idx = (rf.t - done_sel + w - 1ull) / w - 1ull;
                     unsigned long long before = 0ull;
                     int owner = -1;
-                    for (int q = 0; q < kC; ++q) {
+                    for (uint32_t q = 0; q < C; ++q) {
                         const unsigned long long c = cs->rcnt[q];
-                        if (owner < 0 && idx < before + c) {
-                            owner = q;
+                        if (idx < before + c) {
+                            owner = static_cast<int>(q);
                             break;
                         }
                         before += c;
@@ -1512,30 +1765,35 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                     if (owner < 0) {
                         st.err = 9;
                     } else {
-                        rf.above_c += idx;  // count before the crossing tie (excl.)
+                        rf.above_c += idx;  // entries before the crossing tie
                         rf.above_w += idx * w;
                         rf.tie_w = w;
                         if (owner == static_cast<int>(crank)) {
                             const unsigned long long li = idx - before;
                             unsigned long long taken = 0ull;
                             if (tid == 0) ls->bc[13] = 0ull;
-                            for (int j = 0; j < NV; ++j) {
+                            for (int m = 0; m < nq_iter; ++m) {
+                                const int q = tid + m * kNT;
                                 uint32_t t = 0;
+                                if (q < nq) {
 #pragma unroll
-                                for (int i = 0; i < SW; ++i) t += rf_match(j * SW + i) ? 1u : 0u;
+                                    for (int i = 0; i < 4; ++i) t += rf_match(4 * q + i, K[4 * q + i]) ? 1u : 0u;
+                                }
                                 uint32_t tot = 0;
                                 const uint32_t ex2 = block_excl_u32<kNT>(t, ls->red32, &tot);
                                 unsigned long long r2 = taken + ex2;
+                                if (q < nq) {
 #pragma unroll
-                                for (int i = 0; i < SW; ++i) {
-                                    if (!rf_match(j * SW + i)) continue;
-                                    if (r2 == li) ls->bc[13] = comp_at(j * SW + i);
-                                    ++r2;
+                                    for (int i = 0; i < 4; ++i) {
+                                        if (!rf_match(4 * q + i, K[4 * q + i])) continue;
+                                        if (r2 == li) ls->bc[13] = comp_of(K[4 * q + i], static_cast<uint32_t>(c0 + 4 * q + i));
+                                        ++r2;
+                                    }
                                 }
                                 taken += tot;
                             }
                             __syncthreads();
-                            if (tid < kC) cluster.map_shared_rank(cs, tid)->rsel = ls->bc[13];
+                            if (tid < static_cast<int>(C)) cluster.map_shared_rank(cs, tid)->rsel = ls->bc[13];
                         }
                         rf.phase = 3;
                     }
@@ -1558,18 +1816,16 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                     rf_build(rf.buf);
                 } else if (rf.phase == 2) {
                     uint32_t c = 0;
-#pragma unroll
-                    for (int q = 0; q < EPT; ++q) c += rf_match(q) ? 1u : 0u;
+                    for (int e = tid; e < len; e += kNT) c += rf_match(e, K[e]) ? 1u : 0u;
                     const unsigned long long tc = block_sum_u64<kNT>(c, ls->red);
-                    if (tid < kC) cluster.map_shared_rank(cs, tid)->rcnt[crank] = tc;
+                    if (tid < static_cast<int>(C)) cluster.map_shared_rank(cs, tid)->rcnt[crank] = tc;
                 }
             }
         } else if (st.pending_kind == 2) {
             if (st.stage == kStDSum) {
                 // dense residual: totals, then the owner CTA of the crossing finds the token
                 double rs = 0.0, ps = 0.0;
-#pragma unroll
-                for (int q = 0; q < kC; ++q) {
+                for (uint32_t q = 0; q < C; ++q) {
                     rs += cs->rsum[q];
                     ps += cs->psum[q];
                 }
@@ -1577,10 +1833,10 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                 const double target = rc.u_draw * (use_res ? rs : 1.0);
                 int owner = -1;
                 double before = 0.0;
-                for (int q = 0; q < kC; ++q) {
+                for (uint32_t q = 0; q < C; ++q) {
                     const double v = use_res ? cs->rsum[q] : cs->psum[q];
-                    if (owner < 0 && before + v > target && v > 0.0) {
-                        owner = q;
+                    if (before + v > target && v > 0.0) {
+                        owner = static_cast<int>(q);
                         break;
                     }
                     before += v;
@@ -1591,26 +1847,29 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                     st.pending_kind = 0;
                 } else {
                     if (owner == static_cast<int>(crank)) {
-                        // ordered scan of my entries in vocabulary-id order (slot-major)
+                        // ordered scan of my entries in vocabulary-id order
                         const float* qrow = a.q + (static_cast<size_t>(rc.stream) * a.k + rc.vidx) * a.row_stride + c0;
                         const double zk_d = static_cast<double>(st.zkept);
                         double run = before;
                         unsigned long long found = ~0ull;
-                        for (int j = 0; j < NV && found == ~0ull; ++j) {
-                            double vals[SW];
+                        for (int m = 0; m < nq_iter && found == ~0ull; ++m) {
+                            const int q = tid + m * kNT;
+                            double vals[4];
                             double s = 0.0;
 #pragma unroll
-                            for (int i = 0; i < SW; ++i) {
-                                const int q = j * SW + i;
-                                const uint32_t k = keys[q];
+                            for (int i = 0; i < 4; ++i) {
+                                const int e = 4 * q + i;
                                 double v = 0.0;
-                                if (k != 0u) {
-                                    const unsigned long long cp = comp_at(q);
-                                    const float x = kval(k);
-                                    if (cp >= st.xcross && cp >= st.kbound && x >= x_minp) {
-                                        const float pf = static_cast<float>(static_cast<double>(weight_of(x, wc)) / zk_d);
-                                        v = use_res ? fmax(0.0, static_cast<double>(pf) - static_cast<double>(qrow[elem_of<SW>(j, i)]))
-                                                    : static_cast<double>(pf);
+                                if (q < nq && e < len) {
+                                    const uint32_t k = K[e];
+                                    if (k != 0u) {
+                                        const unsigned long long cp = comp_of(k, static_cast<uint32_t>(c0 + e));
+                                        const float x = kval(k);
+                                        if (cp >= st.xcross && cp >= st.kbound && x >= x_minp) {
+                                            const float pf = static_cast<float>(static_cast<double>(weight_of(x, wc)) / zk_d);
+                                            v = use_res ? fmax(0.0, static_cast<double>(pf) - static_cast<double>(qrow[e]))
+                                                        : static_cast<double>(pf);
+                                        }
                                     }
                                 }
                                 vals[i] = v;
@@ -1621,10 +1880,10 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                             double acc = run + incl - s;
                             unsigned long long cand = ~0ull;
 #pragma unroll
-                            for (int i = 0; i < SW; ++i) {
+                            for (int i = 0; i < 4; ++i) {
                                 acc += vals[i];
                                 if (cand == ~0ull && vals[i] > 0.0 && acc > target)
-                                    cand = static_cast<unsigned long long>(c0 + elem_of<SW>(j, i));
+                                    cand = static_cast<unsigned long long>(c0 + 4 * q + i);
                             }
                             found = block_min_bc(cand, ls);
                             run += tot2;
@@ -1643,8 +1902,7 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                 st.pending_kind = 0;
             } else if (st.stage == kStCount) {
                 unsigned long long nk = 0ull;
-#pragma unroll
-                for (int q = 0; q < kC; ++q) nk += cs->cnt[q];
+                for (uint32_t q = 0; q < C; ++q) nk += cs->cnt[q];
                 st.result = static_cast<int32_t>(nk);
                 st.stage = kStDone;
                 st.pending_kind = 0;
@@ -1699,15 +1957,14 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                 if (P->min_p > 0.0f && Wmin < st.zkept) st.zkept = Wmin;
                 if (MODE == kModeCandidates) {
                     uint32_t c = 0;
-#pragma unroll
-                    for (int q = 0; q < EPT; ++q) {
-                        const uint32_t k = keys[q];
+                    for (int e = tid; e < len; e += kNT) {
+                        const uint32_t k = K[e];
                         if (k == 0u) continue;
-                        const unsigned long long cp = comp_at(q);
+                        const unsigned long long cp = comp_of(k, static_cast<uint32_t>(c0 + e));
                         if (cp >= st.xcross && cp >= st.kbound && kval(k) >= x_minp) ++c;
                     }
                     const unsigned long long tc = block_sum_u64<kNT>(c, ls->red);
-                    if (tid < kC) cluster.map_shared_rank(cs, tid)->cnt[crank] = tc;
+                    if (tid < static_cast<int>(C)) cluster.map_shared_rank(cs, tid)->cnt[crank] = tc;
                     st.stage = kStCount;
                     st.pending_kind = 2;
                 } else if (MODE == kModeVerify && rc.vrole == 0) {
@@ -1732,21 +1989,19 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                             const float* qrow_c = qrow + c0;
                             const double zk_d = static_cast<double>(st.zkept);
                             double rsum = 0.0, psum = 0.0;
-#pragma unroll
-                            for (int q = 0; q < EPT; ++q) {
-                                const uint32_t k = keys[q];
+                            for (int e = tid; e < len; e += kNT) {
+                                const uint32_t k = K[e];
                                 if (k == 0u) continue;
-                                const unsigned long long cp = comp_at(q);
+                                const unsigned long long cp = comp_of(k, static_cast<uint32_t>(c0 + e));
                                 const float x = kval(k);
                                 if (!(cp >= st.xcross && cp >= st.kbound && x >= x_minp)) continue;
                                 const float pf = static_cast<float>(static_cast<double>(weight_of(x, wc)) / zk_d);
-                                rsum += fmax(0.0, static_cast<double>(pf) -
-                                                      static_cast<double>(qrow_c[elem_of<SW>(q / SW, q % SW)]));
+                                rsum += fmax(0.0, static_cast<double>(pf) - static_cast<double>(qrow_c[e]));
                                 psum += static_cast<double>(pf);
                             }
                             rsum = block_sum_f64(rsum, ls);
                             psum = block_sum_f64(psum, ls);
-                            if (tid < kC) {
+                            if (tid < static_cast<int>(C)) {
                                 ClusterShared* dst = cluster.map_shared_rank(cs, tid);
                                 dst->rsum[crank] = rsum;
                                 dst->psum[crank] = psum;
@@ -1765,7 +2020,7 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
                                 st.excl = kept ? dcomp : 0ull;
                                 st.wexcl = wd;
                                 const unsigned long long t = scale_mass(rc.u_draw, zr) + 1ull;
-                                const int bd = kept ? xbin_g(static_cast<uint32_t>(dkey)) : kABins;
+                                const int bd = kept ? xbin_g(dkey) : kABins;
                                 int lo = 0, hi = kABins - 1;
                                 while (lo < hi) {
                                     const int mid = (lo + hi) >> 1;
@@ -1828,9 +2083,9 @@ __global__ void __launch_bounds__(kNT, (EPT <= 80) ? 2 : 1) row_kernel(const Row
 // (speculative.cpp:801-916 / 630-692 decision order)
 
 inline __global__ void verify_finalize_kernel(const RowArgs a, uint32_t n_streams, int32_t* out_accepted,
-                                       int32_t* out_tokens, int32_t* out_n_tokens,
-                                       int32_t* out_first_reject, int32_t* out_uniforms_used,
-                                       int32_t* out_status) {
+                                              int32_t* out_tokens, int32_t* out_n_tokens,
+                                              int32_t* out_first_reject, int32_t* out_uniforms_used,
+                                              int32_t* out_status) {
     const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= n_streams) return;
     const uint32_t kp1 = a.k + 1;
@@ -1900,7 +2155,7 @@ inline __global__ void verify_finalize_kernel(const RowArgs a, uint32_t n_stream
 }
 
 // ---------------------------------------------------------------------------------------------
-// launch of one (mode, dtype) instance family; defined in smp_inst.cu, compiled once per pair
+// launch of one (mode, dtype) kernel; defined in smp_inst.cu, compiled once per pair
 
 template <int MODE, int DT>
 cudaError_t launch_mode_dt(const RowArgs& a, const LaunchPlan& plan, cudaStream_t stream);
@@ -1917,8 +2172,5 @@ SIXI_DECL_INST(kModeGreedy, SIXI_SMP_BF16)
 SIXI_DECL_INST(kModeVerify, SIXI_SMP_F32)
 SIXI_DECL_INST(kModeVerify, SIXI_SMP_BF16)
 #undef SIXI_DECL_INST
-
-// elements per thread of the instantiated kernels
-int pick_ept(uint32_t chunk);
 
 }  // namespace sixi_b200

@@ -11,6 +11,7 @@ import pytest
 REPO = Path(__file__).resolve().parent.parent
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(REPO / "sixi-asi_b200"))
+sys.path.insert(0, str(REPO / "tests"))
 
 
 def pytest_configure(config):

@@ -111,14 +111,26 @@ def make_batches(seed: int):
 
     base = W.config2(rows=ROWS, vocab=VOCAB, seed=seed)
     rng = np.random.default_rng(seed + 17)
-    logits = [base["logits"]] + [rng.normal(0.0, 2.5, size=(ROWS, VOCAB)).astype(np.float32)
-                                 for _ in range(NBUF - 1)]
+    logits = [base["logits"]] + [W.config2_logits(rng, ROWS, VOCAB) for _ in range(NBUF - 1)]
     uniforms = [rng.random(ROWS) for _ in range(NBUF)]
     return base, logits, uniforms
 
 
 def algorithmic_bytes(base: dict) -> int:
     return ROWS * VOCAB * 4 + 4 * int(base["hist_off"][-1])
+
+
+def profiled_traffic() -> int | None:
+    """DRAM bytes (read + write) per row_kernel launch of this workload from the committed ncu
+    summary (profiles/row_kernel_sample_config2.md), or None when it is absent."""
+    import re
+
+    p = REPO / "profiles" / "row_kernel_sample_config2.md"
+    try:
+        m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", p.read_text())
+    except OSError:
+        return None
+    return int(m.group(1)) if m else None
 
 
 def cpu_reference_rows_per_s(base, logits, uniforms, budget_s: float, n_threads: int = 0):
@@ -327,7 +339,7 @@ def main() -> int:
                        "l2": f"inputs larger than L2: {NBUF} rotating batches, "
                              f"{NBUF * ROWS * VOCAB * 4 / 1e6:.0f} MB per GPU"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+                         "frac": achieved / peak, "traffic": profiled_traffic(), "peak_source": peak_kind,
                          "bytes_per_launch": bytes_per_launch},
             "e2e": e2e,
             "cpu_baseline": cpu,

@@ -89,7 +89,21 @@ def config2(rows: int = 32, vocab: int = QWEN_VOCAB, seed: int = 2, hist_lo: int
     off = np.zeros(rows + 1, dtype=np.int64)
     off[1:] = np.cumsum(lens)
     hist = rng.integers(0, vocab, size=int(off[-1]), dtype=np.int32)
+    boost_rows(np.random.default_rng(seed + 0xB005), logits)
     return dict(logits=logits, params=params, hist=hist, hist_off=off, masks=None)
+
+
+def boost_rows(rng: np.random.Generator, logits: np.ndarray, n: int = 16, by: float = 8.0) -> np.ndarray:
+    """Adds `by` to `n` distinct random ids of every row (the boosted tokens of configs 1 and 2)."""
+    vocab = logits.shape[1]
+    for r in range(logits.shape[0]):
+        logits[r, rng.choice(vocab, size=min(n, vocab), replace=False)] += np.float32(by)
+    return logits
+
+
+def config2_logits(rng: np.random.Generator, rows: int = 32, vocab: int = QWEN_VOCAB) -> np.ndarray:
+    """Fresh config-2 logits: N(0, 2.5^2) with 16 ids per row boosted by +8."""
+    return boost_rows(rng, rng.normal(0.0, 2.5, size=(rows, vocab)).astype(np.float32))
 
 
 def config3(rows: int = 32, vocab: int = QWEN_VOCAB, seed: int = 3, **kw) -> dict:

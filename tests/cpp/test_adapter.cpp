@@ -1,0 +1,353 @@
+// test_adapter.cpp - parity of the C++ host adapter (sixi-asi_b200/host/sixi_sampler.hpp) against
+// the CPU oracle (oracle/sixi_oracle.h, port build), written like the engine's own C++ tests.
+//
+//   engine_topk_topp        restates test_sampler_candidates_topk_topp
+//                           (tests/test_routing_and_numerics.cpp:485-545) through the adapter
+//   random_rows             sample_token / compute_sampling_candidates / sample_greedy_argmax on
+//                           seeded rows vs the oracle (V = 1, 33, 4097, 151,936)
+//   rng_consumption         greedy draws nothing, sampled rows draw one uniform, failing rows
+//                           leave the RNG untouched (core_execution.cpp:586-619)
+//   errors                  the engine's error behaviour (null / empty / wrong vocab / NaN)
+//   verify_random           SpeculativeDecoder verification (dense q and one-hot) vs orc_verify,
+//                           and the RNG advanced by exactly the uniforms used
+//   verify_forced_rejection greedy rejection positions (tests/test_determinism_and_speculative.cpp
+//                           forced-rejection checks)
+// Exit status 0 when every check passes. Needs a CUDA device.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <numeric>
+#include <string>
+#include <vector>
+
+#include "../../oracle/sixi_oracle.h"
+#include "sixi_sampler.hpp"
+
+using namespace sixi_b200;
+
+namespace {
+
+int g_fail = 0;
+#define CHECK(cond)                                                                   \
+    do {                                                                              \
+        if (!(cond)) {                                                                \
+            std::fprintf(stderr, "CHECK failed %s:%d: %s\n", __FILE__, __LINE__, #cond); \
+            ++g_fail;                                                                 \
+            return false;                                                             \
+        }                                                                             \
+    } while (0)
+
+// Test RNG with the engine RNG's interface (next_uniform01, checkpoint, restore): SplitMix64.
+struct TestRng {
+    uint64_t s;
+    explicit TestRng(uint64_t seed) : s(seed) {}
+    uint64_t next_u64() {
+        uint64_t z = (s += 0x9E3779B97F4A7C15ull);
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    }
+    double next_uniform01() { return static_cast<double>(next_u64() >> 11) * 0x1.0p-53; }
+    uint64_t checkpoint() const { return s; }
+    void restore(uint64_t st) { s = st; }
+};
+
+std::vector<float> normal_row(TestRng& r, size_t v, float sigma) {
+    std::vector<float> x(v);
+    for (size_t i = 0; i < v; ++i) {  // Box-Muller
+        const double u1 = std::max(r.next_uniform01(), 1e-300), u2 = r.next_uniform01();
+        x[i] = static_cast<float>(sigma * std::sqrt(-2.0 * std::log(u1)) * std::cos(6.283185307179586 * u2));
+    }
+    return x;
+}
+
+// True when u is within 1e-6 of a cumulative boundary of the oracle's candidate list.
+bool near_boundary(const std::vector<float>& x, const sixi_smp_params& p, const std::vector<int32_t>& h, double u) {
+    std::vector<int32_t> ids(x.size());
+    std::vector<double> pr(x.size());
+    uint64_t n = 0;
+    orc_candidates(x.data(), SIXI_SMP_F32, x.size(), &p, h.data(), h.size(), nullptr, x.size(), ids.data(),
+                   pr.data(), &n);
+    double c = 0.0;
+    for (uint64_t i = 0; i < n; ++i) {
+        c += pr[i];
+        if (std::fabs(c - u) < 1e-6) return true;
+    }
+    return false;
+}
+
+bool engine_topk_topp() {
+    const uint64_t V = 5000;
+    auto made = DeviceSampler::create(0, 64, V);
+    CHECK(made.ok());
+    DeviceSampler& s = *made.value();
+    std::vector<float> logits(V);
+    for (uint64_t i = 0; i < V; ++i)
+        logits[i] = std::sin(static_cast<float>(i) * 0.37f) * 3.0f + ((i % 97 == 0) ? 2.5f : 0.0f);
+    SamplingParams p;
+    p.temperature = 1.0f;
+    p.top_k = 20;
+    p.top_p = 1.0f;
+    p.mode = ExecutionMode::StrictReplay;
+    auto cr = s.compute_sampling_candidates(logits.data(), V, p);
+    CHECK(cr.ok());
+    const auto& cands = cr.value();
+    CHECK(cands.size() == 20);
+    std::vector<int32_t> ids(V);
+    std::iota(ids.begin(), ids.end(), 0);
+    std::sort(ids.begin(), ids.end(), [&](int32_t a, int32_t b) {
+        if (logits[a] != logits[b]) return logits[a] > logits[b];
+        return a < b;
+    });
+    double psum = 0.0;
+    for (size_t i = 0; i < 20; ++i) {
+        CHECK(cands[i].id == ids[i]);
+        if (i > 0) CHECK(cands[i - 1].prob >= cands[i].prob);
+        psum += cands[i].prob;
+    }
+    CHECK(std::fabs(psum - 1.0) < 1e-9);
+    CHECK(cands.front().id == s.sample_greedy_argmax(logits.data(), V));
+    p.top_p = 0.5f;
+    auto tp = s.compute_sampling_candidates(logits.data(), V, p);
+    CHECK(tp.ok() && !tp.value().empty() && tp.value().size() < 20);
+    CHECK(tp.value().front().id == ids[0]);
+    double tsum = 0.0;
+    for (const auto& c : tp.value()) tsum += c.prob;
+    CHECK(std::fabs(tsum - 1.0) < 1e-9);
+    TestRng r1(99), r2(99);
+    auto t1 = s.sample_token(logits.data(), V, p, r1);
+    auto t2 = s.sample_token(logits.data(), V, p, r2);
+    CHECK(t1.ok() && t2.ok() && t1.value() == t2.value());
+    bool in_set = false;
+    for (const auto& c : tp.value()) in_set = in_set || c.id == t1.value();
+    CHECK(in_set);
+    p.temperature = 0.0f;
+    TestRng r3(5);
+    const uint64_t before = r3.checkpoint();
+    auto g = s.sample_token(logits.data(), V, p, r3);
+    CHECK(g.ok() && g.value() == ids[0]);
+    CHECK(r3.checkpoint() == before);
+    return true;
+}
+
+bool random_rows() {
+    const uint64_t vocabs[] = {1, 33, 4097, 151936};
+    TestRng gen(20261201);
+    for (uint64_t V : vocabs) {
+        auto made = DeviceSampler::create(0, 16, V);
+        CHECK(made.ok());
+        DeviceSampler& s = *made.value();
+        for (int it = 0; it < 12; ++it) {
+            auto x = normal_row(gen, V, it % 3 == 0 ? 6.0f : 2.5f);
+            SamplingParams p;
+            const float temps[] = {0.0f, 0.3f, 0.7f, 1.0f, 1.5f};
+            const int32_t tks[] = {0, 1, 5, 20, 40, 100, 256};
+            p.temperature = temps[it % 5];
+            p.top_k = tks[(it * 3) % 7];
+            p.top_p = it % 4 == 0 ? 1.0f : 0.6f + 0.1f * static_cast<float>(it % 4);
+            p.repetition_penalty = it % 2 ? 1.2f : 1.0f;
+            p.presence_penalty = it % 3 == 1 ? 0.5f : 0.0f;
+            p.mode = it % 2 ? ExecutionMode::Adaptive : ExecutionMode::StrictReplay;
+            std::vector<int32_t> hist(static_cast<size_t>(gen.next_u64() % 300));
+            for (auto& h : hist) h = static_cast<int32_t>(gen.next_u64() % V);
+            const sixi_smp_params sp = to_smp_params(p);
+            // greedy argmax of the raw row
+            CHECK(s.sample_greedy_argmax(x.data(), V) == orc_greedy_argmax(x.data(), V));
+            // sampled token with the RNG's next uniform
+            TestRng r(1000 + it), peek(1000 + it);
+            const double u = p.temperature > 0.0f ? peek.next_uniform01() : 0.0;
+            auto t = s.sample_token(x.data(), V, p, r, hist);
+            CHECK(t.ok());
+            int32_t ot = -1;
+            CHECK(orc_sample(x.data(), SIXI_SMP_F32, V, &sp, hist.data(), hist.size(), nullptr, u, &ot) == 0);
+            if (t.value() != ot && !near_boundary(x, sp, hist, u)) {
+                std::fprintf(stderr, "V=%llu it=%d token %d vs oracle %d\n", (unsigned long long)V, it, t.value(), ot);
+                CHECK(false);
+            }
+            // candidate list (only lists of at most 256 entries come back through the adapter)
+            std::vector<int32_t> oid(V);
+            std::vector<double> opr(V);
+            uint64_t on = 0;
+            orc_candidates(x.data(), SIXI_SMP_F32, V, &sp, hist.data(), hist.size(), nullptr, V, oid.data(),
+                           opr.data(), &on);
+            auto c = s.compute_sampling_candidates(x.data(), V, p, hist);
+            if (on <= 256) {
+                CHECK(c.ok() && c.value().size() == on);
+                for (uint64_t i = 0; i < on; ++i) {
+                    CHECK(c.value()[i].id == oid[i]);
+                    CHECK(std::fabs(c.value()[i].prob - opr[i]) <= 1e-5 * opr[i] + 1e-300);
+                }
+            } else {
+                CHECK(!c.ok() && c.code() == ErrorCode::OutOfBounds);
+            }
+        }
+    }
+    return true;
+}
+
+bool rng_consumption() {
+    const uint64_t V = 4097;
+    auto made = DeviceSampler::create(0, 4, V);
+    CHECK(made.ok());
+    DeviceSampler& s = *made.value();
+    TestRng gen(7);
+    auto x = normal_row(gen, V, 2.5f);
+    SamplingParams p;
+    p.temperature = 0.0f;
+    TestRng r(11);
+    uint64_t st0 = r.checkpoint();
+    CHECK(s.sample_token(x.data(), V, p, r).ok());
+    CHECK(r.checkpoint() == st0);  // greedy: no uniform
+    p.temperature = 0.8f;
+    CHECK(s.sample_token(x.data(), V, p, r).ok());
+    TestRng one(11);
+    one.next_uniform01();
+    CHECK(r.checkpoint() == one.checkpoint());  // sampled: exactly one uniform
+    x[17] = std::nanf("");
+    st0 = r.checkpoint();
+    auto bad = s.sample_token(x.data(), V, p, r);
+    CHECK(!bad.ok() && bad.code() == ErrorCode::NumericNaNOrInf);
+    CHECK(r.checkpoint() == st0);  // a failing row draws nothing
+    return true;
+}
+
+bool errors() {
+    const uint64_t V = 100;
+    auto made = DeviceSampler::create(0, 4, V);
+    CHECK(made.ok());
+    DeviceSampler& s = *made.value();
+    std::vector<float> x(V, 0.0f);
+    CHECK(s.sample_greedy_argmax(nullptr, V) == -1);
+    CHECK(s.sample_greedy_argmax(x.data(), 0) == -1);
+    SamplingParams p;
+    TestRng r(1);
+    auto e1 = s.sample_token(nullptr, V, p, r);
+    CHECK(!e1.ok() && e1.code() == ErrorCode::InvalidArgument);
+    auto e2 = s.sample_token(x.data(), V + 1, p, r);
+    CHECK(!e2.ok() && e2.code() == ErrorCode::InvalidArgument);
+    // all-equal logits: lowest id wins (engine tie rule)
+    CHECK(s.sample_greedy_argmax(x.data(), V) == 0);
+    auto bad_create = DeviceSampler::create(0, 4, 0);
+    CHECK(!bad_create.ok() && bad_create.code() == ErrorCode::InvalidArgument);
+    return true;
+}
+
+bool verify_random() {
+    const uint64_t vocabs[] = {700, 151936};
+    TestRng gen(4242);
+    for (uint64_t V : vocabs) {
+        auto made = DeviceSampler::create(0, 32, V);
+        CHECK(made.ok());
+        DeviceSampler& s = *made.value();
+        for (int it = 0; it < 8; ++it) {
+            const uint32_t k = 1 + static_cast<uint32_t>(it % 6);
+            std::vector<float> tgt((k + 1) * V), q(k * V);
+            for (uint32_t i = 0; i <= k; ++i) {
+                auto row = normal_row(gen, V, 3.0f);
+                std::copy(row.begin(), row.end(), tgt.begin() + i * V);
+            }
+            std::vector<int32_t> drafts(k);
+            for (uint32_t i = 0; i < k; ++i) {  // q = softmax(target + noise), draft = argmax of q
+                double m = -1e300, z = 0.0;
+                std::vector<double> t(V);
+                for (uint64_t j = 0; j < V; ++j) {
+                    t[j] = tgt[i * V + j] + 0.8 * (gen.next_uniform01() - 0.5);
+                    m = std::max(m, t[j]);
+                }
+                for (uint64_t j = 0; j < V; ++j) z += std::exp(t[j] - m);
+                int32_t best = 0;
+                for (uint64_t j = 0; j < V; ++j) {
+                    q[i * V + j] = static_cast<float>(std::exp(t[j] - m) / z);
+                    if (q[i * V + j] > q[i * V + best]) best = static_cast<int32_t>(j);
+                }
+                drafts[i] = (it % 3 == 2) ? static_cast<int32_t>(gen.next_u64() % V) : best;
+            }
+            SamplingParams p;
+            p.temperature = it % 4 == 3 ? 0.0f : 0.9f;
+            p.top_k = it % 2 ? 0 : 40;
+            p.top_p = 0.9f;
+            p.repetition_penalty = 1.1f;
+            p.mode = ExecutionMode::Adaptive;
+            std::vector<int32_t> ctx(50);
+            for (auto& c : ctx) c = static_cast<int32_t>(gen.next_u64() % V);
+            for (int dense = 0; dense < 2; ++dense) {
+                TestRng r(77 + it), peek(77 + it);
+                std::vector<double> u(k + 1);
+                for (auto& v : u) v = peek.next_uniform01();
+                auto res = s.verify(tgt.data(), dense ? q.data() : nullptr, drafts, p, r, ctx);
+                CHECK(res.ok());
+                const sixi_smp_params sp = to_smp_params(p);
+                const int64_t hoff[2] = {0, static_cast<int64_t>(ctx.size())};
+                int32_t acc = 0, ntok = 0, frej = 0, used = 0, st = 0;
+                std::vector<int32_t> toks(k + 1);
+                orc_verify(tgt.data(), SIXI_SMP_F32, V, V, dense ? q.data() : nullptr, drafts.data(), nullptr, 1, k,
+                           &sp, nullptr, ctx.data(), hoff, u.data(), 0, &acc, toks.data(), &ntok, &frej, &used, &st, 1);
+                CHECK(st == 0);
+                CHECK(res.value().accepted_draft_count == static_cast<uint32_t>(acc));
+                CHECK(res.value().first_rejected_position == frej);
+                CHECK(res.value().uniforms_used == static_cast<uint32_t>(used));
+                CHECK(res.value().committed_tokens.size() == static_cast<size_t>(ntok));
+                for (int32_t i = 0; i < ntok; ++i) CHECK(res.value().committed_tokens[i] == toks[i]);
+                TestRng adv(77 + it);
+                for (int32_t i = 0; i < used; ++i) adv.next_uniform01();
+                CHECK(r.checkpoint() == adv.checkpoint());
+            }
+        }
+    }
+    return true;
+}
+
+bool verify_forced_rejection() {
+    const uint64_t V = 4096;
+    const uint32_t k = 4;
+    auto made = DeviceSampler::create(0, 16, V);
+    CHECK(made.ok());
+    DeviceSampler& s = *made.value();
+    TestRng gen(3);
+    std::vector<float> tgt((k + 1) * V);
+    std::vector<int32_t> am(k + 1);
+    for (uint32_t i = 0; i <= k; ++i) {
+        auto row = normal_row(gen, V, 1.0f);
+        std::copy(row.begin(), row.end(), tgt.begin() + i * V);
+        am[i] = orc_greedy_argmax(row.data(), V);
+    }
+    SamplingParams p;
+    p.temperature = 0.0f;
+    for (uint32_t pos = 0; pos <= k; ++pos) {
+        std::vector<int32_t> drafts(am.begin(), am.begin() + k);
+        if (pos < k) drafts[pos] = (am[pos] + 17) % static_cast<int32_t>(V);
+        TestRng r(1);
+        auto res = s.verify(tgt.data(), nullptr, drafts, p, r, {});
+        CHECK(res.ok());
+        CHECK(res.value().accepted_draft_count == pos);
+        CHECK(res.value().first_rejected_position == (pos < k ? static_cast<int32_t>(pos) : -1));
+        CHECK(res.value().committed_tokens.size() == pos + 1);
+        for (uint32_t i = 0; i <= pos; ++i) CHECK(res.value().committed_tokens[i] == am[i]);
+        CHECK(res.value().uniforms_used == 0 && r.checkpoint() == 1);
+    }
+    return true;
+}
+
+}  // namespace
+
+int main() {
+    struct {
+        const char* name;
+        bool (*fn)();
+    } tests[] = {{"engine_topk_topp", engine_topk_topp},
+                 {"random_rows", random_rows},
+                 {"rng_consumption", rng_consumption},
+                 {"errors", errors},
+                 {"verify_random", verify_random},
+                 {"verify_forced_rejection", verify_forced_rejection}};
+    int passed = 0, n = 0;
+    for (auto& t : tests) {
+        ++n;
+        const bool ok = t.fn();
+        std::printf("%s %s\n", ok ? "PASS" : "FAIL", t.name);
+        passed += ok ? 1 : 0;
+    }
+    std::printf("%d/%d passed\n", passed, n);
+    return passed == n && g_fail == 0 ? 0 : 1;
+}

@@ -1,0 +1,109 @@
+"""GPU parity of the speculative verifier (sixi_smp_verify) against the CPU oracle.
+
+Accept/reject decisions, committed tokens, first-reject positions and the number of uniforms
+consumed are compared bit-exactly (speculative.cpp:801-916 for dense draft probabilities,
+589-692 for one-hot drafts). The seeded inputs below place no decision within 1e-6 of a
+boundary, so no mismatch is excused.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import has_gpu
+
+pytestmark = pytest.mark.gpu
+
+if not has_gpu():
+    pytest.skip("no CUDA device", allow_module_level=True)
+
+import torch  # noqa: E402
+
+import sixi_smp as S  # noqa: E402
+from sixi_smp import workloads as W  # noqa: E402
+from test_gpu_parity import dev, sampler  # noqa: E402
+
+KEYS = ("accepted", "tokens", "n_tokens", "first_reject", "uniforms_used", "status")
+
+
+def run_verify(d: dict, dense: bool, uniforms="given", n_drafts=None, step: int = 0, bf16: bool = True):
+    vocab = d["target_bits"].shape[1]
+    target = d["target_bits"] if bf16 else W.bf16_bits_to_f32(d["target_bits"])
+    u = d["uniforms"] if uniforms == "given" else None
+    smp = sampler(vocab)
+    o = smp.verify(dev(target), dev(d["drafts"]), dev(d["params"]), draft_probs=dev(d["q"]) if dense else None,
+                   n_drafts=dev(n_drafts), masks=dev(d["masks"]), hist=dev(d["hist"]), hist_off=dev(d["hist_off"]),
+                   uniforms=dev(u), step=step)
+    torch.cuda.synchronize()
+    return {k: v.cpu().numpy() for k, v in o.items()}, target, u
+
+
+def check(port, d: dict, dense: bool, uniforms="given", n_drafts=None, step: int = 0, bf16: bool = True):
+    g, target, u = run_verify(d, dense, uniforms, n_drafts, step, bf16)
+    o = port.verify(target, d["drafts"], d["params"], q=d["q"] if dense else None, n_drafts=n_drafts,
+                    masks=d["masks"], hist=d["hist"], hist_off=d["hist_off"], uniforms=u, step=step)
+    for k in KEYS:
+        assert np.array_equal(g[k], o[k]), f"{k}: gpu={g[k]} oracle={o[k]}"
+    return g
+
+
+def test_verify_golden_vectors():
+    """The engine-generated verify goldens, through the GPU."""
+    import golden.make_golden as G
+
+    g = np.load(G.OUT)
+    for i, d in enumerate(G.verify_cases()):
+        o, _, _ = run_verify(d, d["dense"])
+        for k in KEYS:
+            assert np.array_equal(o[k], g[f"v{i}_{k}"]), (i, k, o[k], g[f"v{i}_{k}"])
+
+
+@pytest.mark.parametrize("dense", [True, False])
+@pytest.mark.parametrize("stochastic", [True, False])
+def test_verify_config4_full_vocab(port, dense, stochastic):
+    """Config 4: 32 streams x 8 drafts, V=151,936 bf16 targets, parameter mix, grammar masks."""
+    d = W.config4(streams=32, k=8, seed=41 + dense + 2 * stochastic, stochastic=stochastic, masked=True)
+    g = check(port, d, dense)
+    if stochastic:
+        assert g["accepted"].min() >= 0 and g["accepted"].max() <= 8
+
+
+@pytest.mark.parametrize("vocab", [1, 33, 700, 4097])
+@pytest.mark.parametrize("dense", [True, False])
+def test_verify_small_vocab(port, vocab, dense):
+    for seed in range(3):
+        d = W.config4(streams=5, k=3, vocab=vocab, seed=200 + seed, stochastic=seed != 1, masked=seed % 2 == 0)
+        check(port, d, dense, bf16=seed != 2)
+
+
+def test_verify_ragged_drafts_and_philox(port):
+    """n_drafts below k for some streams, and uniforms drawn by the library (Philox slots 0..k)."""
+    d = W.config4(streams=12, k=6, vocab=3000, seed=77, stochastic=True, masked=True)
+    nd = np.array([6, 0, 1, 2, 3, 4, 5, 6, 0, 6, 3, 1], dtype=np.int32)
+    check(port, d, True, n_drafts=nd)
+    check(port, d, False, n_drafts=nd)
+    check(port, d, True, uniforms=None, step=5)
+    check(port, d, False, uniforms=None, step=9, n_drafts=nd)
+
+
+def test_verify_greedy_forced_rejections(port):
+    """Greedy match rejects exactly at the first wrong draft (engine test: forced rejection)."""
+    rng = np.random.default_rng(3)
+    v, k = 4096, 4
+    tgt = rng.normal(0, 1, size=(k + 1, k + 1, v)).astype(np.float32)
+    drafts = np.empty((k + 1, k), np.int32)
+    for s in range(k + 1):
+        am = tgt[s].argmax(axis=1)
+        drafts[s] = am[:k]
+        if s < k:
+            drafts[s, s] = (am[s] + 17) % v
+    params = S.make_params(k + 1, temperature=0.0)
+    smp = sampler(v)
+    o = smp.verify(dev(tgt.reshape(-1, v)), dev(drafts), dev(params))
+    torch.cuda.synchronize()
+    acc = o["accepted"].cpu().numpy()
+    assert list(acc) == list(range(k + 1))
+    ref = port.verify(tgt.reshape(-1, v), drafts, params)
+    for key in KEYS:
+        assert np.array_equal(o[key].cpu().numpy(), ref[key]), key

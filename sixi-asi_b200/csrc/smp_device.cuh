@@ -12,7 +12,7 @@
 //     every CTA of a cluster derives identical cumulative masses and the selection is
 //     deterministic. The exponent is computed with hi/lo-split constants so that the only
 //     rounding is one fp32 rounding of the exponent and the ex2 approximation (relative error
-//     ~1e-7 per weight); weights below 2^-43 of the maximum are 0 and are never drawn.
+//     ~1e-7 per weight); weights below 2^-44 of the maximum round to 0 and are never drawn.
 #pragma once
 
 #include <cstdint>
@@ -111,22 +111,11 @@ __device__ __forceinline__ float fast_ex2(float x) {
     return y;
 }
 
-// Fixed-point weight round(2^t * 2^43) of t = neg_log2w(x) <= 0, built from the exponent and
-// mantissa of the fp32 power with integer operations (round half up on the dropped bits).
+// Fixed-point weight round(2^t * 2^43) of t = neg_log2w(x) <= 0 (the scaling by 2^43 is exact, the
+// conversion rounds to nearest; 0 below 2^-44).
 __device__ __forceinline__ uint64_t weight_of(float x, const WeightCtx& w) {
-    float t = neg_log2w(x, w);
-    t = fminf(t, 0.0f);
-    const float e = fast_ex2(t);  // in [0, 1]; flushed to 0 below the normal range
-    const uint32_t b = __float_as_uint(e);
-    const int ex = static_cast<int>(b >> 23);
-    const uint32_t m = (b & 0x7FFFFFu) | 0x800000u;
-    const int sh = ex - 107;  // value = m * 2^(ex - 127 - 23) * 2^43
-    const uint32_t r = static_cast<uint32_t>(sh < 0 ? -sh : 0);
-    const uint32_t l = static_cast<uint32_t>(sh > 0 ? sh : 0);
-    const uint32_t rr = r < 31u ? r : 31u;
-    const uint32_t mr = (m + ((1u << rr) >> 1)) >> rr;
-    const uint64_t v = static_cast<uint64_t>(mr) << l;
-    return (ex == 0 || r >= 25u) ? 0ull : v;
+    const float t = fminf(neg_log2w(x, w), 0.0f);
+    return __float2ull_rn(fast_ex2(t) * 8796093022208.0f);  // in [0, 2^43]
 }
 
 // histogram bin of a candidate (0 = most likely); monotone non-increasing in x
@@ -158,6 +147,24 @@ __device__ __forceinline__ uint64_t ceil_mass(float p, uint64_t total) {
     const uint64_t lo = pm * total;
     const uint64_t q = (hi << 16) | (lo >> 48);
     return q + ((lo & ((1ull << 48) - 1)) != 0 ? 1 : 0);
+}
+
+// ---------------------------------------------------------------------------------------------
+// exact 64-bit sums in shared memory from native 32-bit atomics
+//
+// A 64-bit shared-memory atomicAdd is not a single native operation on sm_100 and slows down
+// sharply when threads hit the same address; 32-bit adds are native. A split counter keeps the
+// low and high words in separate arrays: the low word wraps, and the one thread whose add wraps
+// it carries one into the high word, so (hi << 32) | lo is the exact sum in any order.
+
+__device__ __forceinline__ void smem_add_split(uint32_t* lo, uint32_t* hi, unsigned long long w) {
+    const uint32_t l = static_cast<uint32_t>(w);
+    const uint32_t old = atomicAdd(lo, l);
+    const uint32_t h = static_cast<uint32_t>(w >> 32) + ((old + l < old) ? 1u : 0u);
+    if (h != 0u) atomicAdd(hi, h);
+}
+__device__ __forceinline__ unsigned long long join_split(uint32_t lo, uint32_t hi) {
+    return (static_cast<unsigned long long>(hi) << 32) | lo;
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -90,7 +90,8 @@ struct ClusterShared {  // written by remote CTAs of the cluster
     double psum[kCMax];              // dense fallback (p_target) partial sums
     unsigned long long rsel;         // refine: composite of the crossing tie (from its owner)
     unsigned int lcnt[kCMax];        // list path: list lengths pushed to CTA 0
-    unsigned int gcnt[2];            // gather buffer counters
+    unsigned int gseg[2][kCMax];     // gather buffers: entries each source CTA wrote (may
+                                     // exceed the segment, which signals an overfull bin)
     int result;                      // token sent to CTA 0 by the dense-residual owner
     int pad;
 };
@@ -101,8 +102,10 @@ struct LocalShared {
     unsigned long long bc[16];  // broadcast scalars
     double bcd[kNW];
     unsigned int lcount;        // local list fill counter
+    unsigned int gfill[2];      // this CTA's fill of its segment in each gather buffer
     unsigned int pad;
     uint64_t mbar[kStages];
+    sixi_smp_params prm;        // the row's parameters (read once from global memory)
 };
 
 struct Layout {
@@ -304,20 +307,25 @@ __device__ __forceinline__ uint32_t warp_reserve(uint32_t n, unsigned int* count
 // Considers entries c with c >= lowb and c != excl. Finds the first entry in descending order at
 // which the running sum (count, or weight when wc != nullptr) reaches `target` (>= 1) and returns
 // it; *cum_through receives the running sum through it. Returns 0 when the target is not reached.
-inline __device__ unsigned long long block_select(const unsigned long long* g, uint32_t n,
+// The entries are held in C segments of `seg` slots: segment q holds cnt[q] entries.
+inline __device__ unsigned long long block_select(const unsigned long long* g, const unsigned int* cnt,
+                                                  uint32_t C, uint32_t seg,
                                                   unsigned long long target, const WeightCtx* wc,
                                                   unsigned long long lowb, unsigned long long excl,
-                                                  uint32_t* bh, unsigned long long* bw,
+                                                  uint32_t* bh, uint32_t* bw,
                                                   LocalShared* ls, unsigned long long* cum_through) {
     const int tid = threadIdx.x;
     unsigned long long andv = ~0ull, orv = 0ull;
     uint32_t cnt_l = 0;
-    for (uint32_t i = tid; i < n; i += kNT) {
-        const unsigned long long c = g[i];
-        if (c < lowb || c == excl) continue;
-        andv &= c;
-        orv |= c;
-        ++cnt_l;
+    for (uint32_t q = 0; q < C; ++q) {
+        const unsigned long long* gq = g + q * seg;
+        for (uint32_t i = tid; i < cnt[q]; i += kNT) {
+            const unsigned long long c = gq[i];
+            if (c < lowb || c == excl) continue;
+            andv &= c;
+            orv |= c;
+            ++cnt_l;
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -364,14 +372,18 @@ inline __device__ unsigned long long block_select(const unsigned long long* g, u
         for (int i = tid; i < 256; i += kNT) {
             bh[i] = 0;
             bw[i] = 0;
+            bw[256 + i] = 0;
         }
         __syncthreads();
-        for (uint32_t i = tid; i < n; i += kNT) {
-            const unsigned long long c = g[i];
-            if (c < lowb || c == excl || (c & pmask) != prefix) continue;
-            const unsigned int d = static_cast<unsigned int>(c >> shift) & (nd - 1u);
-            atomicAdd(&bh[d], 1u);
-            if (wc) atomicAdd(&bw[d], static_cast<unsigned long long>(weight_of(kval(comp_key(c)), *wc)));
+        for (uint32_t q = 0; q < C; ++q) {
+            const unsigned long long* gq = g + q * seg;
+            for (uint32_t i = tid; i < cnt[q]; i += kNT) {
+                const unsigned long long c = gq[i];
+                if (c < lowb || c == excl || (c & pmask) != prefix) continue;
+                const unsigned int d = static_cast<unsigned int>(c >> shift) & (nd - 1u);
+                atomicAdd(&bh[d], 1u);
+                if (wc) smem_add_split(&bw[d], &bw[256 + d], weight_of(kval(comp_key(c)), *wc));
+            }
         }
         __syncthreads();
         if (tid < 32) {
@@ -381,7 +393,7 @@ inline __device__ unsigned long long block_select(const unsigned long long* g, u
             for (int q = 0; q < 8; ++q) {
                 const int d = 255 - (tid * 8 + q);
                 unsigned long long v = 0;
-                if (d < static_cast<int>(nd)) v = wc ? bw[d] : static_cast<unsigned long long>(bh[d]);
+                if (d < static_cast<int>(nd)) v = wc ? join_split(bw[d], bw[256 + d]) : static_cast<unsigned long long>(bh[d]);
                 part[q] = v;
                 lsum += v;
             }
@@ -418,15 +430,18 @@ inline __device__ unsigned long long block_select(const unsigned long long* g, u
             return 0ull;
         }
         base = ls->bc[1];
-        const unsigned long long cnt = ls->bc[2];
+        const unsigned long long dcnt = ls->bc[2];  // entries with the chosen digit
         prefix |= fd << shift;
         pmask |= (static_cast<unsigned long long>(nd) - 1ull) << shift;
         __syncthreads();
-        if (cnt == 1ull || shift == 0) {
-            for (uint32_t i = tid; i < n; i += kNT) {
-                const unsigned long long c = g[i];
-                if (c < lowb || c == excl || (c & pmask) != prefix) continue;
-                ls->bc[3] = c;
+        if (dcnt == 1ull || shift == 0) {
+            for (uint32_t q = 0; q < C; ++q) {
+                const unsigned long long* gq = g + q * seg;
+                for (uint32_t i = tid; i < cnt[q]; i += kNT) {
+                    const unsigned long long c = gq[i];
+                    if (c < lowb || c == excl || (c & pmask) != prefix) continue;
+                    ls->bc[3] = c;
+                }
             }
             __syncthreads();
             const unsigned long long c = ls->bc[3];
@@ -504,10 +519,17 @@ enum Stage : int {
     kStDone = 8
 };
 
+struct GatherReq {  // the bins a round gathers (bB < 0: one bin)
+    int bA, bufA, bB, bufB;
+    unsigned long long lowb;
+};
+
 struct LState {
     int stage;
     int pending_bin;  // bin of the pending selection (-1 none)
-    int pending_kind; // 0 none, 1 gather, 2 exchange, 3 refine
+    int pending_kind; // 0 none, 1 gather, 2 exchange, 3 refine, 4 resolve a prefetched bin now
+    int pre_bin;      // draw bin gathered ahead of time (-1 none) and its buffer
+    int pre_buf;
     unsigned long long target;
     unsigned long long zk, zkept, kbound, xcross, excl, wexcl;
     int32_t result;
@@ -554,9 +576,11 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     float* KF = reinterpret_cast<float*>(dyn + lay.off_k);
     // X
     unsigned long long* MA = reinterpret_cast<unsigned long long*>(dyn + lay.off_x);
-    unsigned long long* H = reinterpret_cast<unsigned long long*>(dyn + lay.off_x);
-    uint32_t* HC = reinterpret_cast<uint32_t*>(dyn + lay.off_x + 8u * kABins);
-    unsigned long long* CG = H;    // H is dead once the segments are reduced
+    uint32_t* HB = reinterpret_cast<uint32_t*>(dyn + lay.off_x);  // weight sums, bits 16..31 parts
+    uint32_t* HA = HB + kABins;                                      // bits 32.. parts
+    uint32_t* HC = HB + 2 * kABins;                                  // counts
+    unsigned long long* CG = reinterpret_cast<unsigned long long*>(dyn + lay.off_x);  // HB/HA are dead
+                                                                                      // once reduced
     uint32_t* CGC = HC;
     // Y
     uint32_t* hb = reinterpret_cast<uint32_t*>(dyn + lay.off_y);
@@ -564,10 +588,12 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     unsigned long long* LL = reinterpret_cast<unsigned long long*>(dyn + lay.off_y);
     unsigned long long* G0 = reinterpret_cast<unsigned long long*>(dyn + lay.off_y);
     unsigned long long* G1 = G0 + kGCap;
+    uint32_t* HLO = reinterpret_cast<uint32_t*>(dyn + lay.off_y);  // weight sums, bits 0..15 parts
     // Z
     uint32_t* H32 = reinterpret_cast<uint32_t*>(dyn + lay.off_z);
     uint32_t* BH = reinterpret_cast<uint32_t*>(dyn + lay.off_z);
     unsigned long long* BW = reinterpret_cast<unsigned long long*>(dyn + lay.off_z + 1024u);
+    uint32_t* BWS = reinterpret_cast<uint32_t*>(dyn + lay.off_z + 1024u);  // block_select's split sums
     // R
     unsigned long long* R = reinterpret_cast<unsigned long long*>(dyn + lay.off_r);
     uint32_t* RC = reinterpret_cast<uint32_t*>(dyn + lay.off_r + 8u * lay.seg);
@@ -604,8 +630,10 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 bulk_g2s(stg + off, gchunk + off, static_cast<uint32_t>(nb), &ls->mbar[s]);
             }
         }
-        cs->gcnt[0] = 0;
-        cs->gcnt[1] = 0;
+        for (int q = 0; q < kCMax; ++q) {
+            cs->gseg[0][q] = 0;
+            cs->gseg[1][q] = 0;
+        }
         cs->result = -1;
         cs->rsel = 0ull;
         ls->bc[15] = 0;
@@ -613,7 +641,12 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     }
 
     const RowCtx rc = make_row_ctx<MODE>(a, row);
-    const sixi_smp_params* P = rc.p;
+    // The parameters are read from a shared copy: through the global pointer every use after a
+    // barrier or a shared-memory store would be a fresh global load (an L2 round trip, as the L1
+    // is mostly carved out for shared memory).
+    if (tid < static_cast<int>(sizeof(sixi_smp_params) / 4))
+        reinterpret_cast<uint32_t*>(&ls->prm)[tid] = reinterpret_cast<const uint32_t*>(rc.p)[tid];
+    const sixi_smp_params* P = &ls->prm;
     const int32_t len = rc.active ? len_load : 0;
     const int nq = (len + 3) >> 2;  // 4-key groups of this chunk
     const int nq_iter = (nq + kNT - 1) / kNT;
@@ -1364,57 +1397,59 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     unsigned long long Z = 0ull, Wmin = 0ull;
     float x_minp = -FLT_MAX;
     const bool need_counts = k_eff < n_allowed;
-    auto xbin_g = [&](uint32_t key) -> int {
-        const float dd = (M - kval(key)) * wc.bin_scale;
-        int b = dd > 0.0f ? static_cast<int>(dd) : 0;
-        return b < kABins - 1 ? b : kABins - 1;
-    };
+    // bins are uniform in t = log2 of the relative weight (the same t the weight is built from)
+    auto xbin_g = [&](uint32_t key) -> int { return abin_of(kval(key), wc); };
     {
         const float m = kval(min_key);
-        double range = static_cast<double>(M) - static_cast<double>(m);
-        const double cap = 46.0 * 0.6931471805599453 * static_cast<double>(P->temperature);
-        if (range > cap) range = cap;
-        make_weight_ctx(P->temperature, M, 46.0f, wc);
-        wc.bin_scale = static_cast<float>((kABins - 1) / (range > 1e-30 ? range : 1e-30));
+        const double range_log2 = (static_cast<double>(M) - static_cast<double>(m)) * 1.4426950408889634 /
+                                  static_cast<double>(P->temperature);
+        make_weight_ctx(P->temperature, M, static_cast<float>(range_log2), wc);  // caps it at 46
         if (P->min_p > 0.0f) {
             x_minp = static_cast<float>(static_cast<double>(M) +
                                         static_cast<double>(P->temperature) * log(static_cast<double>(P->min_p)));
         }
+        // Weight sums in three 32-bit parts, w = a * 2^32 + b * 2^16 + c (a < 2^12, b, c < 2^16): with
+        // at most 2^16 keys per CTA none of the three sums can wrap, so the adds are fire-and-forget.
+        // The c parts use region Y, which no CTA writes to before the third cluster barrier.
         for (int i = tid; i < kABins; i += kNT) {
-            H[i] = 0ull;
+            HB[i] = 0u;
+            HA[i] = 0u;
             HC[i] = 0u;
+            HLO[i] = 0u;
         }
         __syncthreads();
-        unsigned long long zp = 0ull, wp = 0ull;
-        for (int m = 0; m < nq_iter; ++m) {  // 4 keys per iteration: independent chains
+        // min-p prefix mass (only when min-p is set); the row mass Z is read off the assembled
+        // cumulative histogram instead of being summed separately
+        const bool use_minp = P->min_p > 0.0f;
+        unsigned long long wp = 0ull;
+        const int nq8 = (nq + 1) >> 1;
+        const int it8 = (nq8 + kNT - 1) / kNT;
+#pragma unroll 1
+        for (int m = 0; m < it8; ++m) {  // 8 keys per iteration: independent chains
             const int q = tid + m * kNT;
-            if (q >= nq) break;
-            const uint4 v = reinterpret_cast<const uint4*>(K)[q];
-            const uint32_t k4[4] = {v.x, v.y, v.z, v.w};
-            unsigned long long w4[4];
-            int b4[4];
+            if (q >= nq8) break;
+            const uint4 va = reinterpret_cast<const uint4*>(K)[2 * q];
+            const uint4 vb = (2 * q + 1 < nq) ? reinterpret_cast<const uint4*>(K)[2 * q + 1] : make_uint4(0u, 0u, 0u, 0u);
+            const uint32_t k8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {  // branch-free part: weights, bins, sums
-                const uint32_t k = k4[i];
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t k = k8[i];
                 const float x = kval(k);
                 const unsigned long long w = (k != 0u) ? weight_of(x, wc) : 0ull;
-                w4[i] = w;
-                b4[i] = xbin_g(k);
-                zp += w;
-                wp += (x >= x_minp) ? w : 0ull;
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                if (w4[i]) atomicAdd(&H[b4[i]], w4[i]);
-                if (need_counts && k4[i] != 0u) atomicAdd(&HC[b4[i]], 1u);
+                const int b = abin_of(x, wc);
+                if (use_minp) wp += (x >= x_minp) ? w : 0ull;
+                const uint32_t c = static_cast<uint32_t>(w) & 0xFFFFu;
+                const uint32_t bm = static_cast<uint32_t>(w >> 16) & 0xFFFFu;
+                const uint32_t am = static_cast<uint32_t>(w >> 32);
+                if (c != 0u) atomicAdd(&HLO[b], c);
+                if (bm != 0u) atomicAdd(&HB[b], bm);
+                if (am != 0u) atomicAdd(&HA[b], am);
+                if (need_counts && k != 0u) atomicAdd(&HC[b], 1u);
             }
         }
-        zp = block_sum_u64<kNT>(zp, ls->red);
-        wp = block_sum_u64<kNT>(wp, ls->red);
-        if (tid < static_cast<int>(C)) {
-            ClusterShared* dst = cluster.map_shared_rank(cs, tid);
-            dst->z[crank] = zp;
-            dst->wmin[crank] = wp;
+        if (use_minp) {
+            wp = block_sum_u64<kNT>(wp, ls->red);
+            if (tid < static_cast<int>(C)) cluster.map_shared_rank(cs, tid)->wmin[crank] = wp;
         }
     }
 
@@ -1425,37 +1460,69 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         unsigned long long s = 0ull;
         uint32_t sc = 0;
         for (uint32_t q = 0; q < C; ++q) {
-            s += cluster.map_shared_rank(H, q)[crank * lay.seg + i];
+            const uint32_t j = crank * lay.seg + i;
+            s += (static_cast<unsigned long long>(cluster.map_shared_rank(HA, q)[j]) << 32) +
+                 (static_cast<unsigned long long>(cluster.map_shared_rank(HB, q)[j]) << 16) +
+                 cluster.map_shared_rank(HLO, q)[j];
             if (need_counts) sc += cluster.map_shared_rank(HC, q)[crank * lay.seg + i];
         }
         R[i] = s;
         RC[i] = sc;
     }
-    for (uint32_t q = 0; q < C; ++q) {
-        Z += cs->z[q];
-        Wmin += cs->wmin[q];
+    if (P->min_p > 0.0f) {
+        for (uint32_t q = 0; q < C; ++q) Wmin += cs->wmin[q];
     }
 
     cluster.sync();  // ======================================================== CS3
 
-    // keys of bin b form the interval [lo, hi] (the bin index is non-increasing in the key);
-    // found by binary search over the valid keys [min_key, max key]
-    const uint32_t kmax_valid = comp_key(best);
-    auto bin_key_range = [&](int b, uint32_t* lo_out, uint32_t* hi_out) {
-        uint32_t lo = min_key, hi = kmax_valid;  // smallest key with bin <= b
+    // smallest key in [lo, hi] whose bin is <= bb, or hi + 1 when there is none: a 32-way search
+    // run by every warp (the bin index is non-increasing in the key)
+    auto first_key_bin_le = [&](int bb, uint32_t lo, uint32_t hi) -> unsigned long long {
+        const uint32_t hi0 = hi;
         while (lo < hi) {
-            const uint32_t mid = lo + ((hi - lo) >> 1);
-            if (xbin_g(mid) <= b) hi = mid;
-            else lo = mid + 1;
+            const uint32_t step = (hi - lo) / 31u + 1u;  // the last probe reaches hi
+            const unsigned long long pr = static_cast<unsigned long long>(lo) +
+                                          static_cast<unsigned long long>(lane) * step;
+            const uint32_t probe = pr > hi ? hi : static_cast<uint32_t>(pr);
+            const unsigned ball = __ballot_sync(0xFFFFFFFFu, xbin_g(probe) <= bb);
+            if (ball == 0u) return static_cast<unsigned long long>(hi0) + 1ull;  // only on the first pass
+            const int f = __ffs(ball) - 1;
+            const uint32_t pf = __shfl_sync(0xFFFFFFFFu, probe, f);
+            const uint32_t pp = __shfl_sync(0xFFFFFFFFu, probe, f > 0 ? f - 1 : 0);
+            hi = pf;
+            if (f > 0) lo = pp + 1u;
         }
-        *lo_out = lo;
-        uint32_t lo2 = min_key, hi2 = kmax_valid;  // largest key with bin >= b
-        while (lo2 < hi2) {
-            const uint32_t mid = lo2 + ((hi2 - lo2 + 1) >> 1);
-            if (xbin_g(mid) >= b) lo2 = mid;
-            else hi2 = mid - 1;
+        return (xbin_g(lo) <= bb) ? lo : static_cast<unsigned long long>(hi0) + 1ull;
+    };
+    // Keys of bin b form the interval [lo, hi] of the valid keys [min_key, max key]. Block-wide
+    // (all threads call): warps 0-3 run the four searches of bins bA and bB (bB < 0: none) at
+    // once; r receives loA, hiA, loB, hiB (an empty interval for a missing bB).
+    const uint32_t kmax_valid = comp_key(best);
+    auto bin_ranges = [&](int bA, int bB, uint32_t* r) {
+        const int w = tid >> 5;
+        if (w < 4 && (w < 2 || bB >= 0)) {
+            const int bb = (w < 2 ? bA : bB) - (w & 1);  // odd warps: first key past the bin
+            const unsigned long long f = first_key_bin_le(bb, min_key, kmax_valid);
+            if (lane == 0) ls->bc[4 + w] = f;
         }
-        *hi_out = lo2;
+        __syncthreads();
+#pragma unroll 1
+        for (int j = 0; j < 2; ++j) {
+            uint32_t lo = 1u, hi = 0u;
+            if (j == 0 || bB >= 0) {
+                const unsigned long long ft = ls->bc[4 + 2 * j], ff = ls->bc[5 + 2 * j];
+                lo = ft > kmax_valid ? kmax_valid : static_cast<uint32_t>(ft);
+                hi = ff > kmax_valid ? kmax_valid : (ff == min_key ? min_key : static_cast<uint32_t>(ff - 1ull));
+            }
+            if (j == 0) {
+                r[0] = lo;
+                r[1] = hi;
+            } else {
+                r[2] = lo;
+                r[3] = hi;
+            }
+        }
+        __syncthreads();  // bc[4..7] may be rewritten by the next call
     };
     auto bin_of_target = [&](unsigned long long t) -> int {  // first bin with CG >= t
         int lo = 0, hi = kABins - 1;
@@ -1466,37 +1533,58 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         }
         return lo;
     };
-    // push my entries of bin b (composite >= lowb) into gather buffer gbuf of every CTA
-    auto gather = [&](int b, int gbuf, unsigned long long lowb) {
-        unsigned long long* gb = gbuf ? G1 : G0;
-        uint32_t klo, khi;
-        bin_key_range(b, &klo, &khi);
+    // Pushes my entries of bin bA (and of bin bB when bB >= 0) whose composite is >= lowb into my
+    // segment of gather buffer bufA (bufB) in every CTA of the cluster, then publishes how many I
+    // have (a count above the segment size marks the bin overfull). Slots come from a local
+    // counter, so the remote traffic is plain stores.
+    const uint32_t gseg = static_cast<uint32_t>(kGCap) / C;
+    auto gather = [&](int bA, int bufA, int bB, int bufB, unsigned long long lowb) {
+        uint32_t kr[4];
+        bin_ranges(bA, bB, kr);
+        unsigned long long* gA = (bufA ? G1 : G0) + crank * gseg;
+        unsigned long long* gB = (bufB ? G1 : G0) + crank * gseg;
+        if (tid == 0) {
+            ls->gfill[0] = 0u;
+            ls->gfill[1] = 0u;
+        }
+        __syncthreads();
+#pragma unroll 1
         for (int m = 0; m < nq_iter; ++m) {  // warp-uniform trip count
             const int q = tid + m * kNT;
             uint4 v = make_uint4(0u, 0u, 0u, 0u);
             if (q < nq) v = reinterpret_cast<const uint4*>(K)[q];
             const uint32_t k4[4] = {v.x, v.y, v.z, v.w};
-            uint32_t c = 0;
+            uint32_t mA = 0u, mB = 0u;  // membership bits of the four keys
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                c += (k4[i] >= klo && k4[i] <= khi && comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i)) >= lowb) ? 1u : 0u;
-            if (__ballot_sync(0xFFFFFFFFu, c != 0u) == 0u) continue;
-            const uint32_t incl = warp_incl_u32(c);
-            const uint32_t total = __shfl_sync(0xFFFFFFFFu, incl, 31);
-            for (uint32_t dst = 0; dst < C; ++dst) {
-                uint32_t basei = 0;
-                if (lane == 31) basei = atomicAdd(&cluster.map_shared_rank(cs, dst)->gcnt[gbuf], total);
-                basei = __shfl_sync(0xFFFFFFFFu, basei, 31) + incl - c;
-                unsigned long long* rg = cluster.map_shared_rank(gb, dst);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const unsigned long long cp = comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i));
-                    if (k4[i] >= klo && k4[i] <= khi && cp >= lowb) {
-                        if (basei < static_cast<uint32_t>(kGCap)) rg[basei] = cp;
-                        ++basei;
+            for (int i = 0; i < 4; ++i) {
+                const bool ok = comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i)) >= lowb;
+                mA |= (ok && k4[i] >= kr[0] && k4[i] <= kr[1]) ? (1u << i) : 0u;
+                mB |= (ok && k4[i] >= kr[2] && k4[i] <= kr[3]) ? (1u << i) : 0u;
+            }
+            if (__ballot_sync(0xFFFFFFFFu, (mA | mB) != 0u) == 0u) continue;
+#pragma unroll 1
+            for (int gsel = 0; gsel < 2; ++gsel) {
+                uint32_t mk = gsel ? mB : mA;
+                if (__ballot_sync(0xFFFFFFFFu, mk != 0u) == 0u) continue;
+                uint32_t pos = warp_reserve(static_cast<uint32_t>(__popc(mk)), &ls->gfill[gsel]);
+                unsigned long long* gdst = gsel ? gB : gA;
+                while (mk != 0u) {
+                    const int e = 4 * q + __ffs(mk) - 1;
+                    mk &= mk - 1u;
+                    const unsigned long long cp = comp_of(K[e], static_cast<uint32_t>(c0 + e));
+                    if (pos < gseg) {
+#pragma unroll 1
+                        for (uint32_t dst = 0; dst < C; ++dst) cluster.map_shared_rank(gdst, dst)[pos] = cp;
                     }
+                    ++pos;
                 }
             }
+        }
+        __syncthreads();
+        if (tid < static_cast<int>(C)) {
+            ClusterShared* d = cluster.map_shared_rank(cs, tid);
+            d->gseg[bufA][crank] = ls->gfill[0];
+            if (bB >= 0) d->gseg[bufB][crank] = ls->gfill[1];
         }
     };
 
@@ -1542,10 +1630,15 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     // The state below is advanced identically in every CTA of the cluster: every decision reads
     // only cluster-uniform data (exchanged statistics, the assembled histograms, gathered sets,
     // pushed partial results), so the loop's early exit is uniform within the cluster.
+    Z = CG[kABins - 1];  // every positive weight lies in some bin
+    // rows whose kept set is followed directly by a draw (sampled rows, the verifier's bonus rows)
+    const bool draw_follows = (MODE == kModeSample) || (MODE == kModeVerify && rc.vrole == 1);
     LState st{};
     st.stage = need_counts ? kStKBound : kStTopP;
     st.pending_bin = -1;
     st.pending_kind = 0;
+    st.pre_bin = -1;
+    st.pre_buf = 0;
     st.result = -1;
     st.err = 0;
     st.zk = Z;
@@ -1558,7 +1651,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     // refine digit histograms (double-buffered) in region R: the reduced segments there are last
     // read remotely in the assembly above, at least one barrier before the first refine level
     uint32_t* RH[2] = {reinterpret_cast<uint32_t*>(R), reinterpret_cast<uint32_t*>(R) + 256};
-    unsigned long long* RW[2] = {R + 256, R + 512};
+    uint32_t* RW[2] = {reinterpret_cast<uint32_t*>(R + 256), reinterpret_cast<uint32_t*>(R + 512)};  // split
 
     auto rf_match = [&](int e, uint32_t k) -> bool {
         if (k < rf.klo || k > rf.khi || (k & rf.pmask) != rf.prefix) return false;
@@ -1568,7 +1661,8 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     auto rf_build = [&](int buf) {  // local digit histogram of the refine level
         for (int i = tid; i < 256; i += kNT) {
             RH[buf][i] = 0u;
-            RW[buf][i] = 0ull;
+            RW[buf][i] = 0u;
+            RW[buf][256 + i] = 0u;
         }
         __syncthreads();
         for (int e = tid; e < len; e += kNT) {
@@ -1576,7 +1670,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             if (!rf_match(e, k)) continue;
             const uint32_t d = (k >> rf.shift) & ((1u << rf.width) - 1u);
             atomicAdd(&RH[buf][d], 1u);
-            atomicAdd(&RW[buf][d], static_cast<unsigned long long>(weight_of(kval(k), wc)));
+            smem_add_split(&RW[buf][d], &RW[buf][256 + d], weight_of(kval(k), wc));
         }
         __syncthreads();
     };
@@ -1591,16 +1685,25 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         if (st.stage == kStDone || st.err) break;
         const int cur = round & 1;
         const int prev = cur ^ 1;
+        bool read_buf = false;  // a gather buffer was read in this round
+        // a second pass runs only when the draw bin was gathered ahead of time (pending_kind 4)
+#pragma unroll 1
+        for (int pass = 0; pass < 3; ++pass) {
         bool have_sel = false;
         unsigned long long sel = 0ull, cum_sel = 0ull, wthrough = 0ull;
         const int sel_bin = st.pending_bin;
         // ------------------------------------------------ resolve what the previous round started
-        if (st.pending_kind == 1) {
-            const uint32_t n = cs->gcnt[prev];
+        if (st.pending_kind == 1 || st.pending_kind == 4) {
+            const int gbuf = (st.pending_kind == 4) ? st.pre_buf : prev;
+            if (st.pending_kind == 4) st.pre_bin = -1;
+            const unsigned int* gcn = cs->gseg[gbuf];
+            bool over = false;
+            for (uint32_t q = 0; q < C; ++q) over |= gcn[q] > gseg;
             const unsigned long long lowb = (st.stage == kStKBound) ? 0ull : st.kbound;
             const unsigned long long ex = (st.stage == kStResid) ? st.excl : 0ull;
             const bool cmode = (st.stage == kStKBound);
-            if (n > static_cast<uint32_t>(kGCap)) {
+            read_buf = true;
+            if (over) {
                 // the bin is too full to gather: refine it by key digits across the cluster
                 rf.active = 1;
                 rf.phase = 0;
@@ -1614,7 +1717,12 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 rf.above_c = 0ull;
                 rf.above_w = 0ull;
                 rf.buf = 0;
-                bin_key_range(rf.bin, &rf.klo, &rf.khi);
+                {
+                    uint32_t kr[4];
+                    bin_ranges(rf.bin, -1, kr);
+                    rf.klo = kr[0];
+                    rf.khi = kr[1];
+                }
                 uint32_t lo = 0xFFFFFFFFu, hi = 0u;
                 for (int e = tid; e < len; e += kNT) {
                     const uint32_t k = K[e];
@@ -1627,17 +1735,20 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 if (tid < static_cast<int>(C)) cluster.map_shared_rank(cs, tid)->mm[crank] = (l2 << 32) | h2;
                 st.pending_kind = 3;
             } else {
-                const unsigned long long* gp = prev ? G1 : G0;
-                sel = block_select(gp, n, st.target, cmode ? nullptr : &wc, lowb, ex, BH, BW, ls, &cum_sel);
+                const unsigned long long* gp = gbuf ? G1 : G0;
+                sel = block_select(gp, gcn, C, gseg, st.target, cmode ? nullptr : &wc, lowb, ex, BH, BWS, ls,
+                                   &cum_sel);
                 if (sel == 0ull) {
                     st.err = 2;
                 } else {
                     have_sel = true;
                     if (cmode) {
                         unsigned long long wpart = 0ull;
-                        for (uint32_t i = tid; i < n; i += kNT) {
-                            const unsigned long long c = gp[i];
-                            if (c >= sel) wpart += weight_of(kval(comp_key(c)), wc);
+                        for (uint32_t q = 0; q < C; ++q) {
+                            for (uint32_t i = tid; i < gcn[q]; i += kNT) {
+                                const unsigned long long c = gp[q * gseg + i];
+                                if (c >= sel) wpart += weight_of(kval(comp_key(c)), wc);
+                            }
                         }
                         wthrough = block_sum_u64<kNT>(wpart, ls->red);
                     }
@@ -1645,7 +1756,6 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 st.pending_kind = 0;
             }
             __syncthreads();
-            if (tid == 0) cs->gcnt[prev] = 0u;  // refilled two rounds later, after a barrier
         } else if (st.pending_kind == 3) {
             if (rf.phase == 0) {
                 uint32_t klo = 0xFFFFFFFFu, khi = 0u;
@@ -1674,7 +1784,8 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                     unsigned long long sc = 0ull, sw = 0ull;
                     for (uint32_t q = 0; q < C; ++q) {
                         sc += cluster.map_shared_rank(RH[rf.buf], q)[tid];
-                        sw += cluster.map_shared_rank(RW[rf.buf], q)[tid];
+                        const uint32_t* rw = cluster.map_shared_rank(RW[rf.buf], q);
+                        sw += join_split(rw[tid], rw[256 + tid]);
                     }
                     BH[tid] = static_cast<uint32_t>(sc);
                     BW[tid] = sw;
@@ -1927,6 +2038,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             st.pending_bin = -1;
         }
         // ------------------------------------------------ advance stages and issue the next exchange
+        GatherReq gq{-1, 0, -1, 0, 0ull};
         while (!st.err && st.stage != kStDone && st.pending_kind == 0) {
             if (st.stage == kStKBound) {
                 const unsigned long long t = k_eff;
@@ -1939,7 +2051,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 st.target = t - (lo > 0 ? CGC[lo - 1] : 0u);
                 st.pending_bin = lo;
                 st.pending_kind = 1;
-                gather(lo, cur, 0ull);
+                gq = GatherReq{lo, cur, -1, 0, 0ull};
             } else if (st.stage == kStTopP) {
                 if (P->top_p > 0.0f && P->top_p < 1.0f) {
                     unsigned long long t1 = ceil_mass(P->top_p, st.zk);
@@ -1948,7 +2060,33 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                     st.target = t1 - (b > 0 ? CG[b - 1] : 0ull);
                     st.pending_bin = b;
                     st.pending_kind = 1;
-                    gather(b, cur, st.kbound);
+                    // The kept mass will lie in [CG[b-1] + 1, CG[b]] (min-p can only lower it). When
+                    // both ends put the draw in the same bin, that bin is gathered now as well, into
+                    // the other buffer (free: nothing was read from it in this round).
+                    int b2 = -1;
+                    if (draw_follows && !read_buf) {
+                        unsigned long long zlo = (b > 0 ? CG[b - 1] : 0ull) + 1ull, zhi = CG[b];
+                        if (P->min_p > 0.0f) {
+                            zlo = zlo < Wmin ? zlo : Wmin;
+                            zhi = zhi < Wmin ? zhi : Wmin;
+                        }
+                        if (zlo > 0ull) {
+                            const int blo = bin_of_target(scale_mass(rc.u_draw, zlo) + 1ull);
+                            const int bhi = bin_of_target(scale_mass(rc.u_draw, zhi) + 1ull);
+                            if (blo == bhi) b2 = blo;
+                        }
+                    }
+                    if (b2 >= 0 && b2 != b) {
+                        gq = GatherReq{b, cur, b2, prev, st.kbound};
+                        st.pre_bin = b2;
+                        st.pre_buf = prev;
+                    } else {
+                        gq = GatherReq{b, cur, -1, 0, st.kbound};
+                        if (b2 == b) {
+                            st.pre_bin = b;
+                            st.pre_buf = cur;
+                        }
+                    }
                 } else {
                     st.zkept = st.zk;
                     st.stage = kStKept;
@@ -2033,7 +2171,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                                 st.stage = kStResid;
                                 st.pending_bin = lo;
                                 st.pending_kind = 1;
-                                gather(lo, cur, st.kbound);
+                                gq = GatherReq{lo, cur, -1, 0, st.kbound};
                             } else {
                                 st.stage = kStDraw;  // residual empty: draw from the kept set
                             }
@@ -2047,13 +2185,30 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 const int b = bin_of_target(t);
                 st.target = t - (b > 0 ? CG[b - 1] : 0ull);
                 st.pending_bin = b;
-                st.pending_kind = 1;
-                gather(b, cur, st.kbound);
+                if (b == st.pre_bin) {
+                    st.pending_kind = 4;  // gathered with the top-p bin: resolve it in this round
+                } else if (read_buf && st.pre_bin >= 0) {
+                    // unreachable when the prediction holds; the prefetch buffer may still be read
+                    // by this round's resolution, so the gather waits for the next round
+                    st.pre_bin = -1;
+                    st.pending_kind = 5;
+                } else {
+                    st.pre_bin = -1;
+                    st.pending_kind = 1;
+                    gq = GatherReq{b, cur, -1, 0, st.kbound};
+                }
             } else {
                 st.err = 4;
             }
         }
+        if (gq.bA >= 0) gather(gq.bA, gq.bufA, gq.bB, gq.bufB, gq.lowb);  // the one gather site
+        if (st.pending_kind != 4) break;
+        }  // pass
         cluster.sync();  // ============================================ one barrier per round
+        if (st.pending_kind == 5) {  // deferred draw gather (see kStDraw)
+            st.pending_kind = 0;
+            st.stage = kStDraw;
+        }
     }
     if (st.stage != kStDone && !st.err) st.err = 5;
 

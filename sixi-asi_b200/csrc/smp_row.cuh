@@ -303,18 +303,90 @@ __device__ __forceinline__ uint32_t warp_reserve(uint32_t n, unsigned int* count
 }
 
 // ---------------------------------------------------------------------------------------------
+// The selection below for at most kNT entries in total (block-wide, all threads call): one entry
+// per thread, compacted; its rank is the number of larger entries (a broadcast scan of the list);
+// the entries are scattered into descending order and one block prefix sum of their weights finds
+// the crossing. `hz` is 8 KB of scratch. Same contract as block_select.
+__device__ __forceinline__ unsigned long long block_select_small(const unsigned long long* g, const unsigned int* cnt,
+                                                                uint32_t C, uint32_t seg,
+                                                                unsigned long long target, const WeightCtx wc,
+                                                                bool weighted, unsigned long long lowb,
+                                                                unsigned long long excl, uint32_t* hz,
+                                                                LocalShared* ls, unsigned long long* cum_through) {
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    unsigned long long* L = reinterpret_cast<unsigned long long*>(hz);  // entries, then in order
+    unsigned long long* W = L + kNT;                                    // their weights
+    unsigned long long e = 0ull;
+    bool valid = false;
+    {
+        uint32_t t = static_cast<uint32_t>(tid), q = 0;
+        for (; q < C; ++q) {
+            if (t < cnt[q]) break;
+            t -= cnt[q];
+        }
+        if (q < C) {
+            e = g[q * seg + t];
+            valid = e >= lowb && e != excl;
+        }
+    }
+    uint32_t n = 0;
+    const uint32_t pos = block_excl_u32<kNT>(valid ? 1u : 0u, ls->red32, &n);
+    const unsigned long long we = valid ? (weighted ? weight_of(kval(comp_key(e)), wc) : 1ull) : 0ull;
+    if (valid) {
+        L[pos] = e;
+        W[pos] = we;
+    }
+    if (tid == 0) ls->bc[3] = 0ull;
+    __syncthreads();
+    uint32_t rank = 0;  // entries are unique: rank = number of larger entries
+    if (valid) {
+        for (uint32_t j = 0; j < n; ++j) rank += L[j] > e ? 1u : 0u;
+    }
+    __syncthreads();
+    if (valid) {
+        L[rank] = e;
+        W[rank] = we;
+    }
+    __syncthreads();
+    const unsigned long long ws = (static_cast<uint32_t>(tid) < n) ? W[tid] : 0ull;
+    const unsigned long long inc = warp_incl_u64(ws);
+    if (lane == 31) ls->red[w] = inc;
+    __syncthreads();
+    unsigned long long cum = inc;
+    for (int i = 0; i < w; ++i) cum += ls->red[i];
+    if (static_cast<uint32_t>(tid) < n && ws > 0ull && cum >= target && cum - ws < target) {
+        ls->bc[3] = L[tid];  // the one entry whose prefix first reaches the target
+        ls->bc[4] = cum;
+    }
+    __syncthreads();
+    const unsigned long long sel = ls->bc[3];
+    *cum_through = sel ? ls->bc[4] : 0ull;
+    __syncthreads();  // ls->red and ls->bc are free again
+    return sel;
+}
+
+// ---------------------------------------------------------------------------------------------
 // Exact selection over a shared-memory array of unique composites (block-wide, all threads call).
 // Considers entries c with c >= lowb and c != excl. Finds the first entry in descending order at
-// which the running sum (count, or weight when wc != nullptr) reaches `target` (>= 1) and returns
+// which the running sum (count, or weight when `weighted`) reaches `target` (>= 1) and returns
 // it; *cum_through receives the running sum through it. Returns 0 when the target is not reached.
 // The entries are held in C segments of `seg` slots: segment q holds cnt[q] entries.
-inline __device__ unsigned long long block_select(const unsigned long long* g, const unsigned int* cnt,
+// Radix select over 8-bit digits below the entries' common prefix. `hz` is 2 x 1024 words of
+// scratch: per level a digit histogram of counts and of weights in three 16/16/32-bit parts (at
+// most 1536 entries, so no part can wrap), double-buffered so that a level needs two barriers.
+__device__ __forceinline__ unsigned long long block_select(const unsigned long long* g, const unsigned int* cnt,
                                                   uint32_t C, uint32_t seg,
-                                                  unsigned long long target, const WeightCtx* wc,
+                                                  unsigned long long target, const WeightCtx wc, bool weighted,
                                                   unsigned long long lowb, unsigned long long excl,
-                                                  uint32_t* bh, uint32_t* bw,
-                                                  LocalShared* ls, unsigned long long* cum_through) {
+                                                  uint32_t* hz, LocalShared* ls, unsigned long long* cum_through) {
     const int tid = threadIdx.x;
+    {
+        uint32_t total = 0;
+        for (uint32_t q = 0; q < C; ++q) total += cnt[q];
+        if (total <= static_cast<uint32_t>(kNT))
+            return block_select_small(g, cnt, C, seg, target, wc, weighted, lowb, excl, hz, ls, cum_through);
+    }
+    for (int i = tid; i < 1024; i += kNT) hz[i] = 0u;  // level-0 buffer
     unsigned long long andv = ~0ull, orv = 0ull;
     uint32_t cnt_l = 0;
     for (uint32_t q = 0; q < C; ++q) {
@@ -333,7 +405,7 @@ inline __device__ unsigned long long block_select(const unsigned long long* g, c
         orv |= __shfl_xor_sync(0xFFFFFFFFu, orv, o);
     }
     cnt_l = warp_sum_u32(cnt_l);
-    __syncthreads();
+    __syncthreads();  // earlier readers of ls->red are done
     if ((tid & 31) == 0) {
         ls->red[tid >> 5] = andv;
         ls->red[kNW + (tid >> 5)] = orv;
@@ -349,11 +421,11 @@ inline __device__ unsigned long long block_select(const unsigned long long* g, c
         orv |= ls->red[kNW + w];
         ncons += ls->red[2 * kNW + w];
     }
-    __syncthreads();
+    __syncthreads();  // ls->red is free again
     *cum_through = 0;
     if (ncons == 0) return 0ull;
     if (ncons == 1) {
-        const unsigned long long w = wc ? weight_of(kval(comp_key(andv)), *wc) : 1ull;
+        const unsigned long long w = weighted ? weight_of(kval(comp_key(andv)), wc) : 1ull;
         if (w >= target && w > 0) {
             *cum_through = w;
             return andv;
@@ -365,16 +437,15 @@ inline __device__ unsigned long long block_select(const unsigned long long* g, c
     unsigned long long pmask = (top == 63) ? 0ull : ~((2ull << top) - 1ull);
     unsigned long long prefix = andv & pmask;
     unsigned long long base = 0;
+#pragma unroll 1
     for (int level = 0; level < 9 && top >= 0; ++level) {
+        const int buf = level & 1;
+        uint32_t* bh = hz + buf * 1024;  // counts, then weight parts c, b, a
+        uint32_t* nxt = hz + (buf ^ 1) * 1024;
         const int shift = top - 7 > 0 ? top - 7 : 0;
         const int width = top - shift + 1;
         const unsigned int nd = 1u << width;
-        for (int i = tid; i < 256; i += kNT) {
-            bh[i] = 0;
-            bw[i] = 0;
-            bw[256 + i] = 0;
-        }
-        __syncthreads();
+        for (int i = tid; i < 1024; i += kNT) nxt[i] = 0u;  // read last in the previous level
         for (uint32_t q = 0; q < C; ++q) {
             const unsigned long long* gq = g + q * seg;
             for (uint32_t i = tid; i < cnt[q]; i += kNT) {
@@ -382,10 +453,19 @@ inline __device__ unsigned long long block_select(const unsigned long long* g, c
                 if (c < lowb || c == excl || (c & pmask) != prefix) continue;
                 const unsigned int d = static_cast<unsigned int>(c >> shift) & (nd - 1u);
                 atomicAdd(&bh[d], 1u);
-                if (wc) smem_add_split(&bw[d], &bw[256 + d], weight_of(kval(comp_key(c)), *wc));
+                if (weighted) {
+                    const unsigned long long w = weight_of(kval(comp_key(c)), wc);
+                    const uint32_t wc0 = static_cast<uint32_t>(w) & 0xFFFFu;
+                    const uint32_t wb = static_cast<uint32_t>(w >> 16) & 0xFFFFu;
+                    const uint32_t wa = static_cast<uint32_t>(w >> 32);
+                    if (wc0 != 0u) atomicAdd(&bh[256 + d], wc0);
+                    if (wb != 0u) atomicAdd(&bh[512 + d], wb);
+                    if (wa != 0u) atomicAdd(&bh[768 + d], wa);
+                }
             }
         }
         __syncthreads();
+        unsigned long long* bco = ls->bc + (buf ? 5 : 0);  // double-buffered broadcast slots
         if (tid < 32) {
             unsigned long long part[8];
             unsigned long long lsum = 0;
@@ -393,7 +473,11 @@ inline __device__ unsigned long long block_select(const unsigned long long* g, c
             for (int q = 0; q < 8; ++q) {
                 const int d = 255 - (tid * 8 + q);
                 unsigned long long v = 0;
-                if (d < static_cast<int>(nd)) v = wc ? join_split(bw[d], bw[256 + d]) : static_cast<unsigned long long>(bh[d]);
+                if (d < static_cast<int>(nd)) {
+                    v = weighted ? (static_cast<unsigned long long>(bh[768 + d]) << 32) +
+                                 (static_cast<unsigned long long>(bh[512 + d]) << 16) + bh[256 + d]
+                           : static_cast<unsigned long long>(bh[d]);
+                }
                 part[q] = v;
                 lsum += v;
             }
@@ -415,25 +499,21 @@ inline __device__ unsigned long long block_select(const unsigned long long* g, c
                 const int fd = __shfl_sync(0xFFFFFFFFu, found, src);
                 const unsigned long long ab = __shfl_sync(0xFFFFFFFFu, above, src);
                 if (tid == 0) {
-                    ls->bc[0] = static_cast<unsigned long long>(fd);
-                    ls->bc[1] = ab;
-                    ls->bc[2] = bh[fd];
+                    bco[0] = static_cast<unsigned long long>(fd);
+                    bco[1] = ab;
+                    bco[2] = bh[fd];
                 }
             } else if (tid == 0) {
-                ls->bc[0] = ~0ull;
+                bco[0] = ~0ull;
             }
         }
         __syncthreads();
-        const unsigned long long fd = ls->bc[0];
-        if (fd == ~0ull) {
-            __syncthreads();
-            return 0ull;
-        }
-        base = ls->bc[1];
-        const unsigned long long dcnt = ls->bc[2];  // entries with the chosen digit
+        const unsigned long long fd = bco[0];
+        if (fd == ~0ull) return 0ull;
+        base = bco[1];
+        const unsigned long long dcnt = bco[2];  // entries with the chosen digit
         prefix |= fd << shift;
         pmask |= (static_cast<unsigned long long>(nd) - 1ull) << shift;
-        __syncthreads();
         if (dcnt == 1ull || shift == 0) {
             for (uint32_t q = 0; q < C; ++q) {
                 const unsigned long long* gq = g + q * seg;
@@ -445,8 +525,7 @@ inline __device__ unsigned long long block_select(const unsigned long long* g, c
             }
             __syncthreads();
             const unsigned long long c = ls->bc[3];
-            __syncthreads();
-            const unsigned long long w = wc ? weight_of(kval(comp_key(c)), *wc) : 1ull;
+            const unsigned long long w = weighted ? weight_of(kval(comp_key(c)), wc) : 1ull;
             *cum_through = base + w;
             return c;
         }
@@ -519,17 +598,20 @@ enum Stage : int {
     kStDone = 8
 };
 
-struct GatherReq {  // the bins a round gathers (bB < 0: one bin)
-    int bA, bufA, bB, bufB;
+struct GatherReq {  // the bins a round gathers: bin bA, and bins bBlo..bBhi (bBlo < 0: none)
+    int bA, bufA, bBlo, bBhi, bufB;
     unsigned long long lowb;
 };
+
+constexpr int kPreBins = 4;  // widest bin range gathered ahead of time for the draw
 
 struct LState {
     int stage;
     int pending_bin;  // bin of the pending selection (-1 none)
     int pending_kind; // 0 none, 1 gather, 2 exchange, 3 refine, 4 resolve a prefetched bin now
-    int pre_bin;      // draw bin gathered ahead of time (-1 none) and its buffer
-    int pre_buf;
+    int pre_lo, pre_hi;  // bins gathered ahead of time for the draw (pre_lo < 0: none), and their
+    int pre_buf;         // buffer
+    unsigned long long tabs;  // the draw's target as a cumulative mass from the top
     unsigned long long target;
     unsigned long long zk, zkept, kbound, xcross, excl, wexcl;
     int32_t result;
@@ -550,10 +632,48 @@ struct Refine {
     int top, shift, width;
     unsigned long long above_c, above_w, tie_w;
     int buf;
-    uint32_t klo, khi;  // key interval of the bin
 };
 
 // ---------------------------------------------------------------------------------------------
+
+// The mass-path histogram pass (block-wide): fixed-point weights of the keys K[0, 4 * nq) in three
+// 32-bit parts, w = a * 2^32 + b * 2^16 + c (a < 2^12, b, c < 2^16): with at most 2^16 keys per
+// CTA none of the part sums can wrap, so the adds are fire-and-forget. Returns this thread's
+// share of the min-p prefix mass (keys >= x_minp) when use_minp. Kept out of line so that the
+// loop is scheduled with the whole register budget.
+static __device__ __noinline__ unsigned long long mass_histogram(const uint32_t* K, int nq, const WeightCtx wc,
+                                                          float x_minp, bool use_minp, bool need_counts,
+                                                          uint32_t* HLO, uint32_t* HB, uint32_t* HA,
+                                                          uint32_t* HC) {
+    const int tid = threadIdx.x;
+    unsigned long long wp = 0ull;
+    const int nq8 = (nq + 1) >> 1;
+    const int it8 = (nq8 + kNT - 1) / kNT;
+#pragma unroll 1
+    for (int m = 0; m < it8; ++m) {  // 8 keys per iteration: independent chains
+        const int q = tid + m * kNT;
+        if (q >= nq8) break;
+        const uint4 va = reinterpret_cast<const uint4*>(K)[2 * q];
+        const uint4 vb = (2 * q + 1 < nq) ? reinterpret_cast<const uint4*>(K)[2 * q + 1] : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t k8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t k = k8[i];
+            const float x = kval(k);
+            const unsigned long long w = (k != 0u) ? weight_of(x, wc) : 0ull;
+            const int b = abin_of(x, wc);
+            if (use_minp) wp += (x >= x_minp) ? w : 0ull;
+            const uint32_t c = static_cast<uint32_t>(w) & 0xFFFFu;
+            const uint32_t bm = static_cast<uint32_t>(w >> 16) & 0xFFFFu;
+            const uint32_t am = static_cast<uint32_t>(w >> 32);
+            if (c != 0u) atomicAdd(&HLO[b], c);
+            if (bm != 0u) atomicAdd(&HB[b], bm);
+            if (am != 0u) atomicAdd(&HA[b], am);
+            if (need_counts && k != 0u) atomicAdd(&HC[b], 1u);
+        }
+    }
+    return wp;
+}
 
 template <int DT, int MODE>
 __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
@@ -593,7 +713,6 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     uint32_t* H32 = reinterpret_cast<uint32_t*>(dyn + lay.off_z);
     uint32_t* BH = reinterpret_cast<uint32_t*>(dyn + lay.off_z);
     unsigned long long* BW = reinterpret_cast<unsigned long long*>(dyn + lay.off_z + 1024u);
-    uint32_t* BWS = reinterpret_cast<uint32_t*>(dyn + lay.off_z + 1024u);  // block_select's split sums
     // R
     unsigned long long* R = reinterpret_cast<unsigned long long*>(dyn + lay.off_r);
     uint32_t* RC = reinterpret_cast<uint32_t*>(dyn + lay.off_r + 8u * lay.seg);
@@ -1408,9 +1527,8 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             x_minp = static_cast<float>(static_cast<double>(M) +
                                         static_cast<double>(P->temperature) * log(static_cast<double>(P->min_p)));
         }
-        // Weight sums in three 32-bit parts, w = a * 2^32 + b * 2^16 + c (a < 2^12, b, c < 2^16): with
-        // at most 2^16 keys per CTA none of the three sums can wrap, so the adds are fire-and-forget.
-        // The c parts use region Y, which no CTA writes to before the third cluster barrier.
+        // Weight sums in three 32-bit parts (see mass_histogram). The c parts use region Y, which no
+        // CTA writes to before the third cluster barrier.
         for (int i = tid; i < kABins; i += kNT) {
             HB[i] = 0u;
             HA[i] = 0u;
@@ -1421,32 +1539,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         // min-p prefix mass (only when min-p is set); the row mass Z is read off the assembled
         // cumulative histogram instead of being summed separately
         const bool use_minp = P->min_p > 0.0f;
-        unsigned long long wp = 0ull;
-        const int nq8 = (nq + 1) >> 1;
-        const int it8 = (nq8 + kNT - 1) / kNT;
-#pragma unroll 1
-        for (int m = 0; m < it8; ++m) {  // 8 keys per iteration: independent chains
-            const int q = tid + m * kNT;
-            if (q >= nq8) break;
-            const uint4 va = reinterpret_cast<const uint4*>(K)[2 * q];
-            const uint4 vb = (2 * q + 1 < nq) ? reinterpret_cast<const uint4*>(K)[2 * q + 1] : make_uint4(0u, 0u, 0u, 0u);
-            const uint32_t k8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const uint32_t k = k8[i];
-                const float x = kval(k);
-                const unsigned long long w = (k != 0u) ? weight_of(x, wc) : 0ull;
-                const int b = abin_of(x, wc);
-                if (use_minp) wp += (x >= x_minp) ? w : 0ull;
-                const uint32_t c = static_cast<uint32_t>(w) & 0xFFFFu;
-                const uint32_t bm = static_cast<uint32_t>(w >> 16) & 0xFFFFu;
-                const uint32_t am = static_cast<uint32_t>(w >> 32);
-                if (c != 0u) atomicAdd(&HLO[b], c);
-                if (bm != 0u) atomicAdd(&HB[b], bm);
-                if (am != 0u) atomicAdd(&HA[b], am);
-                if (need_counts && k != 0u) atomicAdd(&HC[b], 1u);
-            }
-        }
+        unsigned long long wp = mass_histogram(K, nq, wc, x_minp, use_minp, need_counts, HLO, HB, HA, HC);
         if (use_minp) {
             wp = block_sum_u64<kNT>(wp, ls->red);
             if (tid < static_cast<int>(C)) cluster.map_shared_rank(cs, tid)->wmin[crank] = wp;
@@ -1475,72 +1568,23 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
 
     cluster.sync();  // ======================================================== CS3
 
-    // smallest key in [lo, hi] whose bin is <= bb, or hi + 1 when there is none: a 32-way search
-    // run by every warp (the bin index is non-increasing in the key)
-    auto first_key_bin_le = [&](int bb, uint32_t lo, uint32_t hi) -> unsigned long long {
-        const uint32_t hi0 = hi;
-        while (lo < hi) {
-            const uint32_t step = (hi - lo) / 31u + 1u;  // the last probe reaches hi
-            const unsigned long long pr = static_cast<unsigned long long>(lo) +
-                                          static_cast<unsigned long long>(lane) * step;
-            const uint32_t probe = pr > hi ? hi : static_cast<uint32_t>(pr);
-            const unsigned ball = __ballot_sync(0xFFFFFFFFu, xbin_g(probe) <= bb);
-            if (ball == 0u) return static_cast<unsigned long long>(hi0) + 1ull;  // only on the first pass
-            const int f = __ffs(ball) - 1;
-            const uint32_t pf = __shfl_sync(0xFFFFFFFFu, probe, f);
-            const uint32_t pp = __shfl_sync(0xFFFFFFFFu, probe, f > 0 ? f - 1 : 0);
-            hi = pf;
-            if (f > 0) lo = pp + 1u;
-        }
-        return (xbin_g(lo) <= bb) ? lo : static_cast<unsigned long long>(hi0) + 1ull;
+    // First bin with CG >= t (the last bin when there is none), by every warp: a 64-way step over
+    // the chunk ends, then a 2-way step within the chunk. CG is non-decreasing.
+    static_assert(kABins == 2048, "two-level search over 32 x 64 bins");
+    auto bin_of_target = [&](unsigned long long t) -> int {
+        const unsigned b1 = __ballot_sync(0xFFFFFFFFu, CG[lane * 64 + 63] >= t);
+        if (b1 == 0u) return kABins - 1;
+        const int base = (__ffs(b1) - 1) * 64;
+        const unsigned b2 = __ballot_sync(0xFFFFFFFFu, CG[base + 2 * lane + 1] >= t);
+        const int j = base + 2 * (__ffs(b2) - 1);
+        return CG[j] >= t ? j : j + 1;
     };
-    // Keys of bin b form the interval [lo, hi] of the valid keys [min_key, max key]. Block-wide
-    // (all threads call): warps 0-3 run the four searches of bins bA and bB (bB < 0: none) at
-    // once; r receives loA, hiA, loB, hiB (an empty interval for a missing bB).
-    const uint32_t kmax_valid = comp_key(best);
-    auto bin_ranges = [&](int bA, int bB, uint32_t* r) {
-        const int w = tid >> 5;
-        if (w < 4 && (w < 2 || bB >= 0)) {
-            const int bb = (w < 2 ? bA : bB) - (w & 1);  // odd warps: first key past the bin
-            const unsigned long long f = first_key_bin_le(bb, min_key, kmax_valid);
-            if (lane == 0) ls->bc[4 + w] = f;
-        }
-        __syncthreads();
-#pragma unroll 1
-        for (int j = 0; j < 2; ++j) {
-            uint32_t lo = 1u, hi = 0u;
-            if (j == 0 || bB >= 0) {
-                const unsigned long long ft = ls->bc[4 + 2 * j], ff = ls->bc[5 + 2 * j];
-                lo = ft > kmax_valid ? kmax_valid : static_cast<uint32_t>(ft);
-                hi = ff > kmax_valid ? kmax_valid : (ff == min_key ? min_key : static_cast<uint32_t>(ff - 1ull));
-            }
-            if (j == 0) {
-                r[0] = lo;
-                r[1] = hi;
-            } else {
-                r[2] = lo;
-                r[3] = hi;
-            }
-        }
-        __syncthreads();  // bc[4..7] may be rewritten by the next call
-    };
-    auto bin_of_target = [&](unsigned long long t) -> int {  // first bin with CG >= t
-        int lo = 0, hi = kABins - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            if (CG[mid] >= t) hi = mid;
-            else lo = mid + 1;
-        }
-        return lo;
-    };
-    // Pushes my entries of bin bA (and of bin bB when bB >= 0) whose composite is >= lowb into my
-    // segment of gather buffer bufA (bufB) in every CTA of the cluster, then publishes how many I
+    // Pushes my entries of bin bA (and of bins bBlo..bBhi when bBlo >= 0) whose composite is >= lowb
+    // into my segment of gather buffer bufA (bufB) in every CTA of the cluster, then publishes how many I
     // have (a count above the segment size marks the bin overfull). Slots come from a local
     // counter, so the remote traffic is plain stores.
     const uint32_t gseg = static_cast<uint32_t>(kGCap) / C;
-    auto gather = [&](int bA, int bufA, int bB, int bufB, unsigned long long lowb) {
-        uint32_t kr[4];
-        bin_ranges(bA, bB, kr);
+    auto gather = [&](int bA, int bufA, int bBlo, int bBhi, int bufB, unsigned long long lowb) {
         unsigned long long* gA = (bufA ? G1 : G0) + crank * gseg;
         unsigned long long* gB = (bufB ? G1 : G0) + crank * gseg;
         if (tid == 0) {
@@ -1556,10 +1600,11 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             const uint32_t k4[4] = {v.x, v.y, v.z, v.w};
             uint32_t mA = 0u, mB = 0u;  // membership bits of the four keys
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const bool ok = comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i)) >= lowb;
-                mA |= (ok && k4[i] >= kr[0] && k4[i] <= kr[1]) ? (1u << i) : 0u;
-                mB |= (ok && k4[i] >= kr[2] && k4[i] <= kr[3]) ? (1u << i) : 0u;
+            for (int i = 0; i < 4; ++i) {  // the bin exactly as the histogram computed it
+                const int bi = xbin_g(k4[i]);
+                const bool ok = k4[i] != 0u && comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i)) >= lowb;
+                mA |= (ok && bi == bA) ? (1u << i) : 0u;
+                mB |= (ok && bi >= bBlo && bi <= bBhi) ? (1u << i) : 0u;
             }
             if (__ballot_sync(0xFFFFFFFFu, (mA | mB) != 0u) == 0u) continue;
 #pragma unroll 1
@@ -1584,7 +1629,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         if (tid < static_cast<int>(C)) {
             ClusterShared* d = cluster.map_shared_rank(cs, tid);
             d->gseg[bufA][crank] = ls->gfill[0];
-            if (bB >= 0) d->gseg[bufB][crank] = ls->gfill[1];
+            if (bBlo >= 0) d->gseg[bufB][crank] = ls->gfill[1];
         }
     };
 
@@ -1637,8 +1682,10 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     st.stage = need_counts ? kStKBound : kStTopP;
     st.pending_bin = -1;
     st.pending_kind = 0;
-    st.pre_bin = -1;
+    st.pre_lo = -1;
+    st.pre_hi = -1;
     st.pre_buf = 0;
+    st.tabs = 0ull;
     st.result = -1;
     st.err = 0;
     st.zk = Z;
@@ -1654,7 +1701,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     uint32_t* RW[2] = {reinterpret_cast<uint32_t*>(R + 256), reinterpret_cast<uint32_t*>(R + 512)};  // split
 
     auto rf_match = [&](int e, uint32_t k) -> bool {
-        if (k < rf.klo || k > rf.khi || (k & rf.pmask) != rf.prefix) return false;
+        if (k == 0u || (k & rf.pmask) != rf.prefix || xbin_g(k) != rf.bin) return false;
         const unsigned long long cp = comp_of(k, static_cast<uint32_t>(c0 + e));
         return cp >= rf.lowb && cp != rf.excl;
     };
@@ -1695,10 +1742,14 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         // ------------------------------------------------ resolve what the previous round started
         if (st.pending_kind == 1 || st.pending_kind == 4) {
             const int gbuf = (st.pending_kind == 4) ? st.pre_buf : prev;
-            if (st.pending_kind == 4) st.pre_bin = -1;
+            if (st.pending_kind == 4) st.pre_lo = -1;
             const unsigned int* gcn = cs->gseg[gbuf];
             bool over = false;
             for (uint32_t q = 0; q < C; ++q) over |= gcn[q] > gseg;
+            if (over && st.pending_kind == 4) {  // refine the draw's own bin
+                const int b = st.pending_bin;
+                st.target = st.tabs - (b > 0 ? CG[b - 1] : 0ull);
+            }
             const unsigned long long lowb = (st.stage == kStKBound) ? 0ull : st.kbound;
             const unsigned long long ex = (st.stage == kStResid) ? st.excl : 0ull;
             const bool cmode = (st.stage == kStKBound);
@@ -1717,12 +1768,6 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 rf.above_c = 0ull;
                 rf.above_w = 0ull;
                 rf.buf = 0;
-                {
-                    uint32_t kr[4];
-                    bin_ranges(rf.bin, -1, kr);
-                    rf.klo = kr[0];
-                    rf.khi = kr[1];
-                }
                 uint32_t lo = 0xFFFFFFFFu, hi = 0u;
                 for (int e = tid; e < len; e += kNT) {
                     const uint32_t k = K[e];
@@ -1736,8 +1781,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 st.pending_kind = 3;
             } else {
                 const unsigned long long* gp = gbuf ? G1 : G0;
-                sel = block_select(gp, gcn, C, gseg, st.target, cmode ? nullptr : &wc, lowb, ex, BH, BWS, ls,
-                                   &cum_sel);
+                sel = block_select(gp, gcn, C, gseg, st.target, wc, !cmode, lowb, ex, BH, ls, &cum_sel);
                 if (sel == 0ull) {
                     st.err = 2;
                 } else {
@@ -2038,7 +2082,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             st.pending_bin = -1;
         }
         // ------------------------------------------------ advance stages and issue the next exchange
-        GatherReq gq{-1, 0, -1, 0, 0ull};
+        GatherReq gq{-1, 0, -1, -1, 0, 0ull};
         while (!st.err && st.stage != kStDone && st.pending_kind == 0) {
             if (st.stage == kStKBound) {
                 const unsigned long long t = k_eff;
@@ -2051,7 +2095,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 st.target = t - (lo > 0 ? CGC[lo - 1] : 0u);
                 st.pending_bin = lo;
                 st.pending_kind = 1;
-                gq = GatherReq{lo, cur, -1, 0, 0ull};
+                gq = GatherReq{lo, cur, -1, -1, 0, 0ull};
             } else if (st.stage == kStTopP) {
                 if (P->top_p > 0.0f && P->top_p < 1.0f) {
                     unsigned long long t1 = ceil_mass(P->top_p, st.zk);
@@ -2060,10 +2104,10 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                     st.target = t1 - (b > 0 ? CG[b - 1] : 0ull);
                     st.pending_bin = b;
                     st.pending_kind = 1;
-                    // The kept mass will lie in [CG[b-1] + 1, CG[b]] (min-p can only lower it). When
-                    // both ends put the draw in the same bin, that bin is gathered now as well, into
-                    // the other buffer (free: nothing was read from it in this round).
-                    int b2 = -1;
+                    // The kept mass will lie in [CG[b-1] + 1, CG[b]] (min-p can only lower it), so the
+                    // draw lands in bins blo..bhi. When that range is narrow it is gathered now as
+                    // well, into the other buffer (free: nothing was read from it in this round).
+                    int blo = -1, bhi = -1;
                     if (draw_follows && !read_buf) {
                         unsigned long long zlo = (b > 0 ? CG[b - 1] : 0ull) + 1ull, zhi = CG[b];
                         if (P->min_p > 0.0f) {
@@ -2071,22 +2115,20 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                             zhi = zhi < Wmin ? zhi : Wmin;
                         }
                         if (zlo > 0ull) {
-                            const int blo = bin_of_target(scale_mass(rc.u_draw, zlo) + 1ull);
-                            const int bhi = bin_of_target(scale_mass(rc.u_draw, zhi) + 1ull);
-                            if (blo == bhi) b2 = blo;
+                            blo = bin_of_target(scale_mass(rc.u_draw, zlo) + 1ull);
+                            bhi = bin_of_target(scale_mass(rc.u_draw, zhi) + 1ull);
+                            if (bhi - blo >= kPreBins) blo = bhi = -1;
                         }
                     }
-                    if (b2 >= 0 && b2 != b) {
-                        gq = GatherReq{b, cur, b2, prev, st.kbound};
-                        st.pre_bin = b2;
+                    if (blo >= 0 && !(blo == b && bhi == b)) {
+                        gq = GatherReq{b, cur, blo, bhi, prev, st.kbound};
                         st.pre_buf = prev;
                     } else {
-                        gq = GatherReq{b, cur, -1, 0, st.kbound};
-                        if (b2 == b) {
-                            st.pre_bin = b;
-                            st.pre_buf = cur;
-                        }
+                        gq = GatherReq{b, cur, -1, -1, 0, st.kbound};
+                        st.pre_buf = cur;  // the draw bin is the top-p bin
                     }
+                    st.pre_lo = blo;
+                    st.pre_hi = bhi;
                 } else {
                     st.zkept = st.zk;
                     st.stage = kStKept;
@@ -2171,7 +2213,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                                 st.stage = kStResid;
                                 st.pending_bin = lo;
                                 st.pending_kind = 1;
-                                gq = GatherReq{lo, cur, -1, 0, st.kbound};
+                                gq = GatherReq{lo, cur, -1, -1, 0, st.kbound};
                             } else {
                                 st.stage = kStDraw;  // residual empty: draw from the kept set
                             }
@@ -2185,23 +2227,26 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 const int b = bin_of_target(t);
                 st.target = t - (b > 0 ? CG[b - 1] : 0ull);
                 st.pending_bin = b;
-                if (b == st.pre_bin) {
-                    st.pending_kind = 4;  // gathered with the top-p bin: resolve it in this round
-                } else if (read_buf && st.pre_bin >= 0) {
+                st.tabs = t;
+                if (st.pre_lo >= 0 && b >= st.pre_lo && b <= st.pre_hi) {
+                    // gathered with the top-p bin: select over the whole prefetched range now
+                    st.target = t - (st.pre_lo > 0 ? CG[st.pre_lo - 1] : 0ull);
+                    st.pending_kind = 4;
+                } else if (read_buf && st.pre_lo >= 0) {
                     // unreachable when the prediction holds; the prefetch buffer may still be read
                     // by this round's resolution, so the gather waits for the next round
-                    st.pre_bin = -1;
+                    st.pre_lo = -1;
                     st.pending_kind = 5;
                 } else {
-                    st.pre_bin = -1;
+                    st.pre_lo = -1;
                     st.pending_kind = 1;
-                    gq = GatherReq{b, cur, -1, 0, st.kbound};
+                    gq = GatherReq{b, cur, -1, -1, 0, st.kbound};
                 }
             } else {
                 st.err = 4;
             }
         }
-        if (gq.bA >= 0) gather(gq.bA, gq.bufA, gq.bB, gq.bufB, gq.lowb);  // the one gather site
+        if (gq.bA >= 0) gather(gq.bA, gq.bufA, gq.bBlo, gq.bBhi, gq.bufB, gq.lowb);  // the one gather site
         if (st.pending_kind != 4) break;
         }  // pass
         cluster.sync();  // ============================================ one barrier per round

@@ -1568,6 +1568,36 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
 
     cluster.sync();  // ======================================================== CS3
 
+    // Smallest valid key whose bin is <= bb (kmax + 1 when there is none); the bin is non-increasing
+    // in the key. The boundary is estimated from the inverse of the bin function and then stepped
+    // to the exact key where xbin_g changes, so the interval matches the histogram exactly.
+    const uint32_t kmax = comp_key(best);
+    const double inv_tscale = static_cast<double>(P->temperature) /
+                              (1.4426950408889634 * static_cast<double>(wc.bin_scale));
+    auto first_key_bin_le = [&](int bb) -> unsigned long long {
+        if (bb < 0 || xbin_g(kmax) > bb) return static_cast<unsigned long long>(kmax) + 1ull;
+        if (xbin_g(min_key) <= bb) return min_key;
+        // now bin(min_key) > bb >= bin(kmax): the answer lies in (min_key, kmax]
+        uint32_t k = fkey(static_cast<float>(static_cast<double>(M) - static_cast<double>(bb + 1) * inv_tscale));
+        k = k <= min_key ? min_key + 1u : (k > kmax ? kmax : k);
+#pragma unroll 1
+        for (int it = 0; it < 64; ++it) {
+            if (xbin_g(k) > bb) {
+                ++k;  // k <= kmax here since bin(kmax) <= bb
+            } else if (xbin_g(k - 1u) <= bb) {
+                --k;  // k - 1 > min_key here since bin(min_key) > bb
+            } else {
+                return k;
+            }
+        }
+        uint32_t lo = min_key + 1u, hi = kmax;  // far from the estimate: bisect
+        while (lo < hi) {
+            const uint32_t mid = lo + ((hi - lo) >> 1);
+            if (xbin_g(mid) <= bb) hi = mid;
+            else lo = mid + 1u;
+        }
+        return lo;
+    };
     // First bin with CG >= t (the last bin when there is none), by every warp: a 64-way step over
     // the chunk ends, then a 2-way step within the chunk. CG is non-decreasing.
     static_assert(kABins == 2048, "two-level search over 32 x 64 bins");
@@ -1585,8 +1615,24 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     // counter, so the remote traffic is plain stores.
     const uint32_t gseg = static_cast<uint32_t>(kGCap) / C;
     auto gather = [&](int bA, int bufA, int bBlo, int bBhi, int bufB, unsigned long long lowb) {
+        // key intervals: bin bA, and bins bBlo..bBhi (empty when bBlo < 0)
+        const uint32_t kloA = static_cast<uint32_t>(first_key_bin_le(bA));
+        const unsigned long long khiA1 = first_key_bin_le(bA - 1);  // one past bin bA
+        uint32_t kloB = 1u;
+        unsigned long long khiB1 = 0ull;
+        if (bBlo >= 0) {
+            kloB = static_cast<uint32_t>(first_key_bin_le(bBhi));
+            khiB1 = first_key_bin_le(bBlo - 1);
+        }
         unsigned long long* gA = (bufA ? G1 : G0) + crank * gseg;
         unsigned long long* gB = (bufB ? G1 : G0) + crank * gseg;
+        // Membership is one unsigned subtract-compare per interval; the composite lower bound is
+        // tested only when it is set (k-bound rows). These loops are bound by the integer pipe.
+        const uint32_t wA = static_cast<uint32_t>(khiA1 - kloA);
+        const uint32_t wB = bBlo >= 0 ? static_cast<uint32_t>(khiB1 - kloB) : 0u;  // empty set B
+        const bool use_lowb = lowb != 0ull;
+        // One pass: per key only the interval tests; a warp reserves slots (local counter) only on
+        // the rare iterations where one of its lanes holds a match.
         if (tid == 0) {
             ls->gfill[0] = 0u;
             ls->gfill[1] = 0u;
@@ -1598,38 +1644,52 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             uint4 v = make_uint4(0u, 0u, 0u, 0u);
             if (q < nq) v = reinterpret_cast<const uint4*>(K)[q];
             const uint32_t k4[4] = {v.x, v.y, v.z, v.w};
-            uint32_t mA = 0u, mB = 0u;  // membership bits of the four keys
+            uint32_t mA = 0u, mB = 0u;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {  // the bin exactly as the histogram computed it
-                const int bi = xbin_g(k4[i]);
-                const bool ok = k4[i] != 0u && comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i)) >= lowb;
-                mA |= (ok && bi == bA) ? (1u << i) : 0u;
-                mB |= (ok && bi >= bBlo && bi <= bBhi) ? (1u << i) : 0u;
+            for (int i = 0; i < 4; ++i) {
+                mA |= (k4[i] - kloA < wA) ? (1u << i) : 0u;
+                mB |= (k4[i] - kloB < wB) ? (1u << i) : 0u;
             }
             if (__ballot_sync(0xFFFFFFFFu, (mA | mB) != 0u) == 0u) continue;
-#pragma unroll 1
-            for (int gsel = 0; gsel < 2; ++gsel) {
-                uint32_t mk = gsel ? mB : mA;
-                if (__ballot_sync(0xFFFFFFFFu, mk != 0u) == 0u) continue;
-                uint32_t pos = warp_reserve(static_cast<uint32_t>(__popc(mk)), &ls->gfill[gsel]);
-                unsigned long long* gdst = gsel ? gB : gA;
-                while (mk != 0u) {
-                    const int e = 4 * q + __ffs(mk) - 1;
-                    mk &= mk - 1u;
-                    const unsigned long long cp = comp_of(K[e], static_cast<uint32_t>(c0 + e));
-                    if (pos < gseg) {
-#pragma unroll 1
-                        for (uint32_t dst = 0; dst < C; ++dst) cluster.map_shared_rank(gdst, dst)[pos] = cp;
+            if (use_lowb) {  // k-bound rows: drop entries below the composite bound
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i)) < lowb) {
+                        mA &= ~(1u << i);
+                        mB &= ~(1u << i);
                     }
-                    ++pos;
+                }
+            }
+            uint32_t pA = warp_reserve(static_cast<uint32_t>(__popc(mA)), &ls->gfill[0]);
+            uint32_t pB = warp_reserve(static_cast<uint32_t>(__popc(mB)), &ls->gfill[1]);
+            uint32_t mk = mA | mB;
+            while (mk != 0u) {
+                const int i = __ffs(mk) - 1;
+                mk &= mk - 1u;
+                const int e = 4 * q + i;
+                const unsigned long long cp = comp_of(K[e], static_cast<uint32_t>(c0 + e));
+                if ((mA >> i) & 1u) {
+                    if (pA < gseg) {
+#pragma unroll 1
+                        for (uint32_t dst = 0; dst < C; ++dst) cluster.map_shared_rank(gA, dst)[pA] = cp;
+                    }
+                    ++pA;
+                }
+                if ((mB >> i) & 1u) {
+                    if (pB < gseg) {
+#pragma unroll 1
+                        for (uint32_t dst = 0; dst < C; ++dst) cluster.map_shared_rank(gB, dst)[pB] = cp;
+                    }
+                    ++pB;
                 }
             }
         }
         __syncthreads();
-        if (tid < static_cast<int>(C)) {
+        const uint32_t tot = ls->gfill[0] | (ls->gfill[1] << 16);
+        if (tid < static_cast<int>(C)) {  // publish my counts (above gseg: the bin is overfull)
             ClusterShared* d = cluster.map_shared_rank(cs, tid);
-            d->gseg[bufA][crank] = ls->gfill[0];
-            if (bBlo >= 0) d->gseg[bufB][crank] = ls->gfill[1];
+            d->gseg[bufA][crank] = tot & 0xFFFFu;
+            if (bBlo >= 0) d->gseg[bufB][crank] = tot >> 16;
         }
     };
 

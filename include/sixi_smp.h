@@ -182,6 +182,32 @@ SIXI_SMP_API int32_t sixi_smp_verify(sixi_smp* h, const sixi_smp_rows* target, c
                         int32_t* out_uniforms_used, int32_t* out_status, void* stream);
 
 /*
+ * sixi_smp_verify without a handle and without any allocation (no counterpart in the engine).
+ * For callers that may not allocate device memory at all - for instance a serving loop whose
+ * device memory is owned by an external allocator, or one that must not call into the CUDA
+ * allocator (cudaMalloc / cudaFree synchronize the device) - and therefore cannot create a
+ * handle. Same arguments, semantics and outputs as sixi_smp_verify, with the vocabulary and the
+ * device given directly; it runs on `device` (made current for the call).
+ *   - The per-row workspace is a static device array of SIXI_SMP_STATIC_VERIFY_ROWS rows (16 bytes
+ *     each, 64 KB): n_streams * (k + 1) larger than that returns SIXI_OUT_OF_BOUNDS.
+ *   - Nothing in it has to start at zero: every row's slot is written before it is read.
+ *   - The first call on each device resolves the workspace address (cudaGetSymbolAddress) and
+ *     sets the kernels' shared-memory limits; make that first call before any stream capture
+ *     begins on that device.
+ *   - All calls on one device share the workspace: calls that overlap in time (on different
+ *     streams, or from different threads) race and must be serialized by the caller.
+ */
+#define SIXI_SMP_STATIC_VERIFY_ROWS 4096u
+SIXI_SMP_API int32_t sixi_smp_verify_static(int32_t device, uint32_t vocab, const sixi_smp_rows* target,
+                               const float* draft_probs, const int32_t* drafts, const int32_t* n_drafts,
+                               uint32_t n_streams, uint32_t k, const sixi_smp_params* params,
+                               const uint32_t* mask_words, const int32_t* hist_tokens,
+                               const int64_t* hist_offsets, const double* uniforms, uint64_t step,
+                               int32_t* out_accepted, int32_t* out_tokens, int32_t* out_n_tokens,
+                               int32_t* out_first_reject, int32_t* out_uniforms_used, int32_t* out_status,
+                               void* stream);
+
+/*
  * Vocab-sharded mode (logits produced vocab-parallel; no counterpart in the engine, which runs on
  * one device). Stage 1 on every rank: for each row of this rank's vocab shard
  * [vocab_offset, vocab_offset + shard_vocab), apply mask and penalties and emit the shard's best

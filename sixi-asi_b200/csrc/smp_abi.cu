@@ -5,6 +5,7 @@
 // sixi_smp_sample_host, whose contract is the engine's host-side sample_token call shape.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <new>
@@ -57,6 +58,13 @@ struct DeviceGuard {
         if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
     }
 };
+
+// Verifier workspace of sixi_smp_verify_static: a file-scope device array (no allocation). Its
+// address on each device is resolved once, by the first call on that device.
+constexpr uint32_t kStaticVerifyRows = SIXI_SMP_STATIC_VERIFY_ROWS;
+__device__ __align__(256) VerifyRowResult g_static_verify_ws[kStaticVerifyRows];
+constexpr int kMaxDevices = 64;
+std::atomic<VerifyRowResult*> g_static_ws_addr[kMaxDevices];
 
 bool rows_ok(const sixi_smp* h, const sixi_smp_rows* rows) {
     if (rows == nullptr || (rows->n_rows > 0 && rows->data == nullptr)) return false;
@@ -345,6 +353,66 @@ int32_t sixi_smp_verify(sixi_smp* h, const sixi_smp_rows* target, const float* d
     a.n_drafts = n_drafts;
     a.k = k;
     a.ws = h->ws;
+    cudaError_t e = sixi_b200::launch_rows(sixi_b200::kModeVerify, a, plan, s);
+    if (e == cudaSuccess)
+        e = sixi_b200::launch_verify_finalize(a, n_streams, out_accepted, out_tokens, out_n_tokens,
+                                              out_first_reject, out_uniforms_used, out_status, s);
+    return from_cuda(e);
+}
+
+int32_t sixi_smp_verify_static(int32_t device, uint32_t vocab, const sixi_smp_rows* target,
+                               const float* draft_probs, const int32_t* drafts, const int32_t* n_drafts,
+                               uint32_t n_streams, uint32_t k, const sixi_smp_params* params,
+                               const uint32_t* mask_words, const int32_t* hist_tokens,
+                               const int64_t* hist_offsets, const double* uniforms, uint64_t step,
+                               int32_t* out_accepted, int32_t* out_tokens, int32_t* out_n_tokens,
+                               int32_t* out_first_reject, int32_t* out_uniforms_used, int32_t* out_status,
+                               void* stream) {
+    LaunchPlan plan{};
+    if (device < 0 || device >= kMaxDevices || vocab == 0 || !sixi_b200::plan_rows(vocab, 1, &plan))
+        return SIXI_INVALID_ARGUMENT;
+    if (target == nullptr || (target->n_rows > 0 && target->data == nullptr) ||
+        (target->dtype != SIXI_SMP_F32 && target->dtype != SIXI_SMP_BF16) || target->row_stride < vocab ||
+        params == nullptr || drafts == nullptr || out_accepted == nullptr || out_tokens == nullptr ||
+        out_n_tokens == nullptr || out_first_reject == nullptr || out_uniforms_used == nullptr ||
+        out_status == nullptr || (hist_tokens != nullptr && hist_offsets == nullptr) || k == 0)
+        return SIXI_INVALID_ARGUMENT;
+    if (static_cast<uint64_t>(n_streams) * (k + 1) != target->n_rows) return SIXI_INVALID_ARGUMENT;
+    if (target->n_rows > kStaticVerifyRows) return SIXI_OUT_OF_BOUNDS;  // larger than the static workspace
+    if (n_streams == 0) return SIXI_OK;
+    if (draft_probs != nullptr && (reinterpret_cast<uintptr_t>(draft_probs) & 3u) != 0)
+        return SIXI_INVALID_ARGUMENT;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device >= n) return SIXI_INVALID_ARGUMENT;
+    DeviceGuard g(device);
+    VerifyRowResult* ws = g_static_ws_addr[device].load(std::memory_order_acquire);
+    if (ws == nullptr) {  // first call on this device: check the architecture, resolve the address
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return SIXI_BACKEND_ERROR;
+        if (prop.major < 10) return SIXI_UNSUPPORTED_HARDWARE;
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_static_verify_ws) != cudaSuccess || p == nullptr) return SIXI_BACKEND_ERROR;
+        ws = static_cast<VerifyRowResult*>(p);
+        g_static_ws_addr[device].store(ws, std::memory_order_release);
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    sixi_smp probe_h;  // the fields base_args reads; no memory is attached to it
+    std::memset(&probe_h, 0, sizeof(probe_h));
+    probe_h.device = device;
+    probe_h.vocab = vocab;
+    probe_h.mask_words = (vocab + 31u) / 32u;
+    RowArgs a = base_args(&probe_h, target, &plan);
+    a.params = params;
+    a.mask = mask_words;
+    a.hist = hist_tokens;
+    a.hist_off = hist_tokens ? hist_offsets : nullptr;
+    a.uniforms = uniforms;
+    a.step = step;
+    a.q = draft_probs;
+    a.drafts = drafts;
+    a.n_drafts = n_drafts;
+    a.k = k;
+    a.ws = ws;
     cudaError_t e = sixi_b200::launch_rows(sixi_b200::kModeVerify, a, plan, s);
     if (e == cudaSuccess)
         e = sixi_b200::launch_verify_finalize(a, n_streams, out_accepted, out_tokens, out_n_tokens,

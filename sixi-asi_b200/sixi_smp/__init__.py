@@ -84,6 +84,8 @@ SIGNATURES = {
     "sixi_smp_candidates": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _P, _U32, _P, _P, _P, _P, _P]),
     "sixi_smp_verify": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32, _P, _P, _P, _P, _P,
                                _U64, _P, _P, _P, _P, _P, _P, _P]),
+    "sixi_smp_verify_static": (_I32, [_I32, _U32, ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32, _P, _P, _P,
+                                      _P, _P, _U64, _P, _P, _P, _P, _P, _P, _P]),
     "sixi_smp_shard_candidates": (_I32, [_P, ctypes.POINTER(Rows), _U32, _U32, _P, _P, _P, _P, _U32,
                                          _P, _P, _P]),
     "sixi_smp_merge_shards": (_I32, [_P, _U32, _U32, _U32, _P, _P, _P, _P, _U64, _P, _P, _P]),
@@ -276,3 +278,30 @@ class Sampler:
                                       hp(out_status), self._stream(stream) if stream is not None else 0)
         _check("sixi_smp_sample_host", st)
         return out_tokens, out_status
+
+
+STATIC_VERIFY_ROWS = 4096  # SIXI_SMP_STATIC_VERIFY_ROWS
+
+
+def verify_static(vocab: int, target, drafts, params, draft_probs=None, n_drafts=None, masks=None, hist=None,
+                  hist_off=None, uniforms=None, step=0, stream=None):
+    """sixi_smp_verify_static: the verifier without a handle or any allocation inside the call
+    (its workspace is a static device array of STATIC_VERIFY_ROWS rows). Outputs are allocated
+    here by torch, on the target's device."""
+    import torch
+
+    S, k = drafts.shape
+    dev = target.device
+    acc = torch.empty(S, dtype=torch.int32, device=dev)
+    toks = torch.empty((S, k + 1), dtype=torch.int32, device=dev)
+    ntok = torch.empty(S, dtype=torch.int32, device=dev)
+    frej = torch.empty(S, dtype=torch.int32, device=dev)
+    used = torch.empty(S, dtype=torch.int32, device=dev)
+    sts = torch.empty(S, dtype=torch.int32, device=dev)
+    rows = Sampler._rows(target)
+    st = _lib().sixi_smp_verify_static(dev.index or 0, vocab, ctypes.byref(rows), _ptr(draft_probs), _ptr(drafts),
+                                       _ptr(n_drafts), S, k, _ptr(params), _ptr(masks), _ptr(hist), _ptr(hist_off),
+                                       _ptr(uniforms), step, _ptr(acc), _ptr(toks), _ptr(ntok), _ptr(frej),
+                                       _ptr(used), _ptr(sts), Sampler._stream(stream))
+    _check("sixi_smp_verify_static", st)
+    return dict(accepted=acc, tokens=toks, n_tokens=ntok, first_reject=frej, uniforms_used=used, status=sts)

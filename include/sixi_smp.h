@@ -209,20 +209,28 @@ SIXI_SMP_API int32_t sixi_smp_verify_static(int32_t device, uint32_t vocab, cons
 
 /*
  * Vocab-sharded mode (logits produced vocab-parallel; no counterpart in the engine, which runs on
- * one device). Stage 1 on every rank: for each row of this rank's vocab shard
- * [vocab_offset, vocab_offset + shard_vocab), apply mask and penalties and emit the shard's best
- * `top_n` (<= 64) candidates (adjusted logit, global id; sorted logit desc, id asc; padded with
- * -inf / -1), the shard max, sum of exp((v - max) / T) over the shard and the allowed count.
- *   mask_words  full-vocabulary masks [n_rows][ceil(full_vocab/32)]; the shard reads its bit range
+ * one device). The handle is created for the full vocabulary.
+ * Stage 1 on every rank: for each row of this rank's slice [vocab_offset, vocab_offset +
+ * shard_vocab) (shard_rows: n_rows rows of shard_vocab <= row_stride logits; shard_vocab <=
+ * 97,000), apply mask and penalties as sixi_smp_sample does and emit the slice's best `top_n`
+ * (1..64) candidates (adjusted logit, global id; sorted logit desc, id asc; padded with -inf / -1),
+ * the slice max, the sum of exp((x - max) / T) over the slice (fp32 terms ~1e-7 relative, fp64
+ * sum) and the allowed count.
+ *   params      [n_rows] (the same records on every rank)
+ *   mask_words  full-vocabulary masks [n_rows][ceil(full_vocab/32)]; the slice reads its bit range
+ *   hist_*      CSR histories of global ids (the same on every rank)
  *   out_cand    [n_rows][top_n] of {float logit; int32 id} (8 bytes each)
  *   out_stats   [n_rows] of {float max; int32 n_allowed; double sum_exp; int32 status; int32 pad}
- * Stage 2 (after an all-gather of both arrays over the ranks) on every rank: merge n_shards
- * shards per row into the final token, identically on every rank. Exact for top_k <= top_n; rows
- * whose top-k or top-p set is not contained in the gathered candidates report
- * SIXI_OUT_OF_BOUNDS in out_status.
+ * Stage 2, after an all-gather of both arrays over the ranks (rank-major: [n_shards][n_rows][top_n]
+ * and [n_shards][n_rows]), runs identically on every rank: it merges the shards of each row and
+ * draws the token as sixi_smp_sample would on the full row (uniforms [n_rows] or NULL for Philox
+ * slot 0). Exact whenever top_k <= top_n. Otherwise the merged list is known down to the worst
+ * listed candidate of any shard whose list was truncated; a row whose top-k, top-p, min-p or draw
+ * decision falls beyond that point reports SIXI_OUT_OF_BOUNDS (n_shards <= 16,
+ * n_shards * top_n <= 1024).
  */
 SIXI_SMP_API int32_t sixi_smp_shard_candidates(sixi_smp* h, const sixi_smp_rows* shard_rows,
-                                  uint32_t vocab_offset, uint32_t full_vocab,
+                                  uint32_t vocab_offset, uint32_t shard_vocab, uint32_t full_vocab,
                                   const sixi_smp_params* params, const uint32_t* mask_words,
                                   const int32_t* hist_tokens, const int64_t* hist_offsets,
                                   uint32_t top_n, void* out_cand, void* out_stats, void* stream);

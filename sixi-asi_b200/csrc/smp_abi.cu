@@ -420,16 +420,63 @@ int32_t sixi_smp_verify_static(int32_t device, uint32_t vocab, const sixi_smp_ro
     return from_cuda(e);
 }
 
-int32_t sixi_smp_shard_candidates(sixi_smp*, const sixi_smp_rows*, uint32_t, uint32_t,
-                                  const sixi_smp_params*, const uint32_t*, const int32_t*,
-                                  const int64_t*, uint32_t, void*, void*, void*) {
-    return SIXI_UNSUPPORTED_HARDWARE;
+int32_t sixi_smp_shard_candidates(sixi_smp* h, const sixi_smp_rows* shard_rows, uint32_t vocab_offset,
+                                  uint32_t shard_vocab, uint32_t full_vocab, const sixi_smp_params* params,
+                                  const uint32_t* mask_words, const int32_t* hist_tokens,
+                                  const int64_t* hist_offsets, uint32_t top_n, void* out_cand, void* out_stats,
+                                  void* stream) {
+    if (h == nullptr || shard_rows == nullptr || params == nullptr || out_cand == nullptr || out_stats == nullptr ||
+        (shard_rows->n_rows > 0 && shard_rows->data == nullptr) ||
+        (shard_rows->dtype != SIXI_SMP_F32 && shard_rows->dtype != SIXI_SMP_BF16) ||
+        (hist_tokens != nullptr && hist_offsets == nullptr))
+        return SIXI_INVALID_ARGUMENT;
+    if (full_vocab != h->vocab || shard_vocab == 0 || shard_vocab > shard_rows->row_stride ||
+        static_cast<uint64_t>(vocab_offset) + shard_vocab > full_vocab || top_n == 0 ||
+        top_n > sixi_b200::kMaxShardTopN || sixi_b200::shard_smem_bytes(shard_vocab) > sixi_b200::kMaxShardSmem)
+        return SIXI_INVALID_ARGUMENT;
+    if (shard_rows->n_rows == 0) return SIXI_OK;
+    DeviceGuard g(h->device);
+    sixi_b200::ShardArgs a{};
+    a.data = shard_rows->data;
+    a.row_stride = shard_rows->row_stride;
+    a.dtype = shard_rows->dtype;
+    a.shard_vocab = shard_vocab;
+    a.vocab_offset = vocab_offset;
+    a.full_vocab = full_vocab;
+    a.mask_words = h->mask_words;
+    a.n_rows = shard_rows->n_rows;
+    a.top_n = top_n;
+    a.params = params;
+    a.mask = mask_words;
+    a.hist = hist_tokens;
+    a.hist_off = hist_tokens ? hist_offsets : nullptr;
+    a.out_cand = static_cast<sixi_b200::ShardCand*>(out_cand);
+    a.out_stats = static_cast<sixi_b200::ShardStats*>(out_stats);
+    return from_cuda(sixi_b200::launch_shard_candidates(a, static_cast<cudaStream_t>(stream)));
 }
 
-int32_t sixi_smp_merge_shards(sixi_smp*, uint32_t, uint32_t, uint32_t, const void*, const void*,
-                              const sixi_smp_params*, const double*, uint64_t, int32_t*, int32_t*,
-                              void*) {
-    return SIXI_UNSUPPORTED_HARDWARE;
+int32_t sixi_smp_merge_shards(sixi_smp* h, uint32_t n_rows, uint32_t n_shards, uint32_t top_n,
+                              const void* gathered_cand, const void* gathered_stats, const sixi_smp_params* params,
+                              const double* uniforms, uint64_t step, int32_t* out_tokens, int32_t* out_status,
+                              void* stream) {
+    if (h == nullptr || gathered_cand == nullptr || gathered_stats == nullptr || params == nullptr ||
+        out_tokens == nullptr || out_status == nullptr || n_shards == 0 || n_shards > sixi_b200::kMaxShards ||
+        top_n == 0 || top_n > sixi_b200::kMaxShardTopN || n_shards * top_n > 1024u)
+        return SIXI_INVALID_ARGUMENT;
+    if (n_rows == 0) return SIXI_OK;
+    DeviceGuard g(h->device);
+    sixi_b200::MergeArgs a{};
+    a.n_rows = n_rows;
+    a.n_shards = n_shards;
+    a.top_n = top_n;
+    a.cand = static_cast<const sixi_b200::ShardCand*>(gathered_cand);
+    a.stats = static_cast<const sixi_b200::ShardStats*>(gathered_stats);
+    a.params = params;
+    a.uniforms = uniforms;
+    a.step = step;
+    a.out_tok = out_tokens;
+    a.out_status = out_status;
+    return from_cuda(sixi_b200::launch_merge_shards(a, static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

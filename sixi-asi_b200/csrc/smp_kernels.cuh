@@ -71,4 +71,53 @@ cudaError_t launch_verify_finalize(const RowArgs& a, uint32_t n_streams, int32_t
                                    int32_t* out_status, cudaStream_t stream);
 cudaError_t prepare_kernels(int device);
 
+// ---- vocab-sharded mode (smp_shard.cu) ---------------------------------------------------------
+struct ShardCand {  // one candidate of a shard (8 bytes, the layout of include/sixi_smp.h)
+    float logit;    // adjusted logit (mask, penalties applied)
+    int32_t id;     // global token id, -1 for padding
+};
+struct ShardStats {  // per-row summary of a shard (24 bytes)
+    float max;       // largest adjusted allowed logit (-inf when none)
+    int32_t n_allowed;
+    double sum_exp;  // sum over allowed ids of exp((x - max) / T) (0 for greedy rows)
+    int32_t status;
+    int32_t pad;
+};
+static_assert(sizeof(ShardCand) == 8 && sizeof(ShardStats) == 24, "shard record layouts");
+
+constexpr uint32_t kMaxShards = 16;
+constexpr uint32_t kMaxShardTopN = 64;
+constexpr size_t kMaxShardSmem = 227 * 1024;
+
+struct ShardArgs {
+    const void* data;
+    uint64_t row_stride;  // elements
+    uint32_t dtype;
+    uint32_t shard_vocab;
+    uint32_t vocab_offset;
+    uint32_t full_vocab;
+    uint32_t mask_words;  // words per full-vocabulary mask row
+    uint32_t n_rows;
+    uint32_t top_n;
+    const sixi_smp_params* params;
+    const uint32_t* mask;
+    const int32_t* hist;
+    const int64_t* hist_off;
+    ShardCand* out_cand;
+    ShardStats* out_stats;
+};
+struct MergeArgs {
+    uint32_t n_rows, n_shards, top_n;
+    const ShardCand* cand;    // [n_shards][n_rows][top_n]
+    const ShardStats* stats;  // [n_shards][n_rows]
+    const sixi_smp_params* params;
+    const double* uniforms;
+    uint64_t step;
+    int32_t* out_tok;
+    int32_t* out_status;
+};
+size_t shard_smem_bytes(uint32_t shard_vocab);
+cudaError_t launch_shard_candidates(const ShardArgs& a, cudaStream_t stream);
+cudaError_t launch_merge_shards(const MergeArgs& a, cudaStream_t stream);
+
 }  // namespace sixi_b200

@@ -86,7 +86,7 @@ SIGNATURES = {
                                _U64, _P, _P, _P, _P, _P, _P, _P]),
     "sixi_smp_verify_static": (_I32, [_I32, _U32, ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32, _P, _P, _P,
                                       _P, _P, _U64, _P, _P, _P, _P, _P, _P, _P]),
-    "sixi_smp_shard_candidates": (_I32, [_P, ctypes.POINTER(Rows), _U32, _U32, _P, _P, _P, _P, _U32,
+    "sixi_smp_shard_candidates": (_I32, [_P, ctypes.POINTER(Rows), _U32, _U32, _U32, _P, _P, _P, _P, _U32,
                                          _P, _P, _P]),
     "sixi_smp_merge_shards": (_I32, [_P, _U32, _U32, _U32, _P, _P, _P, _P, _U64, _P, _P, _P]),
     "sixi_smp_philox_uniform": (ctypes.c_double, [_U64, _U64, _U32]),
@@ -258,6 +258,37 @@ class Sampler:
         _check("sixi_smp_verify", st)
         return dict(accepted=acc, tokens=toks, n_tokens=ntok, first_reject=frej, uniforms_used=used,
                     status=sts)
+
+    # -- vocab-sharded mode ----------------------------------------------------------------------
+    def shard_candidates(self, shard_logits, vocab_offset: int, shard_vocab: int, params, top_n: int = 64,
+                         masks=None, hist=None, hist_off=None, stream=None):
+        """Stage 1 on this rank's slice: shard_logits [n_rows, >= shard_vocab] (a column slice of the
+        full rows is fine). Returns (cand int32 [n_rows, top_n, 2] = (logit bits, id), stats uint8
+        [n_rows, 24])."""
+        import torch
+
+        n = shard_logits.shape[0]
+        cand = torch.empty((n, top_n, 2), dtype=torch.int32, device=shard_logits.device)
+        stats = torch.empty((n, 24), dtype=torch.uint8, device=shard_logits.device)
+        rows = self._rows(shard_logits)
+        st = _lib().sixi_smp_shard_candidates(self.h, ctypes.byref(rows), vocab_offset, shard_vocab, self.vocab,
+                                           _ptr(params), _ptr(masks), _ptr(hist), _ptr(hist_off), top_n,
+                                           _ptr(cand), _ptr(stats), self._stream(stream))
+        _check("sixi_smp_shard_candidates", st)
+        return cand, stats
+
+    def merge_shards(self, gathered_cand, gathered_stats, params, uniforms=None, step: int = 0, stream=None):
+        """Stage 2: gathered_cand [n_shards, n_rows, top_n, 2], gathered_stats [n_shards, n_rows, 24]."""
+        import torch
+
+        S, n, top_n = gathered_cand.shape[0], gathered_cand.shape[1], gathered_cand.shape[2]
+        tok = torch.empty(n, dtype=torch.int32, device=gathered_cand.device)
+        sts = torch.empty(n, dtype=torch.int32, device=gathered_cand.device)
+        st = _lib().sixi_smp_merge_shards(self.h, n, S, top_n, _ptr(gathered_cand), _ptr(gathered_stats),
+                                       _ptr(params), _ptr(uniforms), step, _ptr(tok), _ptr(sts),
+                                       self._stream(stream))
+        _check("sixi_smp_merge_shards", st)
+        return tok, sts
 
     # -- host-buffer entry point ---------------------------------------------------------------
     def sample_host(self, logits: np.ndarray, params: np.ndarray, masks=None, hist=None, hist_off=None,

@@ -106,12 +106,15 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def make_batches(seed: int):
+def make_batches(seed: int, rank: int = 0):
+    """Config-2 batches: one parameter mix and history set (from `seed`, the same on every rank, so
+    that every rank carries the same kind of work) and NBUF rotating logits batches per rank."""
     from sixi_smp import workloads as W
 
     base = W.config2(rows=ROWS, vocab=VOCAB, seed=seed)
-    rng = np.random.default_rng(seed + 17)
-    logits = [base["logits"]] + [W.config2_logits(rng, ROWS, VOCAB) for _ in range(NBUF - 1)]
+    rng = np.random.default_rng(seed + 17 + 7919 * rank)
+    first = base["logits"] if rank == 0 else W.config2_logits(rng, ROWS, VOCAB)
+    logits = [first] + [W.config2_logits(rng, ROWS, VOCAB) for _ in range(NBUF - 1)]
     uniforms = [rng.random(ROWS) for _ in range(NBUF)]
     return base, logits, uniforms
 
@@ -227,7 +230,7 @@ def main() -> int:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
-    base, logits, uniforms = make_batches(1000 + rank)
+    base, logits, uniforms = make_batches(1000, rank)
     d_logits = [torch.from_numpy(x).to(dev) for x in logits]
     d_u = [torch.from_numpy(u).to(dev) for u in uniforms]
     d_params = torch.from_numpy(base["params"].view(np.uint8)).to(dev)

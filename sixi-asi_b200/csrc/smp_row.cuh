@@ -1615,15 +1615,22 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     // counter, so the remote traffic is plain stores.
     const uint32_t gseg = static_cast<uint32_t>(kGCap) / C;
     auto gather = [&](int bA, int bufA, int bBlo, int bBhi, int bufB, unsigned long long lowb) {
-        // key intervals: bin bA, and bins bBlo..bBhi (empty when bBlo < 0)
-        const uint32_t kloA = static_cast<uint32_t>(first_key_bin_le(bA));
-        const unsigned long long khiA1 = first_key_bin_le(bA - 1);  // one past bin bA
-        uint32_t kloB = 1u;
-        unsigned long long khiB1 = 0ull;
-        if (bBlo >= 0) {
-            kloB = static_cast<uint32_t>(first_key_bin_le(bBhi));
-            khiB1 = first_key_bin_le(bBlo - 1);
+        // key intervals: bin bA, and bins bBlo..bBhi (empty when bBlo < 0); the four boundaries are
+        // computed at once by lane 0 of warps 0-3
+        if (tid < 128 && lane == 0) {
+            const int w = tid >> 5;
+            const int bb = w == 0 ? bA : (w == 1 ? bA - 1 : (w == 2 ? bBhi : bBlo - 1));
+            ls->bc[4 + w] = (w < 2 || bBlo >= 0) ? first_key_bin_le(bb) : 0ull;
         }
+        if (tid == 0) {
+            ls->gfill[0] = 0u;
+            ls->gfill[1] = 0u;
+        }
+        __syncthreads();
+        const uint32_t kloA = static_cast<uint32_t>(ls->bc[4]);
+        const unsigned long long khiA1 = ls->bc[5];  // one past bin bA
+        const uint32_t kloB = bBlo >= 0 ? static_cast<uint32_t>(ls->bc[6]) : 1u;
+        const unsigned long long khiB1 = bBlo >= 0 ? ls->bc[7] : 0ull;
         unsigned long long* gA = (bufA ? G1 : G0) + crank * gseg;
         unsigned long long* gB = (bufB ? G1 : G0) + crank * gseg;
         // Membership is one unsigned subtract-compare per interval; the composite lower bound is
@@ -1631,30 +1638,29 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         const uint32_t wA = static_cast<uint32_t>(khiA1 - kloA);
         const uint32_t wB = bBlo >= 0 ? static_cast<uint32_t>(khiB1 - kloB) : 0u;  // empty set B
         const bool use_lowb = lowb != 0ull;
-        // One pass: per key only the interval tests; a warp reserves slots (local counter) only on
-        // the rare iterations where one of its lanes holds a match.
-        if (tid == 0) {
-            ls->gfill[0] = 0u;
-            ls->gfill[1] = 0u;
-        }
-        __syncthreads();
+        // One pass of 8 keys per iteration: per key only the interval tests; a warp reserves slots
+        // (local counter) only on the rare iterations where one of its lanes holds a match. Keys
+        // past the chunk read as 0, which no interval contains.
+        const int nq8 = (nq + 1) >> 1;
+        const int it8 = (nq8 + kNT - 1) / kNT;
 #pragma unroll 1
-        for (int m = 0; m < nq_iter; ++m) {  // warp-uniform trip count
+        for (int m = 0; m < it8; ++m) {  // warp-uniform trip count
             const int q = tid + m * kNT;
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (q < nq) v = reinterpret_cast<const uint4*>(K)[q];
-            const uint32_t k4[4] = {v.x, v.y, v.z, v.w};
+            uint4 va = make_uint4(0u, 0u, 0u, 0u), vb = make_uint4(0u, 0u, 0u, 0u);
+            if (2 * q < nq) va = reinterpret_cast<const uint4*>(K)[2 * q];
+            if (2 * q + 1 < nq) vb = reinterpret_cast<const uint4*>(K)[2 * q + 1];
+            const uint32_t k8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
             uint32_t mA = 0u, mB = 0u;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                mA |= (k4[i] - kloA < wA) ? (1u << i) : 0u;
-                mB |= (k4[i] - kloB < wB) ? (1u << i) : 0u;
+            for (int i = 0; i < 8; ++i) {
+                mA |= (k8[i] - kloA < wA) ? (1u << i) : 0u;
+                mB |= (k8[i] - kloB < wB) ? (1u << i) : 0u;
             }
             if (__ballot_sync(0xFFFFFFFFu, (mA | mB) != 0u) == 0u) continue;
             if (use_lowb) {  // k-bound rows: drop entries below the composite bound
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    if (comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i)) < lowb) {
+                for (int i = 0; i < 8; ++i) {
+                    if (comp_of(k8[i], static_cast<uint32_t>(c0 + 8 * q + i)) < lowb) {
                         mA &= ~(1u << i);
                         mB &= ~(1u << i);
                     }
@@ -1666,7 +1672,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             while (mk != 0u) {
                 const int i = __ffs(mk) - 1;
                 mk &= mk - 1u;
-                const int e = 4 * q + i;
+                const int e = 8 * q + i;
                 const unsigned long long cp = comp_of(K[e], static_cast<uint32_t>(c0 + e));
                 if ((mA >> i) & 1u) {
                     if (pA < gseg) {

@@ -57,6 +57,7 @@ constexpr int kTB = 2048;       // bins of the per-thread-maximum histogram
 constexpr int kStages = 4;      // bulk-copy pipeline stages per chunk
 constexpr int kVecMax = 5;      // 16-byte vectors per thread per stage (bound, see plan)
 constexpr int kMaxRounds = 48;  // bound on the mass path's exchange rounds (normally 2-5)
+constexpr uint32_t kSmallSelect = kNT;  // selections over at most this many entries rank directly
 constexpr uint32_t kWaitIters = 1u << 24;
 constexpr uint32_t kNoList = 0xFFFFFFFFu;
 constexpr int kMaxSmem = 227 * 1024;       // per-block opt-in limit of sm_100
@@ -332,16 +333,33 @@ __device__ __forceinline__ unsigned long long block_select_small(const unsigned 
     uint32_t n = 0;
     const uint32_t pos = block_excl_u32<kNT>(valid ? 1u : 0u, ls->red32, &n);
     const unsigned long long we = valid ? (weighted ? weight_of(kval(comp_key(e)), wc) : 1ull) : 0ull;
-    if (valid) {
-        L[pos] = e;
-        W[pos] = we;
-    }
+    if (valid) L[pos] = e;
     if (tid == 0) ls->bc[3] = 0ull;
+    if (valid && (pos & 1u) == 0u && pos + 1u == n) L[n] = 0ull;  // pad the list to an even length
     __syncthreads();
-    uint32_t rank = 0;  // entries are unique: rank = number of larger entries
-    if (valid) {
-        for (uint32_t j = 0; j < n; ++j) rank += L[j] > e ? 1u : 0u;
+    // Entries are unique: rank = number of larger entries. `tpe` threads share one entry, each
+    // scanning a slice of the list two composites per load, and add their counts.
+    const uint32_t tpe = n <= kNT / 8 ? 8u : (n <= kNT / 4 ? 4u : (n <= kNT / 2 ? 2u : 1u));
+    uint32_t rank = 0;
+    {
+        const uint32_t me = static_cast<uint32_t>(tid) / tpe, part = static_cast<uint32_t>(tid) % tpe;
+        const unsigned long long c = me < n ? L[me] : ~0ull;
+        const uint32_t half = (n + 1u) / 2u;  // pairs
+        const uint32_t per = (half + tpe - 1u) / tpe;
+        const uint32_t j0 = part * per, j1 = (j0 + per < half) ? j0 + per : half;
+        uint32_t r = 0;
+        const ulonglong2* L2 = reinterpret_cast<const ulonglong2*>(L);
+        for (uint32_t j = j0; j < j1; ++j) {
+            const ulonglong2 v = L2[j];
+            r += (v.x > c ? 1u : 0u) + (v.y > c ? 1u : 0u);
+        }
+        for (uint32_t o = 1; o < tpe; o <<= 1) r += __shfl_xor_sync(0xFFFFFFFFu, r, o);
+        // the rank of entry `me` sits in every thread of its group; hand it to the entry's owner
+        // W is free until the scatter (the weights stay in registers): it carries the ranks
+        if (part == 0u && me < n) reinterpret_cast<uint32_t*>(W)[me] = r;
     }
+    __syncthreads();
+    if (valid) rank = reinterpret_cast<const uint32_t*>(W)[pos];
     __syncthreads();
     if (valid) {
         L[rank] = e;
@@ -383,7 +401,7 @@ __device__ __forceinline__ unsigned long long block_select(const unsigned long l
     {
         uint32_t total = 0;
         for (uint32_t q = 0; q < C; ++q) total += cnt[q];
-        if (total <= static_cast<uint32_t>(kNT))
+        if (total <= kSmallSelect)
             return block_select_small(g, cnt, C, seg, target, wc, weighted, lowb, excl, hz, ls, cum_through);
     }
     for (int i = tid; i < 1024; i += kNT) hz[i] = 0u;  // level-0 buffer
@@ -840,12 +858,19 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     const bool has_mask = rc.mask != nullptr;
     const bool use_pbits = rc.pen && !pen_smem;
     uint32_t t_mk = 0u, t_mi = 0u, t_mn = 0xFFFFFFFFu, t_amax = 0u;
-#define SIXI_ADMIT(E, XV, MBIT, PBIT, KOUT)                                                   \
+    bool t_bad = false;  // an allowed raw logit is NaN or infinite (modes that do not track t_amax)
+    // Entries of inactive rows are never allowed (MBIT is 0 for them). AMAX: track the largest
+    // |bits| (raw-argmax modes, whose NaN keys are 0, and the frequency path); elsewhere a
+    // non-finite raw logit shows up in the key extremes (see t_bad).
+    const uint32_t act = len > 0 ? 0xFFFFFFFFu : 0u;
+#define SIXI_ADMIT(E, XV, MBIT, PBIT, KOUT, AMAX)                                             \
     {                                                                                        \
         float x_ = (XV);                                                                     \
-        const bool ok_ = (MBIT) && (E) < len;                                                \
-        const uint32_t raw_ = __float_as_uint(x_) & 0x7FFFFFFFu;                             \
-        t_amax = (ok_ && raw_ > t_amax) ? raw_ : t_amax;                                     \
+        const bool ok_ = (MBIT);                                                             \
+        if (AMAX) {                                                                          \
+            const uint32_t raw_ = __float_as_uint(x_) & 0x7FFFFFFFu;                         \
+            t_amax = (ok_ && raw_ > t_amax) ? raw_ : t_amax;                                 \
+        }                                                                                    \
         x_ = __fadd_rn(x_, 0.0f);                                                            \
         const uint32_t b_ = __float_as_uint(x_);                                             \
         uint32_t k_ = b_ ^ (static_cast<uint32_t>(static_cast<int32_t>(b_) >> 31) | 0x80000000u); \
@@ -880,16 +905,16 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                     if (v < v1) {
                         const int32_t e0 = v * 8;
                         const uint32_t g = static_cast<uint32_t>(c0 + e0);
-                        const uint32_t mb = has_mask ? (mw[(g >> 5) - wbase] >> (g & 31)) & 0xFFu : 0xFFu;
+                        const uint32_t mb = (has_mask ? (mw[(g >> 5) - wbase] >> (g & 31)) & 0xFFu : 0xFFu) & act;
                         const uint32_t pb = use_pbits ? (hb[e0 >> 5] >> (e0 & 31)) & 0xFFu : 0u;
                         const uint32_t w4[4] = {raw4[m].x, raw4[m].y, raw4[m].z, raw4[m].w};
                         uint32_t k8[8];
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             SIXI_ADMIT(e0 + 2 * i, __uint_as_float(w4[i] << 16), (mb >> (2 * i)) & 1u,
-                                       (pb >> (2 * i)) & 1u, k8[2 * i]);
+                                       (pb >> (2 * i)) & 1u, k8[2 * i], kRaw);
                             SIXI_ADMIT(e0 + 2 * i + 1, __uint_as_float(w4[i] & 0xFFFF0000u), (mb >> (2 * i + 1)) & 1u,
-                                       (pb >> (2 * i + 1)) & 1u, k8[2 * i + 1]);
+                                       (pb >> (2 * i + 1)) & 1u, k8[2 * i + 1], kRaw);
                         }
                         *reinterpret_cast<uint4*>(K + e0) = make_uint4(k8[0], k8[1], k8[2], k8[3]);
                         *reinterpret_cast<uint4*>(K + e0 + 4) = make_uint4(k8[4], k8[5], k8[6], k8[7]);
@@ -904,13 +929,13 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                         const float4 f = *reinterpret_cast<const float4*>(stg + 16u * v);
                         const int32_t e0 = v * 4;
                         const uint32_t g = static_cast<uint32_t>(c0 + e0);
-                        const uint32_t mb = has_mask ? (mw[(g >> 5) - wbase] >> (g & 31)) & 0xFu : 0xFu;
+                        const uint32_t mb = (has_mask ? (mw[(g >> 5) - wbase] >> (g & 31)) & 0xFu : 0xFu) & act;
                         const uint32_t pb = use_pbits ? (hb[e0 >> 5] >> (e0 & 31)) & 0xFu : 0u;
                         uint32_t k0, k1, k2, k3;
-                        SIXI_ADMIT(e0 + 0, f.x, mb & 1u, pb & 1u, k0);
-                        SIXI_ADMIT(e0 + 1, f.y, (mb >> 1) & 1u, (pb >> 1) & 1u, k1);
-                        SIXI_ADMIT(e0 + 2, f.z, (mb >> 2) & 1u, (pb >> 2) & 1u, k2);
-                        SIXI_ADMIT(e0 + 3, f.w, (mb >> 3) & 1u, (pb >> 3) & 1u, k3);
+                        SIXI_ADMIT(e0 + 0, f.x, mb & 1u, pb & 1u, k0, kRaw);
+                        SIXI_ADMIT(e0 + 1, f.y, (mb >> 1) & 1u, (pb >> 1) & 1u, k1, kRaw);
+                        SIXI_ADMIT(e0 + 2, f.z, (mb >> 2) & 1u, (pb >> 2) & 1u, k2, kRaw);
+                        SIXI_ADMIT(e0 + 3, f.w, (mb >> 3) & 1u, (pb >> 3) & 1u, k3, kRaw);
                         *reinterpret_cast<uint4*>(K + e0) = make_uint4(k0, k1, k2, k3);
                     }
                 }
@@ -926,9 +951,12 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             const uint32_t mb = allowed(c0 + e) ? 1u : 0u;
             const uint32_t pb = use_pbits ? (hb[e >> 5] >> (e & 31)) & 1u : 0u;
             uint32_t k;
-            SIXI_ADMIT(e, x, mb, pb, k);
+            SIXI_ADMIT(e, x, mb, pb, k, kRaw);
             K[e] = k;
         }
+        // raw non-finite values of the entries seen so far (penalised entries are checked below,
+        // on their raw keys, before a penalty could overflow them)
+        if (!kRaw) t_bad = t_mk >= 0xFF800000u || t_mn <= 0x007FFFFFu;
         if (use_pbits) {
             // sparse penalty fix-up: each penalised id once (test-and-clear on the bitmap)
             __syncthreads();
@@ -941,6 +969,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 if (!(hb[e >> 5] & bit)) continue;
                 const uint32_t old = atomicAnd(&hb[e >> 5], ~bit);
                 if (!(old & bit)) continue;
+                if (!kRaw && (K[e] >= 0xFF800000u || K[e] <= 0x007FFFFFu)) t_bad = true;
                 float v = kval(K[e]);
                 if (rep != 1.0f && rep > 0.0f) v = (v < 0.0f) ? __fmul_rn(v, rep) : __fdiv_rn(v, rep);
                 v = __fsub_rn(v, pres);
@@ -1006,7 +1035,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         __syncthreads();
         for (int32_t e = tid; e < len; e += kNT) {
             uint32_t k;
-            SIXI_ADMIT(e, KF[e], allowed(c0 + e) ? 1u : 0u, 0u, k);
+            SIXI_ADMIT(e, KF[e], allowed(c0 + e) ? 1u : 0u, 0u, k, true);
             K[e] = k;
         }
     }
@@ -1026,15 +1055,17 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         const uint32_t wam = __reduce_max_sync(0xFFFFFFFFu, t_amax);
         const uint32_t wcn = __reduce_add_sync(0xFFFFFFFFu, t_cnt);
         const uint32_t wfi = __reduce_min_sync(0xFFFFFFFFu, t_first);
+        const uint32_t wbad = __reduce_or_sync(0xFFFFFFFFu, t_bad ? 1u : 0u);
         if (lane == 0) {
             ls->red[w * 8 + 0] = (static_cast<unsigned long long>(wmk) << 32) | wmi;
             ls->red[w * 8 + 1] = wmn;
             ls->red[w * 8 + 2] = wam;
             ls->red[w * 8 + 3] = wcn;
             ls->red[w * 8 + 4] = wfi;
+            ls->red[w * 8 + 5] = wbad;
         }
         __syncthreads();
-        uint32_t mk = 0u, mi = 0xFFFFFFFFu, mn = 0xFFFFFFFFu, am = 0u, cn = 0u, fi = 0xFFFFFFFFu;
+        uint32_t mk = 0u, mi = 0xFFFFFFFFu, mn = 0xFFFFFFFFu, am = 0u, cn = 0u, fi = 0xFFFFFFFFu, bd = 0u;
 #pragma unroll
         for (int q = 0; q < kNW; ++q) {
             const uint32_t k = static_cast<uint32_t>(ls->red[q * 8 + 0] >> 32);
@@ -1047,13 +1078,14 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             am = static_cast<uint32_t>(ls->red[q * 8 + 2]) > am ? static_cast<uint32_t>(ls->red[q * 8 + 2]) : am;
             cn += static_cast<uint32_t>(ls->red[q * 8 + 3]);
             fi = static_cast<uint32_t>(ls->red[q * 8 + 4]) < fi ? static_cast<uint32_t>(ls->red[q * 8 + 4]) : fi;
+            bd |= static_cast<uint32_t>(ls->red[q * 8 + 5]);
         }
         RowStat st;
         st.best = (mk != 0u) ? comp_of(mk, static_cast<uint32_t>(c0) + mi) : 0ull;
         st.min_key = mn;
         st.n_allowed = cn;
         st.first = fi;
-        st.flags = (am >= 0x7F800000u ? 1u : 0u) | (ls->bc[15] ? 2u : 0u);
+        st.flags = (am >= 0x7F800000u || bd != 0u ? 1u : 0u) | (ls->bc[15] ? 2u : 0u);
         if (kRaw && fi != 0xFFFFFFFFu && K[fi - static_cast<uint32_t>(c0)] == 0u) st.flags |= 4u;
         st.dhas = (rc.draft >= c0 && rc.draft < c0 + len) ? 1u : 0u;
         st.dkey = st.dhas ? K[rc.draft - c0] : 0u;

@@ -203,6 +203,128 @@ def run_reference(args) -> int:
     return 0
 
 
+def _graph_ms(step, steps: int, warmup: int, stream) -> float:
+    """Runs `warmup` steps eagerly, captures `steps` steps in one CUDA graph and returns the CUDA-
+    event time of its replay on `stream` (ms)."""
+    import torch
+
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            step(i)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(steps):
+            step(i)
+    with torch.cuda.stream(stream):
+        graph.replay()
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def run_workload(args) -> int:
+    """The other configurations of the path on one GPU (reported beside the config-2 line):
+    config1 single-row latency, config3 grammar-masked batch, config4 speculative verification."""
+    import torch
+
+    import sixi_smp as S
+    from sixi_smp import workloads as W
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(device=dev)
+    peak, peak_kind = peaks()
+
+    def t(x):
+        if x is None:
+            return None
+        if x.dtype.names is not None:
+            return torch.from_numpy(np.ascontiguousarray(x).view(np.uint8)).to(dev)
+        if x.dtype == np.uint32:
+            return torch.from_numpy(x.view(np.int32)).to(dev)
+        if x.dtype == np.uint16:
+            return torch.from_numpy(x.view(np.int16)).to(dev).view(torch.bfloat16)
+        return torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+
+    if args.workload in ("config1", "config3"):
+        one = args.workload == "config1"
+        rows = 1 if one else ROWS
+        nbuf = NBUF
+        if one:
+            ds = [W.config1(seed=11 + i) for i in range(nbuf)]
+            base = ds[0]
+            logits = [t(x["logits"]) for x in ds]
+        else:
+            base = W.config3(rows=ROWS, vocab=VOCAB, seed=3)
+            rng = np.random.default_rng(33)
+            logits = [t(base["logits"])] + [t(W.config2_logits(rng, ROWS, VOCAB)) for _ in range(nbuf - 1)]
+        params, masks = t(base["params"]), t(base["masks"])
+        hist, hoff = t(base["hist"]), t(base["hist_off"])
+        u = [torch.rand(rows, dtype=torch.float64, device=dev) for _ in range(nbuf)]
+        smp = S.Sampler(0, 64, VOCAB)
+        tok = torch.empty(rows, dtype=torch.int32, device=dev)
+        sts = torch.empty(rows, dtype=torch.int32, device=dev)
+
+        def step(i):
+            smp.sample(logits[i % nbuf], params, masks=masks, hist=hist, hist_off=hoff, uniforms=u[i % nbuf],
+                       out_tokens=tok, out_status=sts, stream=torch.cuda.current_stream())
+
+        ms = _graph_ms(step, args.steps, args.warmup, stream)
+        nbytes = rows * VOCAB * 4 + 4 * int(base["hist_off"][-1]) + (0 if masks is None else masks.numel() * 4)
+        unit, value = ("us/step", 1e3 * ms / args.steps) if one else ("rows/s", rows * args.steps / (ms / 1e3))
+        metric = ("single-row sampler step latency (config 1), V=151,936 fp32" if one else
+                  "sampled rows/s at B=32,V=151,936 fp32 with grammar masks (config 3)")
+        data = ("synthetic; 16 rotating rows (9.7 MB, L2-resident)" if one else
+                "synthetic; 16 rotating batches (311 MB > L2), one mask set")
+        launches = args.steps
+    elif args.workload == "config4":
+        streams, k = 32, 8
+        nbuf = 2
+        ds = [W.config4(streams=streams, k=k, vocab=VOCAB, seed=40 + i, stochastic=True, masked=True)
+              for i in range(nbuf)]
+        tgt = [t(x["target_bits"]) for x in ds]
+        q = [t(x["q"]) for x in ds]
+        dr = [t(x["drafts"]) for x in ds]
+        params, masks = t(ds[0]["params"]), t(ds[0]["masks"])
+        hist, hoff = t(ds[0]["hist"]), t(ds[0]["hist_off"])
+        u = [t(x["uniforms"]) for x in ds]
+        smp = S.Sampler(0, streams * (k + 1), VOCAB)
+
+        def step(i):
+            smp.verify(tgt[i % nbuf], dr[i % nbuf], params, draft_probs=q[i % nbuf], masks=masks, hist=hist,
+                       hist_off=hoff, uniforms=u[i % nbuf], stream=torch.cuda.current_stream())
+
+        ms = _graph_ms(step, args.steps, args.warmup, stream)
+        nbytes = (streams * (k + 1) * VOCAB * 2 + streams * k * VOCAB * 4 + masks.numel() * 4 + streams * k * 4 +
+                  4 * int(ds[0]["hist_off"][-1]))
+        unit, value = "stream-steps/s", streams * args.steps / (ms / 1e3)
+        metric = "speculative verify stream-steps/s (config 4: S=32, k=8, V=151,936, bf16 target, fp32 q)"
+        data = "synthetic; 2 rotating batches (491 MB > L2)"
+        launches = 2 * args.steps  # row kernel + per-stream finalize
+    else:
+        raise SystemExit(f"unknown workload {args.workload}")
+    per_launch_s = ms / 1e3 / args.steps
+    achieved = nbytes / per_launch_s / 1e9
+    line = {
+        "metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": unit != "us/step", "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if args.workload != "config4" else "bf16", "data": data,
+        "config": {"workload": args.workload},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "peak_source": peak_kind, "bytes_per_launch": int(nbytes)},
+        "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+    smp.close()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -212,10 +334,14 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", default="config2", choices=["config2", "config1", "config3", "config4"],
+                    help="config2 is the headline line; the others are reported beside it (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "config2":
+        return run_workload(args)
 
     import torch
     import torch.distributed as dist

@@ -304,6 +304,59 @@ __device__ __forceinline__ uint32_t warp_reserve(uint32_t n, unsigned int* count
 }
 
 // ---------------------------------------------------------------------------------------------
+// The selection below for at most 32 entries in total (block-wide call, one warp works): lane i
+// takes the i-th entry, ranks come from 32 shuffles, the entries are put in order through a
+// shared scratch and one warp prefix sum finds the crossing; a single barrier publishes the
+// result. Same contract as block_select.
+__device__ __forceinline__ unsigned long long block_select_tiny(const unsigned long long* g, const unsigned int* cnt,
+                                                               uint32_t C, uint32_t seg,
+                                                               unsigned long long target, const WeightCtx wc,
+                                                               bool weighted, unsigned long long lowb,
+                                                               unsigned long long excl, LocalShared* ls,
+                                                               unsigned long long* cum_through) {
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        uint32_t t = static_cast<uint32_t>(lane), q = 0;
+        for (; q < C; ++q) {
+            if (t < cnt[q]) break;
+            t -= cnt[q];
+        }
+        unsigned long long e = 0ull;
+        if (q < C) {
+            e = g[q * seg + t];
+            if (e < lowb || e == excl) e = 0ull;  // 0 sorts below every entry and weighs nothing
+        }
+        const unsigned long long w = e ? (weighted ? weight_of(kval(comp_key(e)), wc) : 1ull) : 0ull;
+        uint32_t rank = 0;  // unique: equal zeros are ordered by lane
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j) {
+            const unsigned long long o = __shfl_sync(0xFFFFFFFFu, e, j);
+            rank += (o > e || (o == e && j < lane)) ? 1u : 0u;
+        }
+        unsigned long long* S = ls->red;  // 64 of its words; the other warps wait at the barrier
+        S[rank] = e;
+        S[32 + rank] = w;
+        __syncwarp();
+        const unsigned long long es = S[lane], ws = S[32 + lane];
+        const unsigned long long cum = warp_incl_u64(ws);
+        const unsigned ball = __ballot_sync(0xFFFFFFFFu, ws > 0ull && cum >= target && cum - ws < target);
+        const int src = ball ? __ffs(ball) - 1 : 0;
+        const unsigned long long se = __shfl_sync(0xFFFFFFFFu, es, src);
+        const unsigned long long sc = __shfl_sync(0xFFFFFFFFu, cum, src);
+        __syncwarp();
+        if (lane == 0) {
+            ls->bc[3] = ball ? se : 0ull;
+            ls->bc[4] = sc;
+        }
+    }
+    __syncthreads();
+    const unsigned long long sel = ls->bc[3];
+    *cum_through = sel ? ls->bc[4] : 0ull;
+    __syncthreads();  // ls->red and ls->bc are free again
+    return sel;
+}
+
+// ---------------------------------------------------------------------------------------------
 // The selection below for at most kNT entries in total (block-wide, all threads call): one entry
 // per thread, compacted; its rank is the number of larger entries (a broadcast scan of the list);
 // the entries are scattered into descending order and one block prefix sum of their weights finds
@@ -401,6 +454,8 @@ __device__ __forceinline__ unsigned long long block_select(const unsigned long l
     {
         uint32_t total = 0;
         for (uint32_t q = 0; q < C; ++q) total += cnt[q];
+        if (total <= 32u)
+            return block_select_tiny(g, cnt, C, seg, target, wc, weighted, lowb, excl, ls, cum_through);
         if (total <= kSmallSelect)
             return block_select_small(g, cnt, C, seg, target, wc, weighted, lowb, excl, hz, ls, cum_through);
     }

@@ -1013,30 +1013,30 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         // on their raw keys, before a penalty could overflow them)
         if (!kRaw) t_bad = t_mk >= 0xFF800000u || t_mn <= 0x007FFFFFu;
         if (use_pbits) {
-            // sparse penalty fix-up: each penalised id once (test-and-clear on the bitmap)
+            // sparse penalty fix-up: each set bit of the history bitmap is one unique allowed id of
+            // this chunk (no second pass over the history in global memory)
             __syncthreads();
             const float rep = P->repetition_penalty, pres = P->presence_penalty;
-            for (int64_t j = tid; j < nht; j += kNT) {
-                const int32_t t = hist_at(rc, j);
-                if (t < c0 || t >= c0 + len) continue;
-                const int32_t e = t - c0;
-                const uint32_t bit = 1u << (e & 31);
-                if (!(hb[e >> 5] & bit)) continue;
-                const uint32_t old = atomicAnd(&hb[e >> 5], ~bit);
-                if (!(old & bit)) continue;
-                if (!kRaw && (K[e] >= 0xFF800000u || K[e] <= 0x007FFFFFu)) t_bad = true;
-                float v = kval(K[e]);
-                if (rep != 1.0f && rep > 0.0f) v = (v < 0.0f) ? __fmul_rn(v, rep) : __fdiv_rn(v, rep);
-                v = __fsub_rn(v, pres);
-                v = __fadd_rn(v, 0.0f);
-                const uint32_t b = __float_as_uint(v);
-                uint32_t k = b ^ (static_cast<uint32_t>(static_cast<int32_t>(b) >> 31) | 0x80000000u);
-                K[e] = k;
-                if (k > t_mk || (k == t_mk && static_cast<uint32_t>(e) < t_mi)) {
-                    t_mk = k;
-                    t_mi = static_cast<uint32_t>(e);
+            const int nbits = (len + 31) >> 5;
+            for (int wi = tid; wi < nbits; wi += kNT) {
+                uint32_t bits = hb[wi];
+                while (bits != 0u) {
+                    const int e = (wi << 5) + __ffs(bits) - 1;
+                    bits &= bits - 1u;
+                    if (!kRaw && (K[e] >= 0xFF800000u || K[e] <= 0x007FFFFFu)) t_bad = true;
+                    float v = kval(K[e]);
+                    if (rep != 1.0f && rep > 0.0f) v = (v < 0.0f) ? __fmul_rn(v, rep) : __fdiv_rn(v, rep);
+                    v = __fsub_rn(v, pres);
+                    v = __fadd_rn(v, 0.0f);
+                    const uint32_t b = __float_as_uint(v);
+                    uint32_t k = b ^ (static_cast<uint32_t>(static_cast<int32_t>(b) >> 31) | 0x80000000u);
+                    K[e] = k;
+                    if (k > t_mk || (k == t_mk && static_cast<uint32_t>(e) < t_mi)) {
+                        t_mk = k;
+                        t_mi = static_cast<uint32_t>(e);
+                    }
+                    t_mn = (k != 0u && k < t_mn) ? k : t_mn;
                 }
-                t_mn = (k != 0u && k < t_mn) ? k : t_mn;
             }
         }
     } else {

@@ -228,3 +228,24 @@ def test_philox_matches_host():
 
     p = binding.port()
     assert vals == [p.philox_uniform(123, 7, s) for s in range(4)]
+
+
+@pytest.mark.parametrize("vocab", [200_003, 262_144, 600_000])
+def test_large_vocab_wide_clusters(port, vocab):
+    """Vocabularies that need clusters of 8 (262,144) and 16 (600,000) CTAs per row."""
+    rng = np.random.default_rng(vocab)
+    rows = 6
+    d = rand_small_case(rng, vocab, rows, "f32")
+    lens = rng.integers(0, 3000, size=rows)
+    off = np.zeros(rows + 1, dtype=np.int64)
+    off[1:] = np.cumsum(lens)
+    d["hist"] = rng.integers(-2, vocab + 2, size=int(off[-1]), dtype=np.int32)
+    d["hist_off"] = off
+    u = rng.random(rows)
+    tok, st = run_sample(d, u)
+    check_against_oracle(port, d, u, tok, st)
+    smp = sampler(vocab)
+    g, gs = smp.greedy_argmax(dev(d["logits"]))
+    torch.cuda.synchronize()
+    for r in range(rows):
+        assert int(g[r]) == port.greedy_argmax(d["logits"][r]), r

@@ -182,6 +182,17 @@ SIXI_SMP_API int32_t sixi_smp_verify(sixi_smp* h, const sixi_smp_rows* target, c
                         int32_t* out_uniforms_used, int32_t* out_status, void* stream);
 
 /*
+ * Full-vocabulary softmax of each row: DeterministicSampler::compute_full_distribution
+ * (src/core/core_execution.cpp:409-447), the producer of dense draft distributions
+ * (src/speculative/speculative.cpp:279-280). temperatures [n_rows] (device); out_probs
+ * [n_rows][out_stride] fp32 (out_stride >= vocab). temperature <= 0 writes a one-hot row at the raw
+ * argmax (sample_greedy_argmax); otherwise float(exp(x / T - max) / sum) with fp64 terms, and all
+ * zeros when the row holds a NaN or +inf, as the engine leaves it.
+ */
+SIXI_SMP_API int32_t sixi_smp_full_distribution(sixi_smp* h, const sixi_smp_rows* rows, const float* temperatures,
+                                   float* out_probs, uint64_t out_stride, void* stream);
+
+/*
  * sixi_smp_verify without a handle and without any allocation (no counterpart in the engine).
  * For callers that may not allocate device memory at all - for instance a serving loop whose
  * device memory is owned by an external allocator, or one that must not call into the CUDA

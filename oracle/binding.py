@@ -26,6 +26,8 @@ _U32 = ctypes.c_uint32
 _U64 = ctypes.c_uint64
 
 _SIGS = {
+    "orc_full_distribution": (None, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float,
+                                     ctypes.c_void_p]),
     "orc_kind": (_I32, []),
     "orc_philox_uniform": (ctypes.c_double, [_U64, _U64, _U32]),
     "orc_greedy_argmax": (_I32, [_P, _U64]),
@@ -106,6 +108,12 @@ class Oracle:
         self.lib.orc_sample_batch(_p(logits), _dtype_of(logits), n, stride, vocab, _p(params), _p(masks),
                                   _p(hist), _p(hist_off), _p(uniforms), step, _p(tok), _p(sts), n_threads)
         return tok, sts
+
+    def full_distribution(self, row: np.ndarray, temperature: float) -> np.ndarray:
+        row = np.ascontiguousarray(row)
+        out = np.zeros(row.size, dtype=np.float32)
+        self.lib.orc_full_distribution(_p(row), _dtype_of(row), row.size, ctypes.c_float(temperature), _p(out))
+        return out
 
     def verify(self, target: np.ndarray, drafts: np.ndarray, params: np.ndarray, q=None, n_drafts=None,
                masks=None, hist=None, hist_off=None, uniforms=None, step: int = 0, n_threads: int = 0,

@@ -183,6 +183,15 @@ EXPORT int32_t orc_greedy_argmax(const float* logits, uint64_t vocab) {
     return DeterministicSampler::sample_greedy_argmax(logits, vocab);
 }
 
+EXPORT void orc_full_distribution(const void* row, uint32_t dtype, uint64_t vocab, float temperature,
+                                  float* out) {
+    std::vector<float> x;
+    load_row(row, dtype, vocab, x);
+    std::vector<float> probs;
+    DeterministicSampler::compute_full_distribution(x.data(), vocab, temperature, probs);
+    for (uint64_t i = 0; i < vocab; ++i) out[i] = i < probs.size() ? probs[i] : 0.0f;
+}
+
 EXPORT int32_t orc_greedy_row(const void* row, uint32_t dtype, uint64_t vocab,
                               const uint32_t* mask, int32_t* out_token) {
     return greedy_row(row, dtype, vocab, mask, out_token);

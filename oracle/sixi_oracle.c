@@ -103,6 +103,42 @@ int32_t orc_greedy_argmax(const float* logits, uint64_t vocab) {
     return best_id;
 }
 
+/* compute_full_distribution (core_execution.cpp:409-447): the scaled maximum ignores NaN; a NaN
+ * or +inf logit makes the sum NaN and every probability 0. Built with -ffp-contract=off like the
+ * engine, so x * inv_temp - max is a multiply then a subtract. */
+void orc_full_distribution(const void* row, uint32_t dtype, uint64_t vocab, float temperature, float* out) {
+    for (uint64_t i = 0; i < vocab; ++i) out[i] = 0.0f;
+    if (row == NULL || vocab == 0) return;
+    float* x = (float*)malloc(vocab * sizeof(float));
+    double* e = (double*)malloc(vocab * sizeof(double));
+    if (x == NULL || e == NULL) {
+        free(x);
+        free(e);
+        return;
+    }
+    load_row(row, dtype, vocab, x);
+    if (temperature <= 0.0f) {
+        out[orc_greedy_argmax(x, vocab)] = 1.0f;
+    } else {
+        const double inv_temp = 1.0 / (double)temperature;
+        double max_scaled = -INFINITY;
+        for (uint64_t i = 0; i < vocab; ++i) {
+            const double s = (double)x[i] * inv_temp;
+            if (s > max_scaled) max_scaled = s;
+        }
+        double sum = 0.0;
+        for (uint64_t i = 0; i < vocab; ++i) {
+            e[i] = exp((double)x[i] * inv_temp - max_scaled);
+            sum += e[i];
+        }
+        if (sum > 0.0) {
+            for (uint64_t i = 0; i < vocab; ++i) out[i] = (float)(e[i] / sum);
+        }
+    }
+    free(x);
+    free(e);
+}
+
 /* argmax of the compacted allowed logits (first allowed element plays the role of index 0) */
 static int32_t masked_argmax(const float* x, uint64_t vocab, const uint32_t* mask) {
     int32_t best_id = -1;

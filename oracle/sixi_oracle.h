@@ -61,6 +61,10 @@ int32_t orc_sample_batch(const void* logits, uint32_t dtype, uint32_t n_rows, ui
                          const double* uniforms, uint64_t step, int32_t* out_tokens,
                          int32_t* out_status, int32_t n_threads);
 
+/* compute_full_distribution (core_execution.cpp:409-447) of one row: temperature <= 0 gives a
+ * one-hot at the raw argmax; otherwise float(exp(x/T - max) / sum) with fp64 terms. */
+void orc_full_distribution(const void* row, uint32_t dtype, uint64_t vocab, float temperature, float* out);
+
 /* Speculative verification, same layout and semantics as sixi_smp_verify (host memory). */
 int32_t orc_verify(const void* target, uint32_t dtype, uint64_t row_stride, uint64_t vocab,
                    const float* draft_probs, const int32_t* drafts, const int32_t* n_drafts,

@@ -360,6 +360,28 @@ int32_t sixi_smp_verify(sixi_smp* h, const sixi_smp_rows* target, const float* d
     return from_cuda(e);
 }
 
+int32_t sixi_smp_full_distribution(sixi_smp* h, const sixi_smp_rows* rows, const float* temperatures,
+                                   float* out_probs, uint64_t out_stride, void* stream) {
+    if (h == nullptr || !rows_ok(h, rows) || temperatures == nullptr || out_probs == nullptr ||
+        out_stride < h->vocab)
+        return SIXI_INVALID_ARGUMENT;
+    if (rows->n_rows == 0) return SIXI_OK;
+    DeviceGuard g(h->device);
+    LaunchPlan plan{};
+    if (!sixi_b200::plan_rows(h->vocab, rows->n_rows, &plan)) return SIXI_INVALID_ARGUMENT;
+    sixi_b200::DistArgs a{};
+    a.data = rows->data;
+    a.row_stride = rows->row_stride;
+    a.dtype = rows->dtype;
+    a.vocab = h->vocab;
+    a.n_rows = rows->n_rows;
+    a.chunk = plan.chunk;
+    a.temperatures = temperatures;
+    a.out = out_probs;
+    a.out_stride = out_stride;
+    return from_cuda(sixi_b200::launch_full_distribution(a, plan, static_cast<cudaStream_t>(stream)));
+}
+
 int32_t sixi_smp_verify_static(int32_t device, uint32_t vocab, const sixi_smp_rows* target,
                                const float* draft_probs, const int32_t* drafts, const int32_t* n_drafts,
                                uint32_t n_streams, uint32_t k, const sixi_smp_params* params,

@@ -1,0 +1,184 @@
+// smp_dist.cu - full-vocabulary softmax rows (sixi_smp_full_distribution), the producer of dense
+// draft distributions: DeterministicSampler::compute_full_distribution
+// (src/core/core_execution.cpp:409-447) per row, with one cluster of CTAs per row.
+//
+//   temperature <= 0  a one-hot row at the raw argmax (strict >, so the lowest id wins ties, a NaN
+//                     at index 0 wins and other NaNs never do; sample_greedy_argmax)
+//   otherwise         float(exp(x / T - max) / sum) with fp64 terms: max over x * (1 / T) (NaN
+//                     ignored); a NaN or +inf logit makes the sum NaN and the engine leaves every
+//                     probability 0, as here. The per-element operations are the engine's (a
+//                     multiply, then a subtract, no contraction); the sum runs in parallel, so it
+//                     differs from the engine's sequential sum only by fp64 rounding.
+#include <cooperative_groups.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cfloat>
+#include <cstdint>
+
+#include "../../include/sixi_smp.h"
+#include "smp_device.cuh"
+#include "smp_kernels.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace sixi_b200 {
+namespace {
+
+constexpr int kDT = 512;
+constexpr int kDW = kDT / 32;
+constexpr int kDMaxC = 16;
+
+struct DistShared {
+    double mx[kDMaxC];               // per-CTA scaled maxima (pushed by every CTA)
+    double sm[kDMaxC];               // per-CTA partial sums
+    unsigned int bad[kDMaxC];        // per-CTA NaN / +inf flags
+    unsigned long long best[kDMaxC]; // per-CTA argmax composites (greedy rows)
+    double redd[kDW];
+    unsigned long long red[kDW];
+    unsigned int redu[kDW];
+};
+
+__device__ __forceinline__ float dist_logit(const DistArgs& a, const uint8_t* row, uint32_t e) {
+    if (a.dtype == SIXI_SMP_BF16)
+        return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(row)[e]) << 16);
+    return reinterpret_cast<const float*>(row)[e];
+}
+
+__global__ void __launch_bounds__(kDT, 1) dist_kernel(const DistArgs a) {
+    __shared__ DistShared sh;
+    cg::cluster_group cluster = cg::this_cluster();
+    const uint32_t C = cluster.num_blocks();
+    const uint32_t crank = cluster.block_rank();
+    const uint32_t row = blockIdx.x / C;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const uint8_t* rowp = static_cast<const uint8_t*>(a.data) +
+                          static_cast<size_t>(row) * a.row_stride * (a.dtype == SIXI_SMP_BF16 ? 2 : 4);
+    float* out = a.out + static_cast<size_t>(row) * a.out_stride;
+    const uint32_t c0 = crank * a.chunk;
+    const uint32_t c1 = c0 + a.chunk < a.vocab ? c0 + a.chunk : a.vocab;
+    const float T = a.temperatures[row];
+    if (T <= 0.0f) {
+        // raw argmax: the composite (key, id) with NaN excluded; a NaN at index 0 is the answer
+        unsigned long long best = 0ull;
+        for (uint32_t e = c0 + tid; e < c1; e += kDT) {
+            const float x = dist_logit(a, rowp, e);
+            if (x != x) continue;
+            const unsigned long long c = comp_of(fkey(x), e);
+            best = c > best ? c : best;
+        }
+        best = warp_max_u64(best);
+        if (lane == 0) sh.red[w] = best;
+        __syncthreads();
+        if (tid == 0) {
+            unsigned long long b = 0ull;
+            for (int i = 0; i < kDW; ++i) b = sh.red[i] > b ? sh.red[i] : b;
+            for (uint32_t q = 0; q < C; ++q) cluster.map_shared_rank(&sh, q)->best[crank] = b;
+        }
+        cluster.sync();
+        unsigned long long b = 0ull;
+        for (uint32_t q = 0; q < C; ++q) b = sh.best[q] > b ? sh.best[q] : b;
+        const float x0 = dist_logit(a, rowp, 0);
+        const uint32_t win = (x0 != x0 || b == 0ull) ? 0u : comp_id(b);
+        for (uint32_t e = c0 + tid; e < c1; e += kDT) out[e] = e == win ? 1.0f : 0.0f;
+        return;
+    }
+    const double inv_temp = 1.0 / static_cast<double>(T);
+    // 1. the scaled maximum (NaN ignored) and the non-finite flag of this chunk
+    double mx = -INFINITY;
+    unsigned int bad = 0u;
+    for (uint32_t e = c0 + tid; e < c1; e += kDT) {
+        const float x = dist_logit(a, rowp, e);
+        bad |= (x != x || x == INFINITY) ? 1u : 0u;
+        const double s = __dmul_rn(static_cast<double>(x), inv_temp);
+        mx = s > mx ? s : mx;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const double t = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+        mx = t > mx ? t : mx;
+        bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, o);
+    }
+    if (lane == 0) {
+        sh.redd[w] = mx;
+        sh.redu[w] = bad;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        double m = -INFINITY;
+        unsigned int bd = 0u;
+        for (int i = 0; i < kDW; ++i) {
+            m = sh.redd[i] > m ? sh.redd[i] : m;
+            bd |= sh.redu[i];
+        }
+        for (uint32_t q = 0; q < C; ++q) {
+            DistShared* d = cluster.map_shared_rank(&sh, q);
+            d->mx[crank] = m;
+            d->bad[crank] = bd;
+        }
+    }
+    cluster.sync();
+    double max_scaled = -INFINITY;
+    unsigned int any_bad = 0u;
+    for (uint32_t q = 0; q < C; ++q) {
+        max_scaled = sh.mx[q] > max_scaled ? sh.mx[q] : max_scaled;
+        any_bad |= sh.bad[q];
+    }
+    // every x * inv_temp - max is NaN when the row holds a NaN or +inf, or is all -inf: zeros
+    const bool zero = any_bad != 0u || max_scaled == -INFINITY;
+    // 2. the partial sums of exp(x * inv_temp - max)
+    double s = 0.0;
+    if (!zero) {
+        for (uint32_t e = c0 + tid; e < c1; e += kDT)
+            s += exp(__dsub_rn(__dmul_rn(static_cast<double>(dist_logit(a, rowp, e)), inv_temp), max_scaled));
+    }
+    s = warp_sum_f64(s);
+    if (lane == 0) sh.redd[w] = s;
+    __syncthreads();
+    if (tid == 0) {
+        double t = 0.0;
+        for (int i = 0; i < kDW; ++i) t += sh.redd[i];
+        for (uint32_t q = 0; q < C; ++q) cluster.map_shared_rank(&sh, q)->sm[crank] = t;
+    }
+    cluster.sync();
+    double sum = 0.0;
+    for (uint32_t q = 0; q < C; ++q) sum += sh.sm[q];
+    // 3. the probabilities
+    if (zero || !(sum > 0.0)) {
+        for (uint32_t e = c0 + tid; e < c1; e += kDT) out[e] = 0.0f;
+        return;
+    }
+    for (uint32_t e = c0 + tid; e < c1; e += kDT) {
+        const double ex = exp(__dsub_rn(__dmul_rn(static_cast<double>(dist_logit(a, rowp, e)), inv_temp), max_scaled));
+        out[e] = static_cast<float>(ex / sum);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_full_distribution(const DistArgs& a, const LaunchPlan& plan, cudaStream_t stream) {
+    static std::atomic<uint64_t> ready{0};  // cluster-size attribute set once per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(ready.load(std::memory_order_acquire) & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(dist_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+        ready.fetch_or(bit, std::memory_order_acq_rel);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_rows * plan.cluster);
+    cfg.blockDim = dim3(kDT);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = plan.cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, dist_kernel, a);
+}
+
+}  // namespace sixi_b200

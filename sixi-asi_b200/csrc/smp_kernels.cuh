@@ -117,6 +117,20 @@ struct MergeArgs {
     int32_t* out_status;
 };
 size_t shard_smem_bytes(uint32_t shard_vocab);
+
+// ---- full-vocabulary softmax rows (smp_dist.cu) -------------------------------------------------
+struct DistArgs {
+    const void* data;
+    uint64_t row_stride;  // elements
+    uint32_t dtype;
+    uint32_t vocab;
+    uint32_t n_rows;
+    uint32_t chunk;       // elements per CTA of a row's cluster
+    const float* temperatures;
+    float* out;
+    uint64_t out_stride;  // elements
+};
+cudaError_t launch_full_distribution(const DistArgs& a, const LaunchPlan& plan, cudaStream_t stream);
 cudaError_t launch_shard_candidates(const ShardArgs& a, cudaStream_t stream);
 cudaError_t launch_merge_shards(const MergeArgs& a, cudaStream_t stream);
 

@@ -84,6 +84,7 @@ SIGNATURES = {
     "sixi_smp_candidates": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _P, _U32, _P, _P, _P, _P, _P]),
     "sixi_smp_verify": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32, _P, _P, _P, _P, _P,
                                _U64, _P, _P, _P, _P, _P, _P, _P]),
+    "sixi_smp_full_distribution": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _U64, _P]),
     "sixi_smp_verify_static": (_I32, [_I32, _U32, ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32, _P, _P, _P,
                                       _P, _P, _U64, _P, _P, _P, _P, _P, _P, _P]),
     "sixi_smp_shard_candidates": (_I32, [_P, ctypes.POINTER(Rows), _U32, _U32, _U32, _P, _P, _P, _P, _U32,
@@ -258,6 +259,17 @@ class Sampler:
         _check("sixi_smp_verify", st)
         return dict(accepted=acc, tokens=toks, n_tokens=ntok, first_reject=frej, uniforms_used=used,
                     status=sts)
+
+    def full_distribution(self, logits, temperatures, stream=None):
+        """compute_full_distribution per row: fp32 probabilities [n_rows, vocab]."""
+        import torch
+
+        out = torch.empty((logits.shape[0], self.vocab), dtype=torch.float32, device=logits.device)
+        rows = self._rows(logits)
+        st = _lib().sixi_smp_full_distribution(self.h, ctypes.byref(rows), _ptr(temperatures), _ptr(out),
+                                            self.vocab, self._stream(stream))
+        _check("sixi_smp_full_distribution", st)
+        return out
 
     # -- vocab-sharded mode ----------------------------------------------------------------------
     def shard_candidates(self, shard_logits, vocab_offset: int, shard_vocab: int, params, top_n: int = 64,

@@ -249,3 +249,31 @@ def test_large_vocab_wide_clusters(port, vocab):
     torch.cuda.synchronize()
     for r in range(rows):
         assert int(g[r]) == port.greedy_argmax(d["logits"][r]), r
+
+
+@pytest.mark.parametrize("vocab", [7, 4097, 151_936])
+def test_full_distribution(port, vocab):
+    """sixi_smp_full_distribution against the restatement of compute_full_distribution."""
+    rng = np.random.default_rng(vocab + 5)
+    rows = 12
+    x = rng.normal(0, 3, size=(rows, vocab)).astype(np.float32)
+    temps = rng.choice(np.array([0.0, 0.25, 0.8, 1.0, 3.0], np.float32), size=rows)
+    if vocab > 10:
+        x[1, 5] = np.nan          # sampled row with a NaN: all zeros
+        temps[1] = 1.0
+        x[2, 0] = np.nan          # greedy row with a NaN at index 0: one-hot at 0
+        temps[2] = 0.0
+        x[3, rng.integers(0, vocab, size=4)] = -np.inf
+        temps[3] = 0.7
+        x[4, 9] = np.inf          # +inf: all zeros
+        temps[4] = 0.5
+    smp = sampler(vocab)
+    for dt in ("f32", "bf16"):
+        xin = x if dt == "f32" else W.f32_to_bf16_bits(x)
+        got = smp.full_distribution(dev(xin), torch.from_numpy(temps).to(DEV)).cpu().numpy()
+        for r in range(rows):
+            want = port.full_distribution(xin[r], float(temps[r]))
+            if temps[r] <= 0 or not np.any(want):
+                assert np.array_equal(got[r], want), (dt, r)
+            else:
+                np.testing.assert_allclose(got[r], want, rtol=1e-6, atol=1e-30, err_msg=f"{dt} row {r}")

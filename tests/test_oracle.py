@@ -150,3 +150,23 @@ def test_masked_tokens_never_sampled(port):
     tok, st = port.sample_batch(d["logits"], d["params"], d["masks"], d["hist"], d["hist_off"], u)
     allowed = W.unpack_mask(d["masks"], 3000)
     assert all(st == 0) and all(allowed[r, tok[r]] for r in range(6))
+
+
+def test_full_distribution_port_matches_reference(port, reference):
+    """compute_full_distribution: the restatement against the engine's own function, including
+    greedy one-hots, NaN / +inf rows (all zeros) and -inf entries."""
+    rng = np.random.default_rng(17)
+    for vocab in (1, 7, 1000, 40000):
+        for t in (0.0, 0.3, 1.0, 2.5):
+            for case in range(3):
+                x = rng.normal(0, 3, size=vocab).astype(np.float32)
+                if vocab > 10 and case == 1:
+                    x[rng.integers(0, vocab)] = np.nan
+                if vocab > 10 and case == 2:
+                    x[rng.integers(0, vocab, size=5)] = -np.inf
+                    x[0] = np.inf if t == 2.5 else x[0]
+                a = port.full_distribution(x, t)
+                b = reference.full_distribution(x, t)
+                assert np.array_equal(a, b), (vocab, t, case)
+    bits = W.f32_to_bf16_bits(rng.normal(0, 2, size=5000).astype(np.float32))
+    assert np.array_equal(port.full_distribution(bits, 0.7), reference.full_distribution(bits, 0.7))

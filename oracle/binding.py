@@ -37,6 +37,11 @@ _SIGS = {
     "orc_sample_batch": (_I32, [_P, _U32, _U32, _U64, _U64, _P, _P, _P, _P, _P, _U64, _P, _P, _I32]),
     "orc_verify": (_I32, [_P, _U32, _U64, _U64, _P, _P, _P, _U32, _U32, _P, _P, _P, _P, _P, _U64,
                           _P, _P, _P, _P, _P, _P, _I32]),
+    # JSON-object grammar automaton (sixi_json_oracle.c)
+    "orc_json_feed": (_I32, [_P, _P, _U64]),
+    "orc_json_fill_masks": (None, [_P, _P, _P, _U32, _I32, _P, _U32, _P, _U64, _I32]),
+    "orc_json_advance": (None, [_P, _P, _P, _U32, _I32, _P, _U32, _P, _U64, _P, _P]),
+    "orc_json_expand": (None, [_P, _P, _P, _U32, _I32, _P, _U32, _P, _U32, _P, _P]),
 }
 
 
@@ -130,6 +135,55 @@ class Oracle:
                             _p(out["accepted"]), _p(out["tokens"]), _p(out["n_tokens"]),
                             _p(out["first_reject"]), _p(out["uniforms_used"]), _p(out["status"]), n_threads)
         return out
+
+
+class JsonVocab:
+    """A vocabulary for the JSON-grammar oracle (token texts as CSR bytes)."""
+
+    def __init__(self, tokens: list[bytes], flags=None, eos_id: int = -1):
+        self.off = np.zeros(len(tokens) + 1, dtype=np.uint64)
+        self.off[1:] = np.cumsum([len(t) for t in tokens])
+        self.data = np.frombuffer(b"".join(tokens) or b"\0", dtype=np.uint8).copy()
+        self.flags = None if flags is None else np.ascontiguousarray(flags, dtype=np.uint8)
+        self.vocab = len(tokens)
+        self.eos = eos_id
+
+
+def json_feed(o: Oracle, state: np.ndarray, text: bytes) -> bool:
+    """Feeds bytes to a 32-byte state in place; False (state unchanged) when refused."""
+    buf = np.frombuffer(text or b"\0", dtype=np.uint8)
+    return bool(o.lib.orc_json_feed(state.ctypes.data, buf.ctypes.data, len(text)))
+
+
+def json_fill_masks(o: Oracle, v: JsonVocab, states: np.ndarray, n_threads: int = 0) -> np.ndarray:
+    states = np.ascontiguousarray(states, dtype=np.uint8).reshape(-1, 32)
+    w = (v.vocab + 31) // 32
+    out = np.zeros((states.shape[0], w), dtype=np.uint32)
+    o.lib.orc_json_fill_masks(v.data.ctypes.data, v.off.ctypes.data, _p(v.flags), v.vocab, v.eos,
+                              states.ctypes.data, states.shape[0], out.ctypes.data, w, n_threads)
+    return out
+
+
+def json_advance(o: Oracle, v: JsonVocab, states: np.ndarray, tokens: np.ndarray, n_tokens=None) -> np.ndarray:
+    """Advances uint8 [n, 32] states in place by tokens ([n] or [n, m] with n_tokens); statuses."""
+    tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+    n = states.shape[0]
+    stride = tokens.shape[1] if tokens.ndim == 2 else 1
+    nt = None if n_tokens is None else np.ascontiguousarray(n_tokens, dtype=np.int32)
+    st = np.zeros(n, dtype=np.int32)
+    o.lib.orc_json_advance(v.data.ctypes.data, v.off.ctypes.data, _p(v.flags), v.vocab, v.eos, states.ctypes.data,
+                           n, tokens.ctypes.data, stride, _p(nt), st.ctypes.data)
+    return st
+
+
+def json_expand(o: Oracle, v: JsonVocab, states: np.ndarray, drafts: np.ndarray, n_drafts=None) -> np.ndarray:
+    drafts = np.ascontiguousarray(drafts, dtype=np.int32)
+    s, k = drafts.shape
+    nd = None if n_drafts is None else np.ascontiguousarray(n_drafts, dtype=np.int32)
+    out = np.zeros((s * (k + 1), 32), dtype=np.uint8)
+    o.lib.orc_json_expand(v.data.ctypes.data, v.off.ctypes.data, _p(v.flags), v.vocab, v.eos, states.ctypes.data,
+                          s, drafts.ctypes.data, k, _p(nd), out.ctypes.data)
+    return out
 
 
 _cache: dict[str, Oracle] = {}

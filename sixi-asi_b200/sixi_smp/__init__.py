@@ -9,6 +9,7 @@ Entry points mirror the engine's sampler/verifier interface (include/sixi_smp.h)
   candidates       DeterministicSampler::compute_sampling_candidates  (:449-584)
   greedy_argmax    DeterministicSampler::sample_greedy_argmax  (:394-407)
   verify           SpeculativeDecoder::step verification       src/speculative/speculative.cpp:589-916
+and the device-side producer of JSON-object grammar masks (include/sixi_json.h, json_grammar.py).
 """
 
 from __future__ import annotations
@@ -91,6 +92,14 @@ SIGNATURES = {
                                          _P, _P, _P]),
     "sixi_smp_merge_shards": (_I32, [_P, _U32, _U32, _U32, _P, _P, _P, _P, _U64, _P, _P, _P]),
     "sixi_smp_philox_uniform": (ctypes.c_double, [_U64, _U64, _U32]),
+    # include/sixi_json.h: the device-side grammar-mask producer (sixi_smp.json_grammar)
+    "sixi_json_vocab_create": (_I32, [_I32, _P, _P, _U32, _P, _I32, ctypes.POINTER(_P)]),
+    "sixi_json_vocab_destroy": (None, [_P]),
+    "sixi_json_vocab_size": (_U32, [_P]),
+    "sixi_json_reset": (_I32, [_P, _P, _U32, _P]),
+    "sixi_json_fill_masks": (_I32, [_P, _P, _U32, _P, _U64, _P]),
+    "sixi_json_advance": (_I32, [_P, _P, _U32, _P, _U64, _P, _P, _P]),
+    "sixi_json_expand_drafts": (_I32, [_P, _P, _U32, _P, _U32, _P, _P, _P]),
 }
 
 

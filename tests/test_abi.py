@@ -1,5 +1,6 @@
 """CPU checks of the C-ABI boundary: the library loads without a GPU, exports every entry point that
-include/sixi_smp.h declares, and the Python records match the C struct layouts."""
+include/sixi_smp.h and include/sixi_json.h declare, and the Python records match the C struct
+layouts."""
 
 from __future__ import annotations
 
@@ -12,19 +13,22 @@ import pytest
 from conftest import REPO
 
 HEADER = REPO / "include" / "sixi_smp.h"
+HEADERS = sorted((REPO / "include").glob("*.h"))
 LIB = REPO / "sixi-asi_b200" / "lib" / "libsixi_smp.so"
 
 
 def declared_symbols() -> list[str]:
-    text = HEADER.read_text()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(sixi_smp_[a-z_]+)\s*\(", text)))
+    names = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b(sixi_(?:smp|json)_[a-z_]+)\s*\(", text))
+    return sorted(names)
 
 
 def test_library_exports_every_declared_symbol():
     assert LIB.exists(), "build the library first (python sixi-asi_b200/build_lib.py)"
     out = subprocess.run(["nm", "-D", "--defined-only", str(LIB)], capture_output=True, text=True, check=True).stdout
-    exported = set(re.findall(r"\bT (sixi_smp_\w+)", out))
+    exported = set(re.findall(r"\bT (sixi_(?:smp|json)_\w+)", out))
     missing = [s for s in declared_symbols() if s not in exported]
     assert not missing, missing
     # nothing else leaks from the library (kernels and helpers are hidden)

@@ -63,6 +63,8 @@ class Oracle:
         self.path = Path(path)
         self.lib = ctypes.CDLL(str(self.path))
         for name, (res, args) in _SIGS.items():
+            if name.startswith("orc_json_") and not hasattr(self.lib, name):
+                continue  # the grammar automaton exists only in the port (the engine's is binary-only)
             fn = getattr(self.lib, name)
             fn.restype = res
             fn.argtypes = args

@@ -230,7 +230,8 @@ def _graph_ms(step, steps: int, warmup: int, stream) -> float:
 
 def run_workload(args) -> int:
     """The other configurations of the path on one GPU (reported beside the config-2 line):
-    config1 single-row latency, config3 grammar-masked batch, config4 speculative verification."""
+    config1 single-row latency, config3 grammar-masked batch, config4 speculative verification,
+    grammar: the JSON-constrained step with device-produced masks."""
     import torch
 
     import sixi_smp as S
@@ -307,6 +308,78 @@ def run_workload(args) -> int:
         metric = "speculative verify stream-steps/s (config 4: S=32, k=8, V=151,936, bf16 target, fp32 q)"
         data = "synthetic; 2 rotating batches (491 MB > L2)"
         launches = 2 * args.steps  # row kernel + per-stream finalize
+    elif args.workload == "grammar":
+        from sixi_smp.json_grammar import JsonGrammar, Tokenizer, json_documents, json_vocab, prefix_states_tokens
+
+        toks, flags, eos = json_vocab(VOCAB, seed=5)
+        gram = JsonGrammar(0, toks, flags, eos)
+        tk = Tokenizer(toks, flags)
+        docs = json_documents(256, seed=21)
+        nst = 4
+        states = []
+        for i in range(nst):  # rows spread over the automaton's modes, as decoding visits them
+            pre, lens = prefix_states_tokens(docs, tk, ROWS, seed=100 + i)
+            st = gram.new_states(ROWS)
+            gram.advance(st, t(pre), t(lens))
+            states.append(st)
+        masks = torch.empty((ROWS, gram.mask_words), dtype=torch.int32, device=dev)
+
+        def mask_step(i):
+            gram.fill_masks(states[i % nst], out=masks, stream=torch.cuda.current_stream())
+
+        mask_ms = _graph_ms(mask_step, args.steps, args.warmup, stream)
+        # the whole constrained step: masks -> masked config-2 sampling -> automaton advance
+        base = W.config2(rows=ROWS, vocab=VOCAB, seed=3)
+        base["params"]["flags"] |= S.ROW_MASKED
+        rng = np.random.default_rng(34)
+        nbuf = NBUF
+        logits = [t(base["logits"])] + [t(W.config2_logits(rng, ROWS, VOCAB)) for _ in range(nbuf - 1)]
+        params, hist, hoff = t(base["params"]), t(base["hist"]), t(base["hist_off"])
+        u = [torch.rand(ROWS, dtype=torch.float64, device=dev) for _ in range(nbuf)]
+        smp = S.Sampler(0, 64, VOCAB)
+        tok = torch.empty(ROWS, dtype=torch.int32, device=dev)
+        sts = torch.empty(ROWS, dtype=torch.int32, device=dev)
+        gst = torch.empty(ROWS, dtype=torch.int32, device=dev)
+        live = gram.new_states(ROWS)
+
+        def step(i):
+            cs = torch.cuda.current_stream()
+            if i % 64 == 0:  # start over from mid-document states now and then
+                live.copy_(states[(i // 64) % nst])
+            gram.fill_masks(live, out=masks, stream=cs)
+            smp.sample(logits[i % nbuf], params, masks=masks, hist=hist, hist_off=hoff, uniforms=u[i % nbuf],
+                       out_tokens=tok, out_status=sts, stream=cs)
+            gram.advance(live, tok, out_status=gst, stream=cs)
+
+        ms = _graph_ms(step, args.steps, args.warmup, stream)
+        torch.cuda.synchronize()
+        assert int((sts != 0).sum()) == 0 and int((gst != 0).sum()) == 0, (sts.tolist(), gst.tolist())
+        vocab_bytes = 20 * VOCAB  # inline heads + meta words, L2-resident across rows and steps
+        nbytes = (ROWS * VOCAB * 4 + 4 * int(base["hist_off"][-1]) + 2 * masks.numel() * 4 + vocab_bytes)
+        unit, value = "rows/s", ROWS * args.steps / (ms / 1e3)
+        metric = ("JSON-constrained sampled rows/s at B=32, V=151,936 fp32: device grammar masks + masked "
+                  "sampling + automaton advance")
+        data = ("synthetic; 16 rotating logits batches (311 MB > L2); synthetic 151,936-token vocabulary "
+                "(L2-resident by design: read by every row of every step); states from prefixes of seeded "
+                "JSON documents")
+        launches = 3 * args.steps + args.steps // 64
+        extra = {"mask_rows_per_s": ROWS * args.steps / (mask_ms / 1e3), "mask_us_per_batch": 1e3 * mask_ms / args.steps}
+        if not args.no_cpu:
+            from oracle import binding as OB
+
+            o = OB.port()
+            ov = OB.JsonVocab(toks, flags, eos)
+            hs = states[0].cpu().numpy()
+            thr = os.cpu_count() or 1
+            t0 = time.perf_counter()
+            n = 0
+            while time.perf_counter() - t0 < min(args.cpu_budget, 10.0):
+                OB.json_fill_masks(o, ov, hs, n_threads=thr)
+                n += hs.shape[0]
+            el = time.perf_counter() - t0
+            extra["cpu_baseline"] = {"value": n / el, "unit": "mask rows/s", "cores": thr, "kind": "port",
+                                     "sample": f"{n} rows of JSON-grammar masks (oracle automaton, {thr} threads)"}
+        gram_obj = gram
     else:
         raise SystemExit(f"unknown workload {args.workload}")
     per_launch_s = ms / 1e3 / args.steps
@@ -320,6 +393,9 @@ def run_workload(args) -> int:
                      "traffic": None, "peak_source": peak_kind, "bytes_per_launch": int(nbytes)},
         "gpu_launches": launches,
     }
+    if args.workload == "grammar":
+        line.update(extra)
+        gram_obj.close()
     print(json.dumps(line), flush=True)
     smp.close()
     return 0
@@ -334,7 +410,7 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="config2", choices=["config2", "config1", "config3", "config4"],
+    ap.add_argument("--workload", default="config2", choices=["config2", "config1", "config3", "config4", "grammar"],
                     help="config2 is the headline line; the others are reported beside it (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

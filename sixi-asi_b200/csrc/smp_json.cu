@@ -6,8 +6,9 @@
 // device for every (row, token) pair:
 //   json_mask_kernel     one thread per token and row: the token's bytes are fed to a register
 //                        copy of the row's state; a warp's 32 verdicts are one mask word (ballot).
-//                        Tokens that are plain string content (precomputed per token) are decided
-//                        without a walk when the row is inside a string, the common case.
+//                        Tokens whose first byte the state refuses (a per-block table of the 256
+//                        byte values) and tokens that are plain string content (precomputed per
+//                        token) while the row is inside a string are decided without a walk.
 //   json_advance_kernel  one thread per row: applies the sampled (or committed) tokens.
 //   json_expand_kernel   one thread per stream: the per-draft states of a speculative step.
 // The vocabulary is uploaded once: the first 16 bytes of every token inline (one 16-byte load per
@@ -17,6 +18,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <initializer_list>
 #include <new>
 #include <vector>
 
@@ -24,12 +26,13 @@
 
 namespace {
 
-// token flags (bits 24..31 of the meta word; bits 0..23 hold the length)
-constexpr uint32_t kTokSpecial = 1u << 24;
-constexpr uint32_t kTokEos = 1u << 25;
-constexpr uint32_t kTokPlain = 1u << 26;  // clean string state -> same clean string state
-constexpr uint32_t kLenMask = (1u << 24) - 1u;
-constexpr uint32_t kMaxTokenBytes = kLenMask;
+// Meta of a token: x = length in bytes; y = flags (bits 0..7), first byte (bits 8..15), first
+// byte that is not JSON whitespace (bits 16..23), count of '{' and '[' bytes (bits 24..31, capped).
+constexpr uint32_t kTokSpecial = 1u << 0;
+constexpr uint32_t kTokEos = 1u << 1;
+constexpr uint32_t kTokPlain = 1u << 2;  // clean string state -> same clean string state
+constexpr uint32_t kTokAllWs = 1u << 3;  // only whitespace
+constexpr uint64_t kMaxTokenBytes = 0xFFFFFFFFull;
 
 constexpr uint32_t M_START = SIXI_JSON_START, M_OBJ_FIRST = SIXI_JSON_OBJ_FIRST, M_OBJ_KEY = SIXI_JSON_OBJ_KEY,
                    M_COLON = SIXI_JSON_COLON, M_VALUE = SIXI_JSON_VALUE, M_ARR_FIRST = SIXI_JSON_ARR_FIRST,
@@ -299,12 +302,43 @@ __host__ __device__ inline bool js_byte(JS& s, uint32_t c) {
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Contexts. A context fixes the mode, the part of the state that the mode reads (string kind and
+// open UTF-8 sequence, literal position, \u digits left) and the kind of the innermost open
+// container. At upload every (token, context) pair gets a verdict bit and a dependency bit; the
+// verdict holds for every state of that context unless the token closes the innermost container
+// and goes on (then the container below decides: dependency bit, the token is walked). A row's
+// context is found through a 64K-entry table indexed by ctx_key.
+constexpr uint32_t kMaxCtx = 96;
+constexpr uint32_t kCtxWords = kMaxCtx / 32;
+constexpr uint32_t kNoCtx = 0xFFu;
+constexpr uint32_t kCtxKeys = 1u << 16;
+constexpr uint32_t kCtxMaxDepth = 64;  // rows at least this deep are walked (push limit)
+constexpr uint32_t kCtxMaxOpens = SIXI_JSON_MAX_DEPTH - kCtxMaxDepth;  // tokens opening more: walked
+
+__host__ __device__ inline uint32_t ctx_key(uint32_t mode, uint32_t aux, uint32_t pos, uint32_t utf8,
+                                            uint32_t top) {
+    const bool str_like = mode == M_STR || mode == M_ESC || mode == M_HEX;
+    const uint32_t a = (str_like || mode == M_LIT) ? aux : 0u;
+    const uint32_t p = (mode == M_LIT || mode == M_HEX) ? pos : 0u;
+    const uint32_t u = mode == M_STR ? utf8 : 0u;
+    return (mode & 31u) | ((a & 3u) << 5) | ((p & 7u) << 7) | ((u & 31u) << 10) | ((top & 1u) << 15);
+}
+
+__host__ __device__ inline uint32_t ctx_key_of(const JS& s) {
+    return ctx_key(s.mode, s.aux, s.pos, s.utf8, s.depth > 0 ? js_top_is_obj(s) : 0u);
+}
+
 struct JVocab {
     const uint4* head;      // [V] first 16 bytes of each token (zero padded)
-    const uint32_t* meta;   // [V] length | flags
+    const uint2* meta;      // [V] length; flags and first bytes
     const uint8_t* bytes;   // all token bytes
     const uint64_t* off;    // [V] offset of each token in `bytes`
+    const uint8_t* ctx_table;  // [kCtxKeys] context index of a ctx_key, kNoCtx when none
+    const uint32_t* acc;    // [kCtxWords][V] verdict bits (bit c % 32 of word c / 32)
+    const uint32_t* dep;    // [kCtxWords][V] dependency bits
     uint32_t vocab;
+    int32_t eos;
 };
 
 __device__ __forceinline__ uint32_t head_byte(const uint4& h, uint32_t i) {
@@ -329,42 +363,123 @@ __device__ __forceinline__ bool js_token(JS& s, const JVocab& v, uint32_t id, ui
 
 // Applies token `id` to the state; false when it is not allowed there.
 __device__ __forceinline__ bool js_apply(JS& s, const JVocab& v, uint32_t id) {
-    const uint32_t meta = v.meta[id];
-    if (meta & kTokEos) return s.mode == M_DONE;
-    const uint32_t len = meta & kLenMask;
-    if ((meta & kTokSpecial) || len == 0u) return false;
-    if (s.mode == M_STR && s.utf8 == 0u && (meta & kTokPlain)) return true;
+    const uint2 meta = v.meta[id];
+    if (meta.y & kTokEos) return s.mode == M_DONE;
+    const uint32_t len = meta.x;
+    if ((meta.y & kTokSpecial) || len == 0u) return false;
+    if (s.mode == M_STR && s.utf8 == 0u && (meta.y & kTokPlain)) return true;
     JS t = s;
     if (!js_token(t, v, id, len, v.head[id])) return false;
     s = t;
     return true;
 }
 
-constexpr int kMaskThreads = 256;
-
-__global__ void __launch_bounds__(kMaskThreads) json_mask_kernel(const JVocab v, const sixi_json_state* states,
-                                                                  uint32_t* mask, uint64_t stride) {
-    const uint32_t row = blockIdx.y;
-    const uint32_t id = blockIdx.x * kMaskThreads + threadIdx.x;
-    const uint32_t words = (v.vocab + 31u) / 32u;
-    const sixi_json_state st = states[row];
-    bool ok = false;
-    if (id < v.vocab && st.failed == 0u) {
-        const uint32_t meta = v.meta[id];
-        const uint32_t len = meta & kLenMask;
-        if (meta & kTokEos) {
-            ok = st.mode == M_DONE;
-        } else if ((meta & kTokSpecial) || len == 0u) {
-            ok = false;
-        } else if (st.mode == M_STR && st.utf8 == 0u && (meta & kTokPlain)) {
-            ok = true;
-        } else if (st.mode != M_DONE) {
-            JS s = js_load(st);
-            ok = js_token(s, v, id, len, v.head[id]);
+// One thread per (token, context word): the verdict and dependency bits of 32 contexts.
+__global__ void json_ctx_kernel(const JVocab v, const sixi_json_state* reps, uint32_t n_ctx, uint32_t* acc,
+                                uint32_t* dep) {
+    const uint32_t id = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t cw = blockIdx.y;
+    if (id >= v.vocab) return;
+    const uint2 meta = v.meta[id];
+    const uint32_t len = meta.x;
+    uint32_t a = 0u, d = 0u;
+    if (!(meta.y & (kTokEos | kTokSpecial)) && len > 0u) {
+        const uint4 h = v.head[id];
+        const uint8_t* tail = v.bytes + v.off[id];
+        const bool many_opens = (meta.y >> 24) > kCtxMaxOpens;
+        for (uint32_t j = 0; j < 32u; ++j) {
+            const uint32_t c = cw * 32u + j;
+            if (c >= n_ctx) break;
+            JS s = js_load(reps[c]);
+            const uint32_t d0 = s.depth;
+            bool ok = true, dp = many_opens;
+            for (uint32_t i = 0; i < len && !dp; ++i) {
+                if (!js_byte(s, i < 16u ? head_byte(h, i) : tail[i])) {
+                    ok = false;
+                    break;
+                }
+                if (s.depth < d0 && i + 1u < len) dp = true;  // closed the innermost container, goes on
+            }
+            if (dp) {
+                d |= 1u << j;
+            } else if (ok) {
+                a |= 1u << j;
+            }
         }
     }
-    const uint32_t word = __ballot_sync(0xFFFFFFFFu, ok);
-    if ((threadIdx.x & 31u) == 0u && id / 32u < words) mask[static_cast<uint64_t>(row) * stride + id / 32u] = word;
+    acc[static_cast<uint64_t>(cw) * v.vocab + id] = a;
+    dep[static_cast<uint64_t>(cw) * v.vocab + id] = d;
+}
+
+constexpr int kMaskThreads = 256;
+constexpr int kMaskPerThread = 16;
+constexpr int kMaskPerBlock = kMaskThreads * kMaskPerThread;
+
+// Verdict of token `id` by walking it (rows without a context and dependent pairs). A token whose
+// first byte the state refuses (per-block table of the 256 byte values) is refused without a walk;
+// in modes where whitespace changes nothing the first byte that is not whitespace is screened.
+__device__ __noinline__ bool walk_verdict(const sixi_json_state& st, const JVocab& v, uint32_t id,
+                                          const uint32_t* first_ok) {
+    const uint2 meta = v.meta[id];
+    const uint32_t len = meta.x;
+    if ((meta.y & (kTokSpecial | kTokEos)) || len == 0u) return false;
+    if (st.mode == M_STR && st.utf8 == 0u && (meta.y & kTokPlain)) return true;
+    const bool ws_noop = st.mode <= M_AFTER;
+    if (ws_noop && (meta.y & kTokAllWs)) return true;
+    const uint32_t b = ws_noop ? (meta.y >> 16) & 0xFFu : (meta.y >> 8) & 0xFFu;
+    if (!((first_ok[b >> 5] >> (b & 31u)) & 1u)) return false;
+    JS s = js_load(st);
+    return js_token(s, v, id, len, v.head[id]);
+}
+
+// Block (x, row): tokens [x * 4096, x * 4096 + 4096) of one row, 16 per thread, one ballot per
+// 32 tokens. With a context the verdicts are bits of two coalesced words per token, all loaded
+// before the first is used; dependent pairs and rows without a context walk.
+__global__ void __launch_bounds__(kMaskThreads) json_mask_kernel(const JVocab v, const sixi_json_state* states,
+                                                                  uint32_t* mask, uint64_t stride) {
+    __shared__ uint32_t first_ok[8];
+    const uint32_t row = blockIdx.y;
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t words = (v.vocab + 31u) / 32u;
+    const uint32_t base = blockIdx.x * kMaskPerBlock + threadIdx.x;
+    const sixi_json_state st = states[row];
+    const bool live = st.failed == 0u && st.mode != M_DONE;
+    const JS s0 = js_load(st);
+    const uint32_t ctx = (live && st.depth < kCtxMaxDepth) ? v.ctx_table[ctx_key_of(s0)] : kNoCtx;
+    {
+        JS s = s0;
+        const bool okb = live && js_byte(s, threadIdx.x);
+        const uint32_t w = __ballot_sync(0xFFFFFFFFu, okb);
+        if (lane == 0u) first_ok[threadIdx.x >> 5] = w;
+    }
+    uint32_t a[kMaskPerThread], d[kMaskPerThread];
+    if (ctx != kNoCtx) {
+        const uint64_t cbase = static_cast<uint64_t>(ctx >> 5) * v.vocab;
+#pragma unroll
+        for (int q = 0; q < kMaskPerThread; ++q) {
+            const uint32_t id = base + q * kMaskThreads;
+            a[q] = id < v.vocab ? v.acc[cbase + id] : 0u;
+            d[q] = id < v.vocab ? v.dep[cbase + id] : 0u;
+        }
+    }
+    __syncthreads();
+    const uint32_t cbit = ctx & 31u;
+#pragma unroll
+    for (int q = 0; q < kMaskPerThread; ++q) {
+        const uint32_t id = base + q * kMaskThreads;
+        bool ok = false;
+        if (id < v.vocab && st.failed == 0u) {
+            if (st.mode == M_DONE) {
+                ok = static_cast<int32_t>(id) == v.eos;
+            } else if (ctx != kNoCtx) {
+                ok = (d[q] >> cbit) & 1u ? walk_verdict(st, v, id, first_ok) : ((a[q] >> cbit) & 1u) != 0u;
+            } else {
+                ok = walk_verdict(st, v, id, first_ok);
+            }
+        }
+        const uint32_t word = __ballot_sync(0xFFFFFFFFu, ok);
+        if (lane == 0u && id / 32u < words) mask[static_cast<uint64_t>(row) * stride + id / 32u] = word;
+    }
 }
 
 __global__ void json_advance_kernel(const JVocab v, sixi_json_state* states, uint32_t n_rows, const int32_t* tokens,
@@ -438,9 +553,13 @@ struct sixi_json_vocab {
     uint32_t vocab;
     int32_t eos_id;
     uint4* head;
-    uint32_t* meta;
+    uint2* meta;
     uint8_t* bytes;
     uint64_t* off;
+    uint8_t* ctx_table;
+    sixi_json_state* ctx_rep;
+    uint32_t* acc;
+    uint32_t* dep;
 };
 
 namespace {
@@ -464,7 +583,7 @@ int32_t status_of(cudaError_t e) {
 }
 
 JVocab view(const sixi_json_vocab* v) {
-    return JVocab{v->head, v->meta, v->bytes, v->off, v->vocab};
+    return JVocab{v->head, v->meta, v->bytes, v->off, v->ctx_table, v->acc, v->dep, v->vocab, v->eos_id};
 }
 
 void free_vocab(sixi_json_vocab* v) {
@@ -472,7 +591,49 @@ void free_vocab(sixi_json_vocab* v) {
     cudaFree(v->meta);
     cudaFree(v->bytes);
     cudaFree(v->off);
+    cudaFree(v->ctx_table);
+    cudaFree(v->ctx_rep);
+    cudaFree(v->acc);
+    cudaFree(v->dep);
     delete v;
+}
+
+// Every context with its representative state (innermost container at depth 2, or the start).
+void build_contexts(std::vector<sixi_json_state>& reps, std::vector<uint8_t>& table) {
+    table.assign(kCtxKeys, static_cast<uint8_t>(kNoCtx));
+    auto add = [&](uint32_t mode, uint32_t aux, uint32_t pos, uint32_t utf8, uint32_t top) {
+        sixi_json_state t;
+        std::memset(&t, 0, sizeof(t));
+        t.mode = static_cast<uint8_t>(mode);
+        t.aux = static_cast<uint8_t>(aux);
+        t.pos = static_cast<uint8_t>(pos);
+        t.utf8 = static_cast<uint8_t>(utf8);
+        if (mode != M_START) {
+            t.depth = 2;
+            t.stack[0] = 1u | (top << 1);
+        }
+        table[ctx_key(mode, aux, pos, utf8, mode == M_START ? 0u : top)] = static_cast<uint8_t>(reps.size());
+        reps.push_back(t);
+    };
+    add(M_START, 0, 0, 0, 0);
+    add(M_OBJ_FIRST, 0, 0, 0, 1);
+    add(M_OBJ_KEY, 0, 0, 0, 1);
+    add(M_COLON, 0, 0, 0, 1);
+    add(M_ARR_FIRST, 0, 0, 0, 0);
+    const uint32_t str_slots[3][2] = {{1, 1}, {0, 0}, {0, 1}};  // (aux, top): key, value in array/object
+    const uint32_t utf8_codes[8] = {0, 1, 2, 6, 10, 3, 15, 19};
+    for (const auto& sl : str_slots) {
+        for (uint32_t u : utf8_codes) add(M_STR, sl[0], 0, u, sl[1]);
+        add(M_ESC, sl[0], 0, 0, sl[1]);
+        for (uint32_t p = 1; p <= 4; ++p) add(M_HEX, sl[0], p, 0, sl[1]);
+    }
+    for (uint32_t top = 0; top < 2; ++top) {
+        add(M_VALUE, 0, 0, 0, top);
+        add(M_AFTER, 0, 0, 0, top);
+        for (uint32_t m : {M_NEG, M_ZERO, M_INT, M_DOT, M_FRAC, M_EXP, M_EXPS, M_EXPD}) add(m, 0, 0, 0, top);
+        for (uint32_t w = 0; w < 3; ++w)
+            for (uint32_t p = 1; p < lit_len(w); ++p) add(M_LIT, w, p, 0, top);
+    }
 }
 
 }  // namespace
@@ -488,7 +649,7 @@ int32_t sixi_json_vocab_create(int32_t device, const uint8_t* host_bytes, const 
     *out = nullptr;
     const uint64_t total = host_offsets[vocab];
     std::vector<uint4> head(vocab);
-    std::vector<uint32_t> meta(vocab);
+    std::vector<uint2> meta(vocab);
     for (uint32_t i = 0; i < vocab; ++i) {
         if (host_offsets[i + 1] < host_offsets[i] || host_offsets[i + 1] > total) return SIXI_INVALID_ARGUMENT;
         const uint64_t len = host_offsets[i + 1] - host_offsets[i];
@@ -497,11 +658,17 @@ int32_t sixi_json_vocab_create(int32_t device, const uint8_t* host_bytes, const 
         uint8_t h[16] = {};
         std::memcpy(h, p, len < 16 ? len : 16);
         std::memcpy(&head[i], h, 16);
-        uint32_t m = static_cast<uint32_t>(len);
-        if (host_flags && (host_flags[i] & SIXI_JSON_TOKEN_SPECIAL)) m |= kTokSpecial;
-        if (static_cast<int64_t>(i) == eos_id) m |= kTokEos;
-        if (len > 0 && !(m & (kTokSpecial | kTokEos)) && host_plain(p, len)) m |= kTokPlain;
-        meta[i] = m;
+        uint32_t f = 0u;
+        if (host_flags && (host_flags[i] & SIXI_JSON_TOKEN_SPECIAL)) f |= kTokSpecial;
+        if (static_cast<int64_t>(i) == eos_id) f |= kTokEos;
+        if (len > 0 && !(f & (kTokSpecial | kTokEos)) && host_plain(p, len)) f |= kTokPlain;
+        uint64_t nws = 0, opens = 0;
+        while (nws < len && is_ws(p[nws])) ++nws;
+        for (uint64_t k = 0; k < len; ++k) opens += (p[k] == 0x7Bu || p[k] == 0x5Bu) ? 1u : 0u;
+        if (len > 0 && nws == len) f |= kTokAllWs;
+        const uint32_t b0 = len > 0 ? p[0] : 0u, bn = nws < len ? p[nws] : 0u;
+        const uint32_t no = static_cast<uint32_t>(opens < 255 ? opens : 255);
+        meta[i] = make_uint2(static_cast<uint32_t>(len), f | (b0 << 8) | (bn << 16) | (no << 24));
     }
     DevGuard g(device);
     sixi_json_vocab* v = new (std::nothrow) sixi_json_vocab{};
@@ -510,13 +677,31 @@ int32_t sixi_json_vocab_create(int32_t device, const uint8_t* host_bytes, const 
     v->vocab = vocab;
     v->eos_id = eos_id;
     cudaError_t e = cudaMalloc(&v->head, sizeof(uint4) * vocab);
-    if (e == cudaSuccess) e = cudaMalloc(&v->meta, sizeof(uint32_t) * vocab);
+    if (e == cudaSuccess) e = cudaMalloc(&v->meta, sizeof(uint2) * vocab);
     if (e == cudaSuccess) e = cudaMalloc(&v->bytes, total > 0 ? total : 1);
     if (e == cudaSuccess) e = cudaMalloc(&v->off, sizeof(uint64_t) * vocab);
     if (e == cudaSuccess) e = cudaMemcpy(v->head, head.data(), sizeof(uint4) * vocab, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(v->meta, meta.data(), sizeof(uint32_t) * vocab, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(v->meta, meta.data(), sizeof(uint2) * vocab, cudaMemcpyHostToDevice);
     if (e == cudaSuccess && total > 0) e = cudaMemcpy(v->bytes, host_bytes, total, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(v->off, host_offsets, sizeof(uint64_t) * vocab, cudaMemcpyHostToDevice);
+    // per-(token, context) verdicts, computed on the device once
+    std::vector<sixi_json_state> reps;
+    std::vector<uint8_t> table;
+    build_contexts(reps, table);
+    if (reps.size() > kMaxCtx) e = cudaErrorInvalidValue;
+    if (e == cudaSuccess) e = cudaMalloc(&v->ctx_table, kCtxKeys);
+    if (e == cudaSuccess) e = cudaMalloc(&v->ctx_rep, sizeof(sixi_json_state) * reps.size());
+    if (e == cudaSuccess) e = cudaMalloc(&v->acc, sizeof(uint32_t) * kCtxWords * vocab);
+    if (e == cudaSuccess) e = cudaMalloc(&v->dep, sizeof(uint32_t) * kCtxWords * vocab);
+    if (e == cudaSuccess) e = cudaMemcpy(v->ctx_table, table.data(), kCtxKeys, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(v->ctx_rep, reps.data(), sizeof(sixi_json_state) * reps.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        const dim3 grid((vocab + 255u) / 256u, kCtxWords);
+        json_ctx_kernel<<<grid, 256>>>(view(v), v->ctx_rep, static_cast<uint32_t>(reps.size()), v->acc, v->dep);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    }
     if (e != cudaSuccess) {
         free_vocab(v);
         return status_of(e);
@@ -547,7 +732,7 @@ int32_t sixi_json_fill_masks(const sixi_json_vocab* v, const sixi_json_state* st
         return SIXI_INVALID_ARGUMENT;
     if (n_rows == 0) return SIXI_OK;
     DevGuard g(v->device);
-    const dim3 grid((v->vocab + kMaskThreads - 1) / kMaskThreads, n_rows);
+    const dim3 grid((v->vocab + kMaskPerBlock - 1) / kMaskPerBlock, n_rows);
     json_mask_kernel<<<grid, kMaskThreads, 0, static_cast<cudaStream_t>(stream)>>>(view(v), states, mask_words,
                                                                                    mask_stride);
     return status_of(cudaGetLastError());

@@ -156,25 +156,38 @@ def json_vocab(vocab: int = 151_936, seed: int = 5) -> tuple[list[bytes], np.nda
     for n in (16, 20, 24, 32):
         add(b" " * n)  # long whitespace runs
     letters = np.frombuffer(b"abcdefghijklmnopqrstuvwxyz", dtype=np.uint8)
+    punct = [b"()", b"();", b"->", b"==", b"!=", b"/*", b"*/", b"//", b"::", b"=>", b"...", b"--", b"**", b"<=", b">=",
+             b"();\n", b"){", b"});", b"':", b"',", b"('", b"')", b"=\"", b"\">", b"</", b"/>", b"#", b"@", b"$", b"%"]
+    # form probabilities of a byte-level BPE vocabulary: words with and without a leading space
+    # dominate, then capitalised words, CJK and accented pieces (some split mid-character),
+    # code punctuation, and a few percent of pieces that carry a double quote
+    forms = np.array([0.30, 0.38, 0.07, 0.07, 0.10, 0.01, 0.02, 0.03, 0.02])
     while len(toks) < vocab - 3:
         ln = int(rng.choice([2, 3, 4, 5, 6, 7, 8, 9, 10, 12, 14, 18, 24], p=[.06, .12, .16, .16, .14, .11, .08,
                                                                              .06, .04, .03, .02, .015, .005]))
         w = bytes(letters[rng.integers(0, 26, size=ln)])
-        form = rng.integers(0, 10)
-        if form == 0:
-            w = w.capitalize()
-        elif form == 1:
+        form = int(rng.choice(len(forms), p=forms / forms.sum()))
+        if form == 1:
             w = b" " + w
         elif form == 2:
-            w = b'"' + w
+            w = w.capitalize()
         elif form == 3:
-            w = w + b'"'
-        elif form == 4:
-            w = b'"' + w + b'":'
-        elif form == 5:
-            w = b' "' + w + b'": "'
-        elif form == 6:
             w = b" " + w.capitalize()
+        elif form in (4, 5):
+            cps = rng.integers(0x4E00, 0xA000, size=int(rng.integers(1, 3))) if rng.random() < 0.7 else \
+                rng.integers(0xC0, 0x250, size=int(rng.integers(1, 4)))
+            w = "".join(chr(int(c)) for c in cps).encode()
+            if form == 5:  # a piece split inside a UTF-8 sequence
+                cut = int(rng.integers(1, len(w)))
+                w = w[:cut] if rng.random() < 0.5 else w[cut:]
+            elif rng.random() < 0.3:
+                w = b" " + w
+        elif form == 6:
+            w = punct[int(rng.integers(0, len(punct)))] + (w[:2] if rng.random() < 0.5 else b"")
+        elif form == 7:
+            w = [b'"' + w, w + b'"', b'"' + w + b'":', b' "' + w + b'": "', b' "' + w, w + b'",'][int(rng.integers(0, 6))]
+        elif form == 8:
+            w = str(int(rng.integers(0, 10 ** int(rng.integers(1, 6))))).encode()
         add(w)
     specials = [b"<|im_start|>", b"<|im_end|>", b"<|endoftext|>"]
     flags = np.zeros(len(toks) + len(specials), dtype=np.uint8)

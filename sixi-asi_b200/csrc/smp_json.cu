@@ -4,11 +4,12 @@
 // text a prefix of one JSON object (docs/API.md:45-76 in the engine); its automaton is binary-only.
 // This is a byte-level pushdown automaton for RFC 8259 JSON with a top-level object, run on the
 // device for every (row, token) pair:
-//   json_mask_kernel     one thread per token and row: the token's bytes are fed to a register
-//                        copy of the row's state; a warp's 32 verdicts are one mask word (ballot).
-//                        Tokens whose first byte the state refuses (a per-block table of the 256
-//                        byte values) and tokens that are plain string content (precomputed per
-//                        token) while the row is inside a string are decided without a walk.
+//   json_ctx_kernel      at upload, one thread per token and 32 contexts: the token's verdict in
+//                        each context (a class of states, see "Contexts"), giving one mask row per
+//                        context and a short list of tokens whose verdict the context leaves open.
+//   json_mask_kernel     per row: a copy of its context's mask row, then the open tokens walked
+//                        through a register copy of the row's state (rows without a context walk
+//                        every token); blocks stage their words in shared memory.
 //   json_advance_kernel  one thread per row: applies the sampled (or committed) tokens.
 //   json_expand_kernel   one thread per stream: the per-draft states of a speculative step.
 // The vocabulary is uploaded once: the first 16 bytes of every token inline (one 16-byte load per
@@ -335,9 +336,11 @@ struct JVocab {
     const uint8_t* bytes;   // all token bytes
     const uint64_t* off;    // [V] offset of each token in `bytes`
     const uint8_t* ctx_table;  // [kCtxKeys] context index of a ctx_key, kNoCtx when none
-    const uint32_t* acc;    // [kCtxWords][V] verdict bits (bit c % 32 of word c / 32)
-    const uint32_t* dep;    // [kCtxWords][V] dependency bits
+    const uint32_t* ctx_mask;  // [n_ctx][wpad] allowed-token bits of each context (dependent pairs 0)
+    const uint32_t* dep_off;   // [n_ctx + 1] each context's dependent tokens in dep_ids
+    const int32_t* dep_ids;    // ascending ids per context
     uint32_t vocab;
+    uint32_t wpad;             // mask words per context row (ceil(V / 32) rounded up to 4)
     int32_t eos;
 };
 
@@ -412,8 +415,8 @@ __global__ void json_ctx_kernel(const JVocab v, const sixi_json_state* reps, uin
 }
 
 constexpr int kMaskThreads = 256;
-constexpr int kMaskPerThread = 16;
-constexpr int kMaskPerBlock = kMaskThreads * kMaskPerThread;
+constexpr uint32_t kMaskSplit = 4;  // blocks per row
+constexpr uint32_t kMaskMaxWords = 2048;  // words per block (shared memory)
 
 // Verdict of token `id` by walking it (rows without a context and dependent pairs). A token whose
 // first byte the state refuses (per-block table of the 256 byte values) is refused without a walk;
@@ -432,16 +435,21 @@ __device__ __noinline__ bool walk_verdict(const sixi_json_state& st, const JVoca
     return js_token(s, v, id, len, v.head[id]);
 }
 
-// Block (x, row): tokens [x * 4096, x * 4096 + 4096) of one row, 16 per thread, one ballot per
-// 32 tokens. With a context the verdicts are bits of two coalesced words per token, all loaded
-// before the first is used; dependent pairs and rows without a context walk.
+// Block (x, row) builds mask words [w0, w1) of one row in shared memory. With a context: a copy of
+// the context's mask row, then the context's dependent tokens in range are walked and or-ed in.
+// Without one (rows 64 or more containers deep): every token in range is walked. Done rows allow
+// only end-of-sequence; failed rows nothing.
 __global__ void __launch_bounds__(kMaskThreads) json_mask_kernel(const JVocab v, const sixi_json_state* states,
-                                                                  uint32_t* mask, uint64_t stride) {
+                                                                  uint32_t* mask, uint64_t stride,
+                                                                  uint32_t words_per_block) {
     __shared__ uint32_t first_ok[8];
+    __shared__ __align__(16) uint32_t sw[kMaskMaxWords];
     const uint32_t row = blockIdx.y;
     const uint32_t lane = threadIdx.x & 31u;
     const uint32_t words = (v.vocab + 31u) / 32u;
-    const uint32_t base = blockIdx.x * kMaskPerBlock + threadIdx.x;
+    const uint32_t w0 = blockIdx.x * words_per_block;
+    const uint32_t w1 = w0 + words_per_block < words ? w0 + words_per_block : words;
+    if (w0 >= w1) return;
     const sixi_json_state st = states[row];
     const bool live = st.failed == 0u && st.mode != M_DONE;
     const JS s0 = js_load(st);
@@ -452,34 +460,35 @@ __global__ void __launch_bounds__(kMaskThreads) json_mask_kernel(const JVocab v,
         const uint32_t w = __ballot_sync(0xFFFFFFFFu, okb);
         if (lane == 0u) first_ok[threadIdx.x >> 5] = w;
     }
-    uint32_t a[kMaskPerThread], d[kMaskPerThread];
+    const uint32_t n = w1 - w0;
     if (ctx != kNoCtx) {
-        const uint64_t cbase = static_cast<uint64_t>(ctx >> 5) * v.vocab;
-#pragma unroll
-        for (int q = 0; q < kMaskPerThread; ++q) {
-            const uint32_t id = base + q * kMaskThreads;
-            a[q] = id < v.vocab ? v.acc[cbase + id] : 0u;
-            d[q] = id < v.vocab ? v.dep[cbase + id] : 0u;
-        }
+        // w0 and wpad are multiples of 4: 16-byte copies
+        const uint4* src = reinterpret_cast<const uint4*>(v.ctx_mask + static_cast<uint64_t>(ctx) * v.wpad + w0);
+        for (uint32_t i = threadIdx.x; i < (n + 3u) / 4u; i += kMaskThreads) reinterpret_cast<uint4*>(sw)[i] = src[i];
+    } else {
+        for (uint32_t i = threadIdx.x; i < n; i += kMaskThreads) sw[i] = 0u;
     }
     __syncthreads();
-    const uint32_t cbit = ctx & 31u;
-#pragma unroll
-    for (int q = 0; q < kMaskPerThread; ++q) {
-        const uint32_t id = base + q * kMaskThreads;
-        bool ok = false;
-        if (id < v.vocab && st.failed == 0u) {
-            if (st.mode == M_DONE) {
-                ok = static_cast<int32_t>(id) == v.eos;
-            } else if (ctx != kNoCtx) {
-                ok = (d[q] >> cbit) & 1u ? walk_verdict(st, v, id, first_ok) : ((a[q] >> cbit) & 1u) != 0u;
-            } else {
-                ok = walk_verdict(st, v, id, first_ok);
-            }
+    if (ctx != kNoCtx) {
+        const uint32_t d0 = v.dep_off[ctx], d1 = v.dep_off[ctx + 1];
+        for (uint32_t k = d0 + threadIdx.x; k < d1; k += kMaskThreads) {
+            const uint32_t id = static_cast<uint32_t>(v.dep_ids[k]);
+            if (id / 32u < w0 || id / 32u >= w1) continue;
+            if (walk_verdict(st, v, id, first_ok)) atomicOr(&sw[id / 32u - w0], 1u << (id & 31u));
         }
-        const uint32_t word = __ballot_sync(0xFFFFFFFFu, ok);
-        if (lane == 0u && id / 32u < words) mask[static_cast<uint64_t>(row) * stride + id / 32u] = word;
+    } else if (live) {
+        for (uint32_t id = w0 * 32u + threadIdx.x; id < w1 * 32u && id < v.vocab; id += kMaskThreads) {
+            const bool ok = walk_verdict(st, v, id, first_ok);
+            const uint32_t word = __ballot_sync(__activemask(), ok);
+            if (lane == 0u) sw[id / 32u - w0] = word;
+        }
+    } else if (st.failed == 0u && v.eos >= 0 && static_cast<uint32_t>(v.eos) / 32u >= w0 &&
+               static_cast<uint32_t>(v.eos) / 32u < w1 && threadIdx.x == 0) {
+        sw[static_cast<uint32_t>(v.eos) / 32u - w0] = 1u << (v.eos & 31);  // complete: end-of-sequence only
     }
+    __syncthreads();
+    uint32_t* dst = mask + static_cast<uint64_t>(row) * stride + w0;
+    for (uint32_t i = threadIdx.x; i < n; i += kMaskThreads) dst[i] = sw[i];
 }
 
 __global__ void json_advance_kernel(const JVocab v, sixi_json_state* states, uint32_t n_rows, const int32_t* tokens,
@@ -558,8 +567,10 @@ struct sixi_json_vocab {
     uint64_t* off;
     uint8_t* ctx_table;
     sixi_json_state* ctx_rep;
-    uint32_t* acc;
-    uint32_t* dep;
+    uint32_t* ctx_mask;
+    uint32_t* dep_off;
+    int32_t* dep_ids;
+    uint32_t wpad;
 };
 
 namespace {
@@ -583,7 +594,8 @@ int32_t status_of(cudaError_t e) {
 }
 
 JVocab view(const sixi_json_vocab* v) {
-    return JVocab{v->head, v->meta, v->bytes, v->off, v->ctx_table, v->acc, v->dep, v->vocab, v->eos_id};
+    return JVocab{v->head, v->meta, v->bytes, v->off, v->ctx_table, v->ctx_mask, v->dep_off, v->dep_ids,
+                  v->vocab, v->wpad, v->eos_id};
 }
 
 void free_vocab(sixi_json_vocab* v) {
@@ -593,8 +605,9 @@ void free_vocab(sixi_json_vocab* v) {
     cudaFree(v->off);
     cudaFree(v->ctx_table);
     cudaFree(v->ctx_rep);
-    cudaFree(v->acc);
-    cudaFree(v->dep);
+    cudaFree(v->ctx_mask);
+    cudaFree(v->dep_off);
+    cudaFree(v->dep_ids);
     delete v;
 }
 
@@ -691,16 +704,59 @@ int32_t sixi_json_vocab_create(int32_t device, const uint8_t* host_bytes, const 
     if (reps.size() > kMaxCtx) e = cudaErrorInvalidValue;
     if (e == cudaSuccess) e = cudaMalloc(&v->ctx_table, kCtxKeys);
     if (e == cudaSuccess) e = cudaMalloc(&v->ctx_rep, sizeof(sixi_json_state) * reps.size());
-    if (e == cudaSuccess) e = cudaMalloc(&v->acc, sizeof(uint32_t) * kCtxWords * vocab);
-    if (e == cudaSuccess) e = cudaMalloc(&v->dep, sizeof(uint32_t) * kCtxWords * vocab);
+    uint32_t* d_acc = nullptr;
+    uint32_t* d_dep = nullptr;
+    if (e == cudaSuccess) e = cudaMalloc(&d_acc, sizeof(uint32_t) * kCtxWords * vocab);
+    if (e == cudaSuccess) e = cudaMalloc(&d_dep, sizeof(uint32_t) * kCtxWords * vocab);
     if (e == cudaSuccess) e = cudaMemcpy(v->ctx_table, table.data(), kCtxKeys, cudaMemcpyHostToDevice);
     if (e == cudaSuccess)
         e = cudaMemcpy(v->ctx_rep, reps.data(), sizeof(sixi_json_state) * reps.size(), cudaMemcpyHostToDevice);
+    const uint32_t n_ctx = static_cast<uint32_t>(reps.size());
     if (e == cudaSuccess) {
         const dim3 grid((vocab + 255u) / 256u, kCtxWords);
-        json_ctx_kernel<<<grid, 256>>>(view(v), v->ctx_rep, static_cast<uint32_t>(reps.size()), v->acc, v->dep);
+        JVocab jv = view(v);
+        json_ctx_kernel<<<grid, 256>>>(jv, v->ctx_rep, n_ctx, d_acc, d_dep);
         e = cudaGetLastError();
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    }
+    // per context: the mask row of its verdicts and the ascending list of its dependent tokens
+    std::vector<uint32_t> acc, dep;
+    if (e == cudaSuccess) {
+        acc.resize(static_cast<size_t>(kCtxWords) * vocab);
+        dep.resize(static_cast<size_t>(kCtxWords) * vocab);
+        e = cudaMemcpy(acc.data(), d_acc, sizeof(uint32_t) * acc.size(), cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = cudaMemcpy(dep.data(), d_dep, sizeof(uint32_t) * dep.size(), cudaMemcpyDeviceToHost);
+    }
+    cudaFree(d_acc);
+    cudaFree(d_dep);
+    v->wpad = ((vocab + 31u) / 32u + 3u) / 4u * 4u;
+    if (e == cudaSuccess) {
+        std::vector<uint32_t> cmask(static_cast<size_t>(n_ctx) * v->wpad, 0u);
+        std::vector<uint32_t> doff(n_ctx + 1, 0u);
+        std::vector<int32_t> dids;
+        for (uint32_t c = 0; c < n_ctx; ++c) {
+            const uint32_t* a = acc.data() + static_cast<size_t>(c / 32u) * vocab;
+            const uint32_t* d = dep.data() + static_cast<size_t>(c / 32u) * vocab;
+            uint32_t* m = cmask.data() + static_cast<size_t>(c) * v->wpad;
+            for (uint32_t i = 0; i < vocab; ++i) {
+                if ((d[i] >> (c & 31u)) & 1u) {
+                    dids.push_back(static_cast<int32_t>(i));
+                } else if ((a[i] >> (c & 31u)) & 1u) {
+                    m[i / 32u] |= 1u << (i & 31u);
+                }
+            }
+            doff[c + 1] = static_cast<uint32_t>(dids.size());
+        }
+        if (dids.empty()) dids.push_back(0);
+        e = cudaMalloc(&v->ctx_mask, sizeof(uint32_t) * cmask.size());
+        if (e == cudaSuccess) e = cudaMalloc(&v->dep_off, sizeof(uint32_t) * doff.size());
+        if (e == cudaSuccess) e = cudaMalloc(&v->dep_ids, sizeof(int32_t) * dids.size());
+        if (e == cudaSuccess)
+            e = cudaMemcpy(v->ctx_mask, cmask.data(), sizeof(uint32_t) * cmask.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(v->dep_off, doff.data(), sizeof(uint32_t) * doff.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(v->dep_ids, dids.data(), sizeof(int32_t) * dids.size(), cudaMemcpyHostToDevice);
     }
     if (e != cudaSuccess) {
         free_vocab(v);
@@ -732,9 +788,14 @@ int32_t sixi_json_fill_masks(const sixi_json_vocab* v, const sixi_json_state* st
         return SIXI_INVALID_ARGUMENT;
     if (n_rows == 0) return SIXI_OK;
     DevGuard g(v->device);
-    const dim3 grid((v->vocab + kMaskPerBlock - 1) / kMaskPerBlock, n_rows);
+    // words per block: a multiple of 4 (16-byte copies), at most kMaskMaxWords
+    const uint32_t words = (v->vocab + 31u) / 32u;
+    uint32_t split = kMaskSplit;
+    while ((words + split - 1) / split > kMaskMaxWords - 3u) ++split;
+    const uint32_t wpb = ((words + split - 1) / split + 3u) / 4u * 4u;
+    const dim3 grid((words + wpb - 1) / wpb, n_rows);
     json_mask_kernel<<<grid, kMaskThreads, 0, static_cast<cudaStream_t>(stream)>>>(view(v), states, mask_words,
-                                                                                   mask_stride);
+                                                                                   mask_stride, wpb);
     return status_of(cudaGetLastError());
 }
 

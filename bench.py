@@ -123,12 +123,12 @@ def algorithmic_bytes(base: dict) -> int:
     return ROWS * VOCAB * 4 + 4 * int(base["hist_off"][-1])
 
 
-def profiled_traffic() -> int | None:
-    """DRAM bytes (read + write) per row_kernel launch of this workload from the committed ncu
-    summary (profiles/row_kernel_sample_config2.md), or None when it is absent."""
+def profiled_traffic(name: str = "row_kernel_sample_config2.md") -> int | None:
+    """DRAM bytes (read + write) per row_kernel launch of a workload from its committed ncu summary
+    (profiles/<name>), or None when it is absent."""
     import re
 
-    p = REPO / "profiles" / "row_kernel_sample_config2.md"
+    p = REPO / "profiles" / name
     try:
         m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", p.read_text())
     except OSError:
@@ -302,7 +302,11 @@ def run_workload(args) -> int:
                        hist_off=hoff, uniforms=u[i % nbuf], stream=torch.cuda.current_stream())
 
         ms = _graph_ms(step, args.steps, args.warmup, stream)
-        nbytes = (streams * (k + 1) * VOCAB * 2 + streams * k * VOCAB * 4 + masks.numel() * 4 + streams * k * 4 +
+        # bytes the verifier must read: the target rows, q at each drafted id (the accept test), the
+        # masks, drafts and histories. q is read further only where a draft is rejected (the
+        # residual: at the kept candidates, or over the row on the top_k = 0 path), which this
+        # count leaves out; the ncu capture (profiles/verify_config4_traffic.md) has the total.
+        nbytes = (streams * (k + 1) * VOCAB * 2 + streams * k * 4 + masks.numel() * 4 + streams * k * 4 +
                   4 * int(ds[0]["hist_off"][-1]))
         unit, value = "stream-steps/s", streams * args.steps / (ms / 1e3)
         metric = "speculative verify stream-steps/s (config 4: S=32, k=8, V=151,936, bf16 target, fp32 q)"
@@ -390,7 +394,8 @@ def run_workload(args) -> int:
         "dtype": "f32" if args.workload != "config4" else "bf16", "data": data,
         "config": {"workload": args.workload},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "peak_source": peak_kind, "bytes_per_launch": int(nbytes)},
+                     "traffic": profiled_traffic("verify_config4_traffic.md") if args.workload == "config4" else None,
+                     "peak_source": peak_kind, "bytes_per_launch": int(nbytes)},
         "gpu_launches": launches,
     }
     if args.workload == "grammar":

@@ -16,7 +16,7 @@
 #include <stdint.h>
 #include <string.h>
 
-#include "../include/sixi_json.h"
+#include "sixi_json_oracle.h"
 
 typedef struct {
     int mode, aux, pos, rem, rng, depth;

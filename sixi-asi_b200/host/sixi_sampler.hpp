@@ -28,6 +28,7 @@
 #include <utility>
 #include <vector>
 
+#include "../../include/sixi_json.h"
 #include "../../include/sixi_smp.h"
 
 namespace sixi_b200 {
@@ -460,6 +461,68 @@ private:
     cudaStream_t stream_ = nullptr;
     detail::DeviceBuffer d_logits_, d_params_, d_mask_, d_hist_, d_hoff_, d_u_, d_out_, d_cand_, d_q_, d_drafts_,
         d_vout_;
+};
+
+// Device-side grammar masks for `response_format: {"type": "json_object"}` answers
+// (include/sixi_json.h): one uploaded vocabulary, automaton states in caller-owned device memory,
+// asynchronous calls on the caller's stream. Together with DeviceSampler::sample_rows (masked
+// rows) a constrained step never leaves the device.
+class JsonMaskProducer {
+public:
+    // `texts[i]` is token i's text (the tokenizer's bytes), `special[i]` marks control tokens
+    // (may be empty), `eos_id` the end-of-sequence token (or -1).
+    static Result<std::unique_ptr<JsonMaskProducer>> create(int device, const std::vector<std::string>& texts,
+                                                            const std::vector<uint8_t>& special, int32_t eos_id) {
+        std::vector<uint64_t> off(texts.size() + 1, 0);
+        for (size_t i = 0; i < texts.size(); ++i) off[i + 1] = off[i] + texts[i].size();
+        std::string bytes;
+        bytes.reserve(off.back());
+        for (const auto& t : texts) bytes += t;
+        std::vector<uint8_t> flags(texts.size(), 0);
+        for (size_t i = 0; i < special.size() && i < flags.size(); ++i)
+            flags[i] = special[i] ? static_cast<uint8_t>(SIXI_JSON_TOKEN_SPECIAL) : 0u;
+        sixi_json_vocab* v = nullptr;
+        const int32_t st = sixi_json_vocab_create(device, reinterpret_cast<const uint8_t*>(bytes.data()), off.data(),
+                                                  static_cast<uint32_t>(texts.size()), flags.data(), eos_id, &v);
+        if (st != SIXI_OK)
+            return Result<std::unique_ptr<JsonMaskProducer>>(detail::status_of(st, "sixi_json_vocab_create"));
+        return Result<std::unique_ptr<JsonMaskProducer>>(std::unique_ptr<JsonMaskProducer>(new JsonMaskProducer(v)));
+    }
+    ~JsonMaskProducer() { sixi_json_vocab_destroy(v_); }
+    JsonMaskProducer(const JsonMaskProducer&) = delete;
+    JsonMaskProducer& operator=(const JsonMaskProducer&) = delete;
+
+    uint32_t vocab() const noexcept { return sixi_json_vocab_size(v_); }
+    uint32_t mask_words() const noexcept { return (vocab() + 31u) / 32u; }
+
+    Status reset(sixi_json_state* states, uint32_t n, cudaStream_t stream) const {
+        return detail::status_of(sixi_json_reset(v_, states, n, stream), "sixi_json_reset");
+    }
+    Status fill_masks(const sixi_json_state* states, uint32_t n, uint32_t* masks, cudaStream_t stream) const {
+        return detail::status_of(sixi_json_fill_masks(v_, states, n, masks, mask_words(), stream),
+                                 "sixi_json_fill_masks");
+    }
+    Status advance(sixi_json_state* states, uint32_t n, const int32_t* tokens, int32_t* status,
+                   cudaStream_t stream) const {
+        return detail::status_of(sixi_json_advance(v_, states, n, tokens, 1, nullptr, status, stream),
+                                 "sixi_json_advance");
+    }
+    // committed tokens of a speculative step: tokens[r * stride + j], j < counts[r]
+    Status advance_many(sixi_json_state* states, uint32_t n, const int32_t* tokens, uint64_t stride,
+                        const int32_t* counts, int32_t* status, cudaStream_t stream) const {
+        return detail::status_of(sixi_json_advance(v_, states, n, tokens, stride, counts, status, stream),
+                                 "sixi_json_advance");
+    }
+    Status expand_drafts(const sixi_json_state* states, uint32_t n_streams, const int32_t* drafts, uint32_t k,
+                         const int32_t* n_drafts, sixi_json_state* out_states, cudaStream_t stream) const {
+        return detail::status_of(
+            sixi_json_expand_drafts(v_, states, n_streams, drafts, k, n_drafts, out_states, stream),
+            "sixi_json_expand_drafts");
+    }
+
+private:
+    explicit JsonMaskProducer(sixi_json_vocab* v) : v_(v) {}
+    sixi_json_vocab* v_ = nullptr;
 };
 
 }  // namespace sixi_b200

@@ -12,6 +12,9 @@
 //                           and the RNG advanced by exactly the uniforms used
 //   verify_forced_rejection greedy rejection positions (tests/test_determinism_and_speculative.cpp
 //                           forced-rejection checks)
+//   json_constrained        JsonMaskProducer + masked sample_rows: a greedy constrained decode
+//                           writes the intended JSON object although a disallowed token scores
+//                           higher, and every mask equals the CPU automaton's (sixi_json_oracle.h)
 // Exit status 0 when every check passes. Needs a CUDA device.
 #include <algorithm>
 #include <cmath>
@@ -21,6 +24,7 @@
 #include <string>
 #include <vector>
 
+#include "../../oracle/sixi_json_oracle.h"
 #include "../../oracle/sixi_oracle.h"
 #include "sixi_sampler.hpp"
 
@@ -329,6 +333,103 @@ bool verify_forced_rejection() {
     return true;
 }
 
+bool json_constrained() {
+    // vocabulary: every byte, a few multi-byte pieces, one control token and end-of-sequence
+    std::vector<std::string> texts;
+    for (int b = 0; b < 256; ++b) texts.push_back(std::string(1, static_cast<char>(b)));
+    for (const char* t : {"{\"", "\":", "\": ", " [", "true", "false", "], ", "}}", ", \"", "12", "ab"})
+        texts.push_back(t);
+    const int32_t ctl = static_cast<int32_t>(texts.size());
+    texts.push_back("<|ctl|>");
+    const int32_t eos = static_cast<int32_t>(texts.size());
+    texts.push_back("<|endoftext|>");
+    std::vector<uint8_t> special(texts.size(), 0);
+    special[ctl] = 1;
+    const uint32_t V = static_cast<uint32_t>(texts.size());
+    auto jp = JsonMaskProducer::create(0, texts, special, eos);
+    CHECK(jp.ok());
+    auto made = DeviceSampler::create(0, 4, V);
+    CHECK(made.ok());
+    JsonMaskProducer& g = *jp.value();
+    DeviceSampler& s = *made.value();
+    // the intended answer, greedily tokenised by longest match
+    const std::string doc = "{\"ab\": [12, true, {\"x\": false}], \"c\": {\"d\": {}}}";
+    std::vector<int32_t> want;
+    for (size_t i = 0; i < doc.size();) {
+        int32_t best = -1;
+        size_t bl = 0;
+        for (int32_t t = 0; t < ctl; ++t)
+            if (texts[t].size() > bl && doc.compare(i, texts[t].size(), texts[t]) == 0) best = t, bl = texts[t].size();
+        want.push_back(best);
+        i += bl;
+    }
+    want.push_back(eos);
+    const uint32_t W = g.mask_words();
+    sixi_json_state* d_st = nullptr;
+    uint32_t* d_mask = nullptr;
+    float* d_logits = nullptr;
+    sixi_smp_params* d_p = nullptr;
+    int32_t *d_tok = nullptr, *d_sts = nullptr, *d_gst = nullptr;
+    cudaMalloc(&d_st, sizeof(sixi_json_state));
+    cudaMalloc(&d_mask, 4 * W);
+    cudaMalloc(&d_logits, 4 * V);
+    cudaMalloc(&d_p, sizeof(sixi_smp_params));
+    cudaMalloc(&d_tok, 4);
+    cudaMalloc(&d_sts, 4);
+    cudaMalloc(&d_gst, 4);
+    SamplingParams sp;
+    sp.temperature = 0.0f;
+    const sixi_smp_params p = to_smp_params(sp, true);
+    cudaStream_t st = s.stream();
+    cudaMemcpyAsync(d_p, &p, sizeof p, cudaMemcpyHostToDevice, st);
+    CHECK(g.reset(d_st, 1, st).ok());
+    std::vector<uint8_t> flat;
+    std::vector<uint64_t> off(V + 1, 0);
+    for (uint32_t i = 0; i < V; ++i) {
+        off[i + 1] = off[i] + texts[i].size();
+        flat.insert(flat.end(), texts[i].begin(), texts[i].end());
+    }
+    TestRng gen(11);
+    std::vector<int32_t> got;
+    for (size_t step = 0; step < want.size(); ++step) {
+        std::vector<float> x = normal_row(gen, V, 1.0f);
+        x[want[step]] += 20.0f;
+        x[eos] += 30.0f;  // end-of-sequence scores highest but is allowed only after the object
+        x[ctl] += 40.0f;  // a control token is never allowed
+        cudaMemcpyAsync(d_logits, x.data(), 4 * V, cudaMemcpyHostToDevice, st);
+        CHECK(g.fill_masks(d_st, 1, d_mask, st).ok());
+        sixi_smp_rows rows{d_logits, SIXI_SMP_F32, 1, V};
+        CHECK(s.sample_rows(rows, d_p, d_mask, nullptr, nullptr, nullptr, step, d_tok, d_sts, st).ok());
+        // the device mask of this state equals the CPU automaton's
+        sixi_json_state hs;
+        std::vector<uint32_t> m(W), om(W);
+        cudaMemcpyAsync(&hs, d_st, sizeof hs, cudaMemcpyDeviceToHost, st);
+        cudaMemcpyAsync(m.data(), d_mask, 4 * W, cudaMemcpyDeviceToHost, st);
+        CHECK(g.advance(d_st, 1, d_tok, d_gst, st).ok());
+        int32_t tok = -1, sts = -1, gst = -1;
+        cudaMemcpyAsync(&tok, d_tok, 4, cudaMemcpyDeviceToHost, st);
+        cudaMemcpyAsync(&sts, d_sts, 4, cudaMemcpyDeviceToHost, st);
+        cudaMemcpyAsync(&gst, d_gst, 4, cudaMemcpyDeviceToHost, st);
+        CHECK(cudaStreamSynchronize(st) == cudaSuccess);
+        orc_json_fill_masks(flat.data(), off.data(), special.data(), V, eos, &hs, 1, om.data(), W, 1);
+        CHECK(m == om);
+        CHECK(sts == SIXI_OK && gst == SIXI_OK);
+        got.push_back(tok);
+    }
+    CHECK(got == want);
+    sixi_json_state fin;
+    cudaMemcpy(&fin, d_st, sizeof fin, cudaMemcpyDeviceToHost);
+    CHECK(fin.mode == SIXI_JSON_DONE && fin.failed == 0);
+    cudaFree(d_st);
+    cudaFree(d_mask);
+    cudaFree(d_logits);
+    cudaFree(d_p);
+    cudaFree(d_tok);
+    cudaFree(d_sts);
+    cudaFree(d_gst);
+    return true;
+}
+
 }  // namespace
 
 int main() {
@@ -340,7 +441,8 @@ int main() {
                  {"rng_consumption", rng_consumption},
                  {"errors", errors},
                  {"verify_random", verify_random},
-                 {"verify_forced_rejection", verify_forced_rejection}};
+                 {"verify_forced_rejection", verify_forced_rejection},
+                 {"json_constrained", json_constrained}};
     int passed = 0, n = 0;
     for (auto& t : tests) {
         ++n;

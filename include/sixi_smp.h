@@ -193,6 +193,28 @@ SIXI_SMP_API int32_t sixi_smp_full_distribution(sixi_smp* h, const sixi_smp_rows
                                    float* out_probs, uint64_t out_stride, void* stream);
 
 /*
+ * sixi_smp_verify with dense q given as the draft model's logits: q of draft row r is
+ * compute_full_distribution(draft_logits row r, draft_temperatures[r]) (src/speculative/
+ * speculative.cpp:279-280 builds it so; src/core/core_execution.cpp:409-447), and verification
+ * follows speculative.cpp:801-916 as in sixi_smp_verify with that q. q is never stored: a
+ * statistics pass keeps each draft row's maximum and fp64 sum, and the verifier evaluates q with
+ * the same operations where it reads it (the drafted id; the residual on rejection). Results equal
+ * sixi_smp_full_distribution followed by sixi_smp_verify on the same rows. draft_logits: S*k rows
+ * (fp32 or bf16, row_stride >= vocab); draft_temperatures: [S*k] (device). Other arguments and
+ * outputs as sixi_smp_verify. S*k must not exceed the handle's max_rows.
+ */
+SIXI_SMP_API int32_t sixi_smp_verify_draft_logits(sixi_smp* h, const sixi_smp_rows* target,
+                                                  const sixi_smp_rows* draft_logits,
+                                                  const float* draft_temperatures, const int32_t* drafts,
+                                                  const int32_t* n_drafts, uint32_t n_streams, uint32_t k,
+                                                  const sixi_smp_params* params, const uint32_t* mask_words,
+                                                  const int32_t* hist_tokens, const int64_t* hist_offsets,
+                                                  const double* uniforms, uint64_t step, int32_t* out_accepted,
+                                                  int32_t* out_tokens, int32_t* out_n_tokens,
+                                                  int32_t* out_first_reject, int32_t* out_uniforms_used,
+                                                  int32_t* out_status, void* stream);
+
+/*
  * sixi_smp_verify without a handle and without any allocation (no counterpart in the engine).
  * For callers that may not allocate device memory at all - for instance a serving loop whose
  * device memory is owned by an external allocator, or one that must not call into the CUDA

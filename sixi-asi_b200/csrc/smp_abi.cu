@@ -24,6 +24,7 @@ struct sixi_smp {
     uint32_t vocab;
     uint32_t mask_words;
     VerifyRowResult* ws;         // verifier per-row workspace [max_rows]
+    sixi_b200::DraftStat* qstat; // draft-row distribution statistics [max_rows]
     sixi_smp_params* d_default;  // default params (raw argmax entry)
     // staging of sixi_smp_sample_host
     void* d_logits;
@@ -103,6 +104,70 @@ cudaError_t grow(T** p, size_t* cap, size_t need) {
     return e;
 }
 
+// Verification with dense q stored (draft_probs), evaluated from draft logits (qlog with their
+// temperatures: a statistics pass first), or one-hot (neither).
+int32_t verify_impl(sixi_smp* h, const sixi_smp_rows* target, const float* draft_probs,
+                    const sixi_smp_rows* qlog, const float* qlog_temps, const int32_t* drafts,
+                    const int32_t* n_drafts, uint32_t n_streams, uint32_t k, const sixi_smp_params* params,
+                    const uint32_t* mask_words, const int32_t* hist_tokens, const int64_t* hist_offsets,
+                    const double* uniforms, uint64_t step, int32_t* out_accepted, int32_t* out_tokens,
+                    int32_t* out_n_tokens, int32_t* out_first_reject, int32_t* out_uniforms_used,
+                    int32_t* out_status, void* stream) {
+    if (h == nullptr || !rows_ok(h, target) || params == nullptr || drafts == nullptr ||
+        out_accepted == nullptr || out_tokens == nullptr || out_n_tokens == nullptr ||
+        out_first_reject == nullptr || out_uniforms_used == nullptr || out_status == nullptr ||
+        (hist_tokens != nullptr && hist_offsets == nullptr) || k == 0)
+        return SIXI_INVALID_ARGUMENT;
+    if (static_cast<uint64_t>(n_streams) * (k + 1) != target->n_rows) return SIXI_INVALID_ARGUMENT;
+    if (target->n_rows > h->max_rows) return SIXI_INVALID_ARGUMENT;
+    if (n_streams == 0) return SIXI_OK;
+    if (draft_probs != nullptr && (reinterpret_cast<uintptr_t>(draft_probs) & 3u) != 0)
+        return SIXI_INVALID_ARGUMENT;
+    DeviceGuard g(h->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSuccess;
+    if (qlog != nullptr) {
+        // the draft rows' maxima and sums, with the plan sixi_smp_full_distribution uses for them
+        LaunchPlan dplan{};
+        if (!sixi_b200::plan_rows(h->vocab, qlog->n_rows, &dplan)) return SIXI_INVALID_ARGUMENT;
+        sixi_b200::DistArgs d{};
+        d.data = qlog->data;
+        d.row_stride = qlog->row_stride;
+        d.dtype = qlog->dtype;
+        d.vocab = h->vocab;
+        d.n_rows = qlog->n_rows;
+        d.chunk = dplan.chunk;
+        d.temperatures = qlog_temps;
+        d.out = nullptr;
+        d.stats = h->qstat;
+        e = sixi_b200::launch_full_distribution(d, dplan, s);
+    }
+    LaunchPlan plan{};
+    RowArgs a = base_args(h, target, &plan);
+    a.params = params;
+    a.mask = mask_words;
+    a.hist = hist_tokens;
+    a.hist_off = hist_tokens ? hist_offsets : nullptr;
+    a.uniforms = uniforms;
+    a.step = step;
+    a.q = draft_probs;
+    if (qlog != nullptr) {
+        a.qlog = qlog->data;
+        a.qlog_stride = qlog->row_stride;
+        a.qlog_dtype = qlog->dtype;
+        a.qstat = h->qstat;
+    }
+    a.drafts = drafts;
+    a.n_drafts = n_drafts;
+    a.k = k;
+    a.ws = h->ws;
+    if (e == cudaSuccess) e = sixi_b200::launch_rows(sixi_b200::kModeVerify, a, plan, s);
+    if (e == cudaSuccess)
+        e = sixi_b200::launch_verify_finalize(a, n_streams, out_accepted, out_tokens, out_n_tokens,
+                                              out_first_reject, out_uniforms_used, out_status, s);
+    return from_cuda(e);
+}
+
 }  // namespace
 
 extern "C" {
@@ -127,6 +192,7 @@ int32_t sixi_smp_create(int32_t device, uint32_t max_rows, uint32_t vocab, sixi_
     h->mask_words = (vocab + 31u) / 32u;
     cudaError_t e = cudaSuccess;
     if (max_rows > 0) e = cudaMalloc(&h->ws, sizeof(VerifyRowResult) * max_rows);
+    if (e == cudaSuccess && max_rows > 0) e = cudaMalloc(&h->qstat, sizeof(sixi_b200::DraftStat) * max_rows);
     if (e == cudaSuccess) e = cudaMalloc(&h->d_default, sizeof(sixi_smp_params));
     if (e == cudaSuccess) {
         sixi_smp_params p;
@@ -149,6 +215,7 @@ int32_t sixi_smp_destroy(sixi_smp* h) {
     if (h == nullptr) return SIXI_OK;
     DeviceGuard g(h->device);
     cudaFree(h->ws);
+    cudaFree(h->qstat);
     cudaFree(h->d_default);
     cudaFree(h->d_logits);
     cudaFree(h->d_params);
@@ -328,36 +395,25 @@ int32_t sixi_smp_verify(sixi_smp* h, const sixi_smp_rows* target, const float* d
                         const double* uniforms, uint64_t step, int32_t* out_accepted,
                         int32_t* out_tokens, int32_t* out_n_tokens, int32_t* out_first_reject,
                         int32_t* out_uniforms_used, int32_t* out_status, void* stream) {
-    if (h == nullptr || !rows_ok(h, target) || params == nullptr || drafts == nullptr ||
-        out_accepted == nullptr || out_tokens == nullptr || out_n_tokens == nullptr ||
-        out_first_reject == nullptr || out_uniforms_used == nullptr || out_status == nullptr ||
-        (hist_tokens != nullptr && hist_offsets == nullptr) || k == 0)
+    return verify_impl(h, target, draft_probs, nullptr, nullptr, drafts, n_drafts, n_streams, k, params, mask_words,
+                       hist_tokens, hist_offsets, uniforms, step, out_accepted, out_tokens, out_n_tokens,
+                       out_first_reject, out_uniforms_used, out_status, stream);
+}
+
+int32_t sixi_smp_verify_draft_logits(sixi_smp* h, const sixi_smp_rows* target, const sixi_smp_rows* draft_logits,
+                                     const float* draft_temperatures, const int32_t* drafts,
+                                     const int32_t* n_drafts, uint32_t n_streams, uint32_t k,
+                                     const sixi_smp_params* params, const uint32_t* mask_words,
+                                     const int32_t* hist_tokens, const int64_t* hist_offsets,
+                                     const double* uniforms, uint64_t step, int32_t* out_accepted,
+                                     int32_t* out_tokens, int32_t* out_n_tokens, int32_t* out_first_reject,
+                                     int32_t* out_uniforms_used, int32_t* out_status, void* stream) {
+    if (h == nullptr || draft_logits == nullptr || !rows_ok(h, draft_logits) || draft_temperatures == nullptr ||
+        static_cast<uint64_t>(n_streams) * k != draft_logits->n_rows)
         return SIXI_INVALID_ARGUMENT;
-    if (static_cast<uint64_t>(n_streams) * (k + 1) != target->n_rows) return SIXI_INVALID_ARGUMENT;
-    if (target->n_rows > h->max_rows) return SIXI_INVALID_ARGUMENT;
-    if (n_streams == 0) return SIXI_OK;
-    if (draft_probs != nullptr && (reinterpret_cast<uintptr_t>(draft_probs) & 3u) != 0)
-        return SIXI_INVALID_ARGUMENT;
-    DeviceGuard g(h->device);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    LaunchPlan plan{};
-    RowArgs a = base_args(h, target, &plan);
-    a.params = params;
-    a.mask = mask_words;
-    a.hist = hist_tokens;
-    a.hist_off = hist_tokens ? hist_offsets : nullptr;
-    a.uniforms = uniforms;
-    a.step = step;
-    a.q = draft_probs;
-    a.drafts = drafts;
-    a.n_drafts = n_drafts;
-    a.k = k;
-    a.ws = h->ws;
-    cudaError_t e = sixi_b200::launch_rows(sixi_b200::kModeVerify, a, plan, s);
-    if (e == cudaSuccess)
-        e = sixi_b200::launch_verify_finalize(a, n_streams, out_accepted, out_tokens, out_n_tokens,
-                                              out_first_reject, out_uniforms_used, out_status, s);
-    return from_cuda(e);
+    return verify_impl(h, target, nullptr, draft_logits, draft_temperatures, drafts, n_drafts, n_streams, k, params,
+                       mask_words, hist_tokens, hist_offsets, uniforms, step, out_accepted, out_tokens,
+                       out_n_tokens, out_first_reject, out_uniforms_used, out_status, stream);
 }
 
 int32_t sixi_smp_full_distribution(sixi_smp* h, const sixi_smp_rows* rows, const float* temperatures,

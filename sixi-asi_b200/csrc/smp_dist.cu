@@ -1,6 +1,8 @@
 // smp_dist.cu - full-vocabulary softmax rows (sixi_smp_full_distribution), the producer of dense
 // draft distributions: DeterministicSampler::compute_full_distribution
-// (src/core/core_execution.cpp:409-447) per row, with one cluster of CTAs per row.
+// (src/core/core_execution.cpp:409-447) per row, with one cluster of CTAs per row. With `stats` and
+// no `out` only the row's maximum and sum are kept (DraftStat), from which the verifier evaluates
+// the same q values where it reads them (sixi_smp_verify_draft_logits).
 //
 //   temperature <= 0  a one-hot row at the raw argmax (strict >, so the lowest id wins ties, a NaN
 //                     at index 0 wins and other NaNs never do; sample_greedy_argmax)
@@ -54,7 +56,7 @@ __global__ void __launch_bounds__(kDT, 1) dist_kernel(const DistArgs a) {
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const uint8_t* rowp = static_cast<const uint8_t*>(a.data) +
                           static_cast<size_t>(row) * a.row_stride * (a.dtype == SIXI_SMP_BF16 ? 2 : 4);
-    float* out = a.out + static_cast<size_t>(row) * a.out_stride;
+    float* out = a.out != nullptr ? a.out + static_cast<size_t>(row) * a.out_stride : nullptr;
     const uint32_t c0 = crank * a.chunk;
     const uint32_t c1 = c0 + a.chunk < a.vocab ? c0 + a.chunk : a.vocab;
     const float T = a.temperatures[row];
@@ -80,7 +82,10 @@ __global__ void __launch_bounds__(kDT, 1) dist_kernel(const DistArgs a) {
         for (uint32_t q = 0; q < C; ++q) b = sh.best[q] > b ? sh.best[q] : b;
         const float x0 = dist_logit(a, rowp, 0);
         const uint32_t win = (x0 != x0 || b == 0ull) ? 0u : comp_id(b);
-        for (uint32_t e = c0 + tid; e < c1; e += kDT) out[e] = e == win ? 1.0f : 0.0f;
+        if (a.stats != nullptr && crank == 0 && tid == 0)
+            a.stats[row] = DraftStat{0.0, 0.0, 0.0, static_cast<int32_t>(win), 1};
+        if (a.out != nullptr)
+            for (uint32_t e = c0 + tid; e < c1; e += kDT) out[e] = e == win ? 1.0f : 0.0f;
         return;
     }
     const double inv_temp = 1.0 / static_cast<double>(T);
@@ -143,6 +148,9 @@ __global__ void __launch_bounds__(kDT, 1) dist_kernel(const DistArgs a) {
     cluster.sync();
     double sum = 0.0;
     for (uint32_t q = 0; q < C; ++q) sum += sh.sm[q];
+    if (a.stats != nullptr && crank == 0 && tid == 0)
+        a.stats[row] = DraftStat{inv_temp, max_scaled, sum, 0, (zero || !(sum > 0.0)) ? 2 : 0};
+    if (a.out == nullptr) return;
     // 3. the probabilities
     if (zero || !(sum > 0.0)) {
         for (uint32_t e = c0 + tid; e < c1; e += kDT) out[e] = 0.0f;

@@ -24,6 +24,20 @@ struct VerifyRowResult {
     int32_t pad;
 };
 
+// Statistics of one draft row's full distribution (DeterministicSampler::compute_full_distribution,
+// src/core/core_execution.cpp:409-447): q_i = float(exp(x_i * inv_t - maxs) / sum) (mode 0), one-hot
+// at `amax` (mode 1: temperature <= 0), or all zero (mode 2: a NaN or +inf logit, no finite
+// maximum, or a sum that is not positive). Written by dist_kernel's statistics pass, read by the
+// verifier, so that q is evaluated where it is needed instead of being stored.
+struct DraftStat {
+    double inv_t;
+    double maxs;
+    double sum;
+    int32_t amax;
+    int32_t mode;
+};
+static_assert(sizeof(DraftStat) == 32, "DraftStat layout");
+
 struct RowArgs {
     const void* data;
     uint64_t row_stride;  // elements
@@ -40,7 +54,11 @@ struct RowArgs {
     const double* uniforms;
     uint64_t step;
     // verify
-    const float* q;
+    const float* q;            // dense draft probabilities [S*k][row_stride], or
+    const void* qlog;          // draft logits [S*k][qlog_stride] (dtype qlog_dtype) with their
+    const DraftStat* qstat;    //   distribution statistics [S*k]: q evaluated on demand
+    uint64_t qlog_stride;
+    uint32_t qlog_dtype;
     const int32_t* drafts;
     const int32_t* n_drafts;
     uint32_t k;
@@ -127,8 +145,9 @@ struct DistArgs {
     uint32_t n_rows;
     uint32_t chunk;       // elements per CTA of a row's cluster
     const float* temperatures;
-    float* out;
+    float* out;           // the distribution rows, or nullptr with `stats` (statistics only)
     uint64_t out_stride;  // elements
+    DraftStat* stats;     // per-row statistics (nullable)
 };
 cudaError_t launch_full_distribution(const DistArgs& a, const LaunchPlan& plan, cudaStream_t stream);
 cudaError_t launch_shard_candidates(const ShardArgs& a, cudaStream_t stream);

@@ -209,7 +209,7 @@ __device__ RowCtx make_row_ctx(const RowArgs& a, uint32_t row) {
         r.greedy = r.p->temperature <= 0.0f;
         // history: base + drafts[0..i) (draft rows); bonus: base (dense q) or base + all drafts
         r.extra = d;
-        r.n_extra = r.vrole == 0 ? static_cast<int32_t>(i) : (a.q ? 0 : (nd > 0 ? nd : 0));
+        r.n_extra = r.vrole == 0 ? static_cast<int32_t>(i) : ((a.q || a.qlog) ? 0 : (nd > 0 ? nd : 0));
         if (a.hist && a.hist_off) {
             r.hist = a.hist + a.hist_off[s];
             r.nh = a.hist_off[s + 1] - a.hist_off[s];
@@ -708,6 +708,45 @@ struct Refine {
 };
 
 // ---------------------------------------------------------------------------------------------
+
+// Draft probabilities of one draft row as the verifier reads them: stored (dense q) or evaluated
+// from the draft logits and their DraftStat with the engine's operations
+// (compute_full_distribution, src/core/core_execution.cpp:409-447): a multiply, a subtract, exp,
+// one division by the fp64 sum, rounded to float.
+struct QView {
+    const float* q;
+    const uint8_t* lg;
+    uint32_t dt;
+    double inv_t, maxs, sum;
+    int32_t amax, mode;
+};
+
+__device__ __forceinline__ QView q_view(const RowArgs& a, size_t qr) {
+    QView v{};
+    if (a.q != nullptr) {
+        v.q = a.q + qr * a.row_stride;
+        return v;
+    }
+    const DraftStat st = a.qstat[qr];
+    v.lg = static_cast<const uint8_t*>(a.qlog) + qr * a.qlog_stride * (a.qlog_dtype == SIXI_SMP_BF16 ? 2u : 4u);
+    v.dt = a.qlog_dtype;
+    v.inv_t = st.inv_t;
+    v.maxs = st.maxs;
+    v.sum = st.sum;
+    v.amax = st.amax;
+    v.mode = st.mode;
+    return v;
+}
+
+__device__ __forceinline__ float q_of(const QView& v, uint32_t i) {
+    if (v.q != nullptr) return v.q[i];
+    if (v.mode == 2) return 0.0f;
+    if (v.mode == 1) return i == static_cast<uint32_t>(v.amax) ? 1.0f : 0.0f;
+    const float x = v.dt == SIXI_SMP_BF16
+                        ? __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(v.lg)[i]) << 16)
+                        : reinterpret_cast<const float*>(v.lg)[i];
+    return static_cast<float>(exp(__dsub_rn(__dmul_rn(static_cast<double>(x), v.inv_t), v.maxs)) / v.sum);
+}
 
 // The mass-path histogram pass (block-wide): fixed-point weights of the keys K[0, 4 * nq) in three
 // 32-bit parts, w = a * 2^32 + b * 2^16 + c (a < 2^12, b, c < 2^16): with at most 2^16 keys per
@@ -1492,11 +1531,11 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             const uint32_t dpos = __reduce_min_sync(0xFFFFFFFFu, mine);
             const double pd = (dpos == 0xFFFFFFFFu) ? 0.0 : FP[dpos];
             const bool in_range = d >= 0 && static_cast<uint32_t>(d) < a.vocab;
-            if (a.q != nullptr) {
+            if (a.q != nullptr || a.qlog != nullptr) {
                 // dense draft probabilities (speculative.cpp:823-903)
-                const float* qrow = a.q + (static_cast<size_t>(rc.stream) * a.k + rc.vidx) * a.row_stride;
+                const QView qv = q_view(a, static_cast<size_t>(rc.stream) * a.k + rc.vidx);
                 const float p_d = static_cast<float>(pd);
-                const float q_d = in_range ? qrow[d] : 1.0f;
+                const float q_d = in_range ? q_of(qv, static_cast<uint32_t>(d)) : 1.0f;
                 const double accept_prob = (q_d <= 0.0f) ? (p_d > 0.0f ? 1.0 : 0.0)
                     : fmin(1.0, static_cast<double>(p_d) / fmax(1e-12, static_cast<double>(q_d)));
                 res_accept = rc.u_accept < accept_prob ? 1 : 0;
@@ -1511,7 +1550,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                         res[j] = 0.0;
                         if (idx < keep) {
                             const uint32_t id = comp_id(FL[idx]);
-                            res[j] = fmax(0.0, static_cast<double>(static_cast<float>(pr[j])) - static_cast<double>(qrow[id]));
+                            res[j] = fmax(0.0, static_cast<double>(static_cast<float>(pr[j])) - static_cast<double>(q_of(qv, id)));
                         }
                         rs += res[j];
                     }
@@ -2156,7 +2195,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 } else {
                     if (owner == static_cast<int>(crank)) {
                         // ordered scan of my entries in vocabulary-id order
-                        const float* qrow = a.q + (static_cast<size_t>(rc.stream) * a.k + rc.vidx) * a.row_stride + c0;
+                        const QView qv = q_view(a, static_cast<size_t>(rc.stream) * a.k + rc.vidx);
                         const double zk_d = static_cast<double>(st.zkept);
                         double run = before;
                         unsigned long long found = ~0ull;
@@ -2175,7 +2214,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                                         const float x = kval(k);
                                         if (cp >= st.xcross && cp >= st.kbound && x >= x_minp) {
                                             const float pf = static_cast<float>(static_cast<double>(weight_of(x, wc)) / zk_d);
-                                            v = use_res ? fmax(0.0, static_cast<double>(pf) - static_cast<double>(qrow[e]))
+                                            v = use_res ? fmax(0.0, static_cast<double>(pf) - static_cast<double>(q_of(qv, static_cast<uint32_t>(c0 + e))))
                                                         : static_cast<double>(pf);
                                         }
                                     }
@@ -2308,10 +2347,10 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                         pd = ed / (static_cast<double>(st.zkept) / kWeightScale);
                     }
                     const bool in_range = rc.draft >= 0 && static_cast<uint32_t>(rc.draft) < a.vocab;
-                    if (a.q != nullptr) {
-                        const float* qrow = a.q + (static_cast<size_t>(rc.stream) * a.k + rc.vidx) * a.row_stride;
+                    if (a.q != nullptr || a.qlog != nullptr) {
+                        const QView qv = q_view(a, static_cast<size_t>(rc.stream) * a.k + rc.vidx);
                         const float p_d = static_cast<float>(pd);
-                        const float q_d = in_range ? qrow[rc.draft] : 1.0f;
+                        const float q_d = in_range ? q_of(qv, static_cast<uint32_t>(rc.draft)) : 1.0f;
                         const double accept_prob = (q_d <= 0.0f) ? (p_d > 0.0f ? 1.0 : 0.0)
                             : fmin(1.0, static_cast<double>(p_d) / fmax(1e-12, static_cast<double>(q_d)));
                         res_accept = rc.u_accept < accept_prob ? 1 : 0;
@@ -2319,7 +2358,6 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                             st.stage = kStDone;
                         } else {
                             // partial sums of the residual and of p_target over this chunk
-                            const float* qrow_c = qrow + c0;
                             const double zk_d = static_cast<double>(st.zkept);
                             double rsum = 0.0, psum = 0.0;
                             for (int e = tid; e < len; e += kNT) {
@@ -2329,7 +2367,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                                 const float x = kval(k);
                                 if (!(cp >= st.xcross && cp >= st.kbound && x >= x_minp)) continue;
                                 const float pf = static_cast<float>(static_cast<double>(weight_of(x, wc)) / zk_d);
-                                rsum += fmax(0.0, static_cast<double>(pf) - static_cast<double>(qrow_c[e]));
+                                rsum += fmax(0.0, static_cast<double>(pf) - static_cast<double>(q_of(qv, static_cast<uint32_t>(c0 + e))));
                                 psum += static_cast<double>(pf);
                             }
                             rsum = block_sum_f64(rsum, ls);

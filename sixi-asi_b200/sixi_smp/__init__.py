@@ -86,6 +86,8 @@ SIGNATURES = {
     "sixi_smp_verify": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32, _P, _P, _P, _P, _P,
                                _U64, _P, _P, _P, _P, _P, _P, _P]),
     "sixi_smp_full_distribution": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _U64, _P]),
+    "sixi_smp_verify_draft_logits": (_I32, [_P, ctypes.POINTER(Rows), ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32,
+                                            _P, _P, _P, _P, _P, _U64, _P, _P, _P, _P, _P, _P, _P]),
     "sixi_smp_verify_static": (_I32, [_I32, _U32, ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32, _P, _P, _P,
                                       _P, _P, _U64, _P, _P, _P, _P, _P, _P, _P]),
     "sixi_smp_shard_candidates": (_I32, [_P, ctypes.POINTER(Rows), _U32, _U32, _U32, _P, _P, _P, _P, _U32,
@@ -266,6 +268,29 @@ class Sampler:
                                  _ptr(hist_off), _ptr(uniforms), step, _ptr(acc), _ptr(toks), _ptr(ntok),
                                  _ptr(frej), _ptr(used), _ptr(sts), self._stream(stream))
         _check("sixi_smp_verify", st)
+        return dict(accepted=acc, tokens=toks, n_tokens=ntok, first_reject=frej, uniforms_used=used,
+                    status=sts)
+
+    def verify_draft_logits(self, target, draft_logits, draft_temperatures, drafts, params, n_drafts=None,
+                            masks=None, hist=None, hist_off=None, uniforms=None, step=0, stream=None):
+        """verify with q = full_distribution(draft_logits, draft_temperatures), never stored."""
+        import torch
+
+        S, k = drafts.shape
+        dev = target.device
+        acc = torch.empty(S, dtype=torch.int32, device=dev)
+        toks = torch.empty((S, k + 1), dtype=torch.int32, device=dev)
+        ntok = torch.empty(S, dtype=torch.int32, device=dev)
+        frej = torch.empty(S, dtype=torch.int32, device=dev)
+        used = torch.empty(S, dtype=torch.int32, device=dev)
+        sts = torch.empty(S, dtype=torch.int32, device=dev)
+        rows = self._rows(target)
+        qrows = self._rows(draft_logits)
+        st = _lib().sixi_smp_verify_draft_logits(
+            self.h, ctypes.byref(rows), ctypes.byref(qrows), _ptr(draft_temperatures), _ptr(drafts), _ptr(n_drafts),
+            S, k, _ptr(params), _ptr(masks), _ptr(hist), _ptr(hist_off), _ptr(uniforms), step, _ptr(acc),
+            _ptr(toks), _ptr(ntok), _ptr(frej), _ptr(used), _ptr(sts), self._stream(stream))
+        _check("sixi_smp_verify_draft_logits", st)
         return dict(accepted=acc, tokens=toks, n_tokens=ntok, first_reject=frej, uniforms_used=used,
                     status=sts)
 

@@ -9,9 +9,9 @@ device. Configurations:
      top-p ~ U[0.7, 1.0], rep ~ U[1.0, 1.3], histories of U[256, 8192] ids uniform over V
   3  config 2 plus a packed allowed-token bitmask per row, allowed fraction log-uniform in
      [1e-4, 0.6], laid out as contiguous id runs
-  4  S streams x k drafts: bf16 target logits N(0, 3^2) [S, k+1, V], dense draft probabilities
-     softmax(target + N(0, 1)) [S, k, V], drafts sampled from them, 20%-density masks on half the
-     streams
+  4  S streams x k drafts: bf16 target logits N(0, 3^2) [S, k+1, V], draft logits target + N(0, 1)
+     [S, k, V] and their dense probabilities softmax(draft logits), drafts sampled from them,
+     20%-density masks on half the streams
 """
 
 from __future__ import annotations
@@ -176,8 +176,8 @@ def config4(streams: int = 32, k: int = 8, vocab: int = QWEN_VOCAB, seed: int = 
     hist = rng.integers(0, vocab, size=int(off[-1]), dtype=np.int32)
     uniforms = rng.random(size=(streams, k + 1))
     return dict(target_bits=target_bits.reshape(streams * (k + 1), vocab), q=q.reshape(streams * k, vocab),
-                drafts=drafts, params=params, masks=masks, hist=hist, hist_off=off, uniforms=uniforms,
-                k=k, streams=streams)
+                draft_logits=noisy.reshape(streams * k, vocab), drafts=drafts, params=params, masks=masks, hist=hist,
+                hist_off=off, uniforms=uniforms, k=k, streams=streams)
 
 
 def uniforms_for(params: np.ndarray, step: int = 0, slots: int = 1) -> np.ndarray:

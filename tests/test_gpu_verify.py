@@ -107,3 +107,44 @@ def test_verify_greedy_forced_rejections(port):
     ref = port.verify(tgt.reshape(-1, v), drafts, params)
     for key in KEYS:
         assert np.array_equal(o[key].cpu().numpy(), ref[key]), key
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_verify_draft_logits_equals_stored_q(port, dtype):
+    """q evaluated from draft logits inside the verifier == q stored by full_distribution, then
+    verified; both == the oracle (compute_full_distribution, then dense-q verification)."""
+    d = W.config4(streams=8, k=4, vocab=151_936, seed=71, stochastic=True, masked=True)
+    S_, k = d["streams"], d["k"]
+    lg = d["draft_logits"].copy()
+    temps = np.where(np.arange(S_ * k) % 5 == 0, 0.0, 0.6 + 0.1 * (np.arange(S_ * k) % 7)).astype(np.float32)
+    lg[3, 1000] = np.nan  # a row whose distribution is all zero
+    lg[6, :] = -np.inf  # no finite maximum: all zero as well
+    if dtype == "bf16":
+        lg_bits = W.f32_to_bf16_bits(lg)
+        lg = W.bf16_bits_to_f32(lg_bits)
+        d_lg = torch.from_numpy(lg_bits.view(np.int16)).to("cuda").view(torch.bfloat16)
+    else:
+        d_lg = dev(lg)
+    # drafts from the evaluated q (one-hot rows draft their argmax, zero rows keep a random draft)
+    smp = sampler(151_936)
+    q = smp.full_distribution(d_lg, dev(temps))
+    qh = q.cpu().numpy()
+    drafts = d["drafts"].copy()
+    for r in range(S_ * k):
+        if temps[r] <= 0:
+            drafts[r // k, r % k] = int(np.argmax(qh[r]))
+    args = dict(n_drafts=None, masks=dev(d["masks"]), hist=dev(d["hist"]), hist_off=dev(d["hist_off"]),
+                uniforms=dev(d["uniforms"]))
+    tgt = dev(d["target_bits"])
+    fused = smp.verify_draft_logits(tgt, d_lg, dev(temps), dev(drafts), dev(d["params"]), **args)
+    stored = smp.verify(tgt, dev(drafts), dev(d["params"]), draft_probs=q, **args)
+    torch.cuda.synchronize()
+    fused = {kk: v.cpu().numpy() for kk, v in fused.items()}
+    stored = {kk: v.cpu().numpy() for kk, v in stored.items()}
+    for kk in KEYS:
+        assert np.array_equal(fused[kk], stored[kk]), kk
+    qo = np.stack([port.full_distribution(lg[r], float(temps[r])) for r in range(S_ * k)])
+    o = port.verify(W.bf16_bits_to_f32(d["target_bits"]), drafts, d["params"], q=qo, masks=d["masks"],
+                    hist=d["hist"], hist_off=d["hist_off"], uniforms=d["uniforms"])
+    for kk in KEYS:
+        assert np.array_equal(fused[kk], o[kk]), f"{kk}: gpu={fused[kk]} oracle={o[kk]}"

@@ -312,6 +312,47 @@ def run_workload(args) -> int:
         metric = "speculative verify stream-steps/s (config 4: S=32, k=8, V=151,936, bf16 target, fp32 q)"
         data = "synthetic; 2 rotating batches (491 MB > L2)"
         launches = 2 * args.steps  # row kernel + per-stream finalize
+    elif args.workload == "config4f":
+        # the drafter -> verifier pipeline from draft logits: q = full_distribution(draft logits)
+        # evaluated inside the verifier (sixi_smp_verify_draft_logits), beside the two-launch
+        # pipeline that stores q first (sixi_smp_full_distribution + sixi_smp_verify)
+        streams, k = 32, 8
+        nbuf = 2
+        ds = [W.config4(streams=streams, k=k, vocab=VOCAB, seed=40 + i, stochastic=True, masked=True)
+              for i in range(nbuf)]
+        tgt = [t(x["target_bits"]) for x in ds]
+        dlg = [t(x["draft_logits"]) for x in ds]
+        dr = [t(x["drafts"]) for x in ds]
+        temps = torch.ones(streams * k, dtype=torch.float32, device=dev)
+        params, masks = t(ds[0]["params"]), t(ds[0]["masks"])
+        hist, hoff = t(ds[0]["hist"]), t(ds[0]["hist_off"])
+        u = [t(x["uniforms"]) for x in ds]
+        smp = S.Sampler(0, streams * (k + 1), VOCAB)
+        qbuf = torch.empty((streams * k, VOCAB), dtype=torch.float32, device=dev)
+
+        def step(i):
+            smp.verify_draft_logits(tgt[i % nbuf], dlg[i % nbuf], temps, dr[i % nbuf], params, masks=masks,
+                                    hist=hist, hist_off=hoff, uniforms=u[i % nbuf], stream=torch.cuda.current_stream())
+
+        def step_stored(i):
+            cs = torch.cuda.current_stream()
+            q = smp.full_distribution(dlg[i % nbuf], temps, stream=cs)
+            smp.verify(tgt[i % nbuf], dr[i % nbuf], params, draft_probs=q, masks=masks, hist=hist, hist_off=hoff,
+                       uniforms=u[i % nbuf], stream=cs)
+
+        ms = _graph_ms(step, args.steps, args.warmup, stream)
+        ms_stored = _graph_ms(step_stored, args.steps, args.warmup, stream)
+        # bytes that must be read: targets and draft logits in full (the statistics pass), masks,
+        # drafts, histories
+        nbytes = (streams * (k + 1) * VOCAB * 2 + streams * k * VOCAB * 4 + masks.numel() * 4 + streams * k * 4 +
+                  4 * int(ds[0]["hist_off"][-1]))
+        unit, value = "stream-steps/s", streams * args.steps / (ms / 1e3)
+        metric = ("speculative verify from draft logits, stream-steps/s (S=32, k=8, V=151,936, bf16 target, "
+                  "fp32 draft logits; q evaluated in the verifier)")
+        data = "synthetic; 2 rotating batches (477 MB > L2)"
+        launches = 3 * args.steps  # statistics pass + row kernel + per-stream finalize
+        extra = {"stored_q_stream_steps_per_s": streams * args.steps / (ms_stored / 1e3),
+                 "stored_q_ms_per_step": ms_stored / args.steps}
     elif args.workload == "grammar":
         from sixi_smp.json_grammar import JsonGrammar, Tokenizer, json_documents, json_vocab, prefix_states_tokens
 
@@ -391,15 +432,16 @@ def run_workload(args) -> int:
     line = {
         "metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": unit != "us/step", "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32" if args.workload != "config4" else "bf16", "data": data,
+        "dtype": "bf16" if args.workload.startswith("config4") else "f32", "data": data,
         "config": {"workload": args.workload},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": profiled_traffic("verify_config4_traffic.md") if args.workload == "config4" else None,
                      "peak_source": peak_kind, "bytes_per_launch": int(nbytes)},
         "gpu_launches": launches,
     }
-    if args.workload == "grammar":
+    if args.workload in ("grammar", "config4f"):
         line.update(extra)
+    if args.workload == "grammar":
         gram_obj.close()
     print(json.dumps(line), flush=True)
     smp.close()
@@ -415,7 +457,8 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="config2", choices=["config2", "config1", "config3", "config4", "grammar"],
+    ap.add_argument("--workload", default="config2", choices=["config2", "config1", "config3", "config4", "config4f",
+                                                                 "grammar"],
                     help="config2 is the headline line; the others are reported beside it (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

@@ -27,11 +27,15 @@ namespace cg = cooperative_groups;
 namespace sixi_b200 {
 namespace {
 
-constexpr int kDT = 512;
+constexpr int kDT = 256;
 constexpr int kDW = kDT / 32;
 constexpr int kDMaxC = 16;
+constexpr uint32_t kDChunk = 12288;     // preferred largest chunk per CTA (48 KB of fp32)
+constexpr uint32_t kDMaxChunk = 37984;  // hard limit: 16 CTAs cover the row engine's widest vocabulary
+constexpr uint32_t kDWaitIters = 1u << 24;  // bound of the bulk-copy wait
 
 struct DistShared {
+    uint64_t mbar;                   // completion of the chunk's bulk copy
     double mx[kDMaxC];               // per-CTA scaled maxima (pushed by every CTA)
     double sm[kDMaxC];               // per-CTA partial sums
     unsigned int bad[kDMaxC];        // per-CTA NaN / +inf flags
@@ -47,8 +51,9 @@ __device__ __forceinline__ float dist_logit(const DistArgs& a, const uint8_t* ro
     return reinterpret_cast<const float*>(row)[e];
 }
 
-__global__ void __launch_bounds__(kDT, 1) dist_kernel(const DistArgs a) {
+__global__ void __launch_bounds__(kDT, 4) dist_kernel(const DistArgs a) {
     __shared__ DistShared sh;
+    extern __shared__ __align__(16) uint8_t xs[];  // the chunk's raw elements (fp32 or bf16)
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t C = cluster.num_blocks();
     const uint32_t crank = cluster.block_rank();
@@ -89,14 +94,46 @@ __global__ void __launch_bounds__(kDT, 1) dist_kernel(const DistArgs a) {
         return;
     }
     const double inv_temp = 1.0 / static_cast<double>(T);
-    // 1. the scaled maximum (NaN ignored) and the non-finite flag of this chunk
+    // 1. the chunk staged in shared memory by one bulk copy (phases 2 and 3 read it there; the
+    // unaligned head or ragged tail with plain loads), its scaled maximum (NaN ignored) and its
+    // non-finite flag
+    const uint32_t n = c1 > c0 ? c1 - c0 : 0u;
+    const uint32_t esz = a.dtype == SIXI_SMP_BF16 ? 2u : 4u;
+    const uint8_t* src = rowp + static_cast<size_t>(c0) * esz;
+    const uint32_t nbulk = (reinterpret_cast<uintptr_t>(src) & 15u) == 0u ? (n * esz) / 16u * 16u / esz : 0u;
+    if (tid == 0) {
+        mbar_init(&sh.mbar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0 && nbulk > 0u) {
+        mbar_arrive_expect_tx(&sh.mbar, nbulk * esz);
+        for (uint32_t off = 0; off < nbulk * esz; off += 32768u) {
+            const uint32_t nb = nbulk * esz - off < 32768u ? nbulk * esz - off : 32768u;
+            bulk_g2s(xs + off, src + off, nb, &sh.mbar);
+        }
+    }
+    uint32_t first = nbulk;  // elements still to load with plain loads
+    if (nbulk > 0u && !mbar_wait(&sh.mbar, 0, kDWaitIters)) first = 0u;  // not expected: reload all
+    for (uint32_t e = first + tid; e < n; e += kDT) {
+        if (esz == 2u) {
+            reinterpret_cast<uint16_t*>(xs)[e] = reinterpret_cast<const uint16_t*>(src)[e];
+        } else {
+            reinterpret_cast<float*>(xs)[e] = reinterpret_cast<const float*>(src)[e];
+        }
+    }
+    __syncthreads();
+    auto xs_at = [&](uint32_t e) -> float {
+        if (esz == 2u) return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(xs)[e]) << 16);
+        return reinterpret_cast<const float*>(xs)[e];
+    };
     double mx = -INFINITY;
     unsigned int bad = 0u;
-    for (uint32_t e = c0 + tid; e < c1; e += kDT) {
-        const float x = dist_logit(a, rowp, e);
+    for (uint32_t e = tid; e < n; e += kDT) {
+        const float x = xs_at(e);
         bad |= (x != x || x == INFINITY) ? 1u : 0u;
-        const double s = __dmul_rn(static_cast<double>(x), inv_temp);
-        mx = s > mx ? s : mx;
+        const double sc = __dmul_rn(static_cast<double>(x), inv_temp);
+        mx = sc > mx ? sc : mx;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -131,11 +168,23 @@ __global__ void __launch_bounds__(kDT, 1) dist_kernel(const DistArgs a) {
     }
     // every x * inv_temp - max is NaN when the row holds a NaN or +inf, or is all -inf: zeros
     const bool zero = any_bad != 0u || max_scaled == -INFINITY;
-    // 2. the partial sums of exp(x * inv_temp - max)
+    // 2. the partial sums of exp(x * inv_temp - max), in the same element order as before staging
     double s = 0.0;
     if (!zero) {
-        for (uint32_t e = c0 + tid; e < c1; e += kDT)
-            s += exp(__dsub_rn(__dmul_rn(static_cast<double>(dist_logit(a, rowp, e)), inv_temp), max_scaled));
+        // four independent exponentials per step, added in element order (the sum is the same as
+        // with one element per step)
+        auto term = [&](uint32_t e) {
+            return exp(__dsub_rn(__dmul_rn(static_cast<double>(xs_at(e)), inv_temp), max_scaled));
+        };
+        uint32_t e = tid;
+        for (; e + 3u * kDT < n; e += 4u * kDT) {
+            const double t0 = term(e), t1 = term(e + kDT), t2 = term(e + 2u * kDT), t3 = term(e + 3u * kDT);
+            s += t0;
+            s += t1;
+            s += t2;
+            s += t3;
+        }
+        for (; e < n; e += kDT) s += term(e);
     }
     s = warp_sum_f64(s);
     if (lane == 0) sh.redd[w] = s;
@@ -156,32 +205,45 @@ __global__ void __launch_bounds__(kDT, 1) dist_kernel(const DistArgs a) {
         for (uint32_t e = c0 + tid; e < c1; e += kDT) out[e] = 0.0f;
         return;
     }
-    for (uint32_t e = c0 + tid; e < c1; e += kDT) {
-        const double ex = exp(__dsub_rn(__dmul_rn(static_cast<double>(dist_logit(a, rowp, e)), inv_temp), max_scaled));
-        out[e] = static_cast<float>(ex / sum);
+    for (uint32_t e = tid; e < n; e += kDT) {
+        const double ex = exp(__dsub_rn(__dmul_rn(static_cast<double>(xs_at(e)), inv_temp), max_scaled));
+        out[c0 + e] = static_cast<float>(ex / sum);
     }
 }
 
 }  // namespace
 
-cudaError_t launch_full_distribution(const DistArgs& a, const LaunchPlan& plan, cudaStream_t stream) {
-    static std::atomic<uint64_t> ready{0};  // cluster-size attribute set once per device
+// The distribution's own launch shape: clusters wide enough (up to 16 CTAs) that a CTA's chunk takes
+// at most 48 KB of shared memory, so that four CTAs (256 threads each) share an SM and one CTA's
+// bulk copy and cluster barriers overlap another's fp64 arithmetic. The row engine's plan is not
+// used.
+cudaError_t launch_full_distribution(const DistArgs& args, const LaunchPlan& plan, cudaStream_t stream) {
+    (void)plan;
+    static std::atomic<uint64_t> ready{0};  // attributes set once per device
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
     if (!(ready.load(std::memory_order_acquire) & bit)) {
         cudaError_t e = cudaFuncSetAttribute(dist_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(dist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(4u * kDMaxChunk));
         if (e != cudaSuccess) return e;
         ready.fetch_or(bit, std::memory_order_acq_rel);
     }
+    uint32_t c = 1;
+    while (c < static_cast<uint32_t>(kDMaxC) && (args.vocab + c - 1) / c > kDChunk) c *= 2;
+    DistArgs a = args;
+    a.chunk = ((args.vocab + c - 1) / c + 7u) / 8u * 8u;  // 16-byte aligned chunk starts
+    if (a.chunk > kDMaxChunk) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.n_rows * plan.cluster);
+    cfg.gridDim = dim3(a.n_rows * c);
     cfg.blockDim = dim3(kDT);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = 4u * a.chunk;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = plan.cluster;
+    attr[0].val.clusterDim.x = c;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;

@@ -752,12 +752,18 @@ __device__ __forceinline__ float q_of(const QView& v, uint32_t i) {
 // 32-bit parts, w = a * 2^32 + b * 2^16 + c (a < 2^12, b, c < 2^16): with at most 2^16 keys per
 // CTA none of the part sums can wrap, so the adds are fire-and-forget. Returns this thread's
 // share of the min-p prefix mass (keys >= x_minp) when use_minp. Kept out of line so that the
-// loop is scheduled with the whole register budget.
+// loop is scheduled with the whole register budget. The adds are predicated reductions (no
+// branches): on the key being valid and the part being non-zero; the b, a and count parts are
+// at fixed offsets from one address (HA = HB + kABins, HC = HB + 2 kABins).
 static __device__ __noinline__ unsigned long long mass_histogram(const uint32_t* K, int nq, const WeightCtx wc,
                                                           float x_minp, bool use_minp, bool need_counts,
                                                           uint32_t* HLO, uint32_t* HB, uint32_t* HA,
                                                           uint32_t* HC) {
+    static_assert(kABins * 4 == 8192, "part offsets below");
+    (void)HA;
+    (void)HC;
     const int tid = threadIdx.x;
+    const uint32_t lo_base = smem_u32(HLO), hi_base = smem_u32(HB);
     unsigned long long wp = 0ull;
     const int nq8 = (nq + 1) >> 1;
     const int it8 = (nq8 + kNT - 1) / kNT;
@@ -772,16 +778,32 @@ static __device__ __noinline__ unsigned long long mass_histogram(const uint32_t*
         for (int i = 0; i < 8; ++i) {
             const uint32_t k = k8[i];
             const float x = kval(k);
-            const unsigned long long w = (k != 0u) ? weight_of(x, wc) : 0ull;
-            const int b = abin_of(x, wc);
-            if (use_minp) wp += (x >= x_minp) ? w : 0ull;
+            const unsigned long long w = weight_of(x, wc);  // meaningless for k == 0 (never added)
+            const uint32_t b = static_cast<uint32_t>(abin_of(x, wc));
             const uint32_t c = static_cast<uint32_t>(w) & 0xFFFFu;
-            const uint32_t bm = static_cast<uint32_t>(w >> 16) & 0xFFFFu;
+            const uint32_t bm = static_cast<uint32_t>(w) >> 16;
             const uint32_t am = static_cast<uint32_t>(w >> 32);
-            if (c != 0u) atomicAdd(&HLO[b], c);
-            if (bm != 0u) atomicAdd(&HB[b], bm);
-            if (am != 0u) atomicAdd(&HA[b], am);
-            if (need_counts && k != 0u) atomicAdd(&HC[b], 1u);
+            const uint32_t alo = lo_base + 4u * b, ahi = hi_base + 4u * b;
+            asm volatile(
+                "{\n\t.reg .pred pk, p;\n\t"
+                "setp.ne.u32 pk, %0, 0;\n\t"
+                "setp.ne.and.u32 p, %3, 0, pk;\n\t"
+                "@p red.shared.add.u32 [%1], %3;\n\t"
+                "setp.ne.and.u32 p, %4, 0, pk;\n\t"
+                "@p red.shared.add.u32 [%2], %4;\n\t"
+                "setp.ne.and.u32 p, %5, 0, pk;\n\t"
+                "@p red.shared.add.u32 [%2+8192], %5;\n\t}" ::"r"(k),
+                "r"(alo), "r"(ahi), "r"(c), "r"(bm), "r"(am)
+                : "memory");
+            if (need_counts) {
+                asm volatile(
+                    "{\n\t.reg .pred pk;\n\t"
+                    "setp.ne.u32 pk, %0, 0;\n\t"
+                    "@pk red.shared.add.u32 [%1+16384], 1;\n\t}" ::"r"(k),
+                    "r"(ahi)
+                    : "memory");
+            }
+            if (use_minp) wp += (k != 0u && x >= x_minp) ? w : 0ull;
         }
     }
     return wp;
@@ -1724,6 +1746,33 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         }
         return lo;
     };
+    // The same boundary found by a whole warp: 32 consecutive keys tested per round in a window
+    // that starts at the estimate and moves by 32 keys until it holds the change of bin (the bin
+    // is monotone in the key, so the ballot is a run of zeros then ones); bisection after that.
+    auto first_key_bin_le_warp = [&](int bb) -> unsigned long long {
+        if (bb < 0 || xbin_g(kmax) > bb) return static_cast<unsigned long long>(kmax) + 1ull;
+        if (xbin_g(min_key) <= bb) return min_key;
+        // the answer lies in [lo, hi]: bin(lo - 1) > bb >= bin(hi)
+        const uint32_t lo = min_key + 1u, hi = kmax;
+        uint32_t k = fkey(static_cast<float>(static_cast<double>(M) - static_cast<double>(bb + 1) * inv_tscale));
+        k = k < lo ? lo : (k > hi ? hi : k);
+        uint32_t start = k - lo >= 16u ? k - 16u : lo;
+#pragma unroll 1
+        for (int it = 0; it < 32; ++it) {
+            const uint32_t kj = start + static_cast<uint32_t>(lane);
+            const bool le = kj >= hi || kj < start || xbin_g(kj) <= bb;  // past hi (or wrapped): true
+            const unsigned bal = __ballot_sync(0xFFFFFFFFu, le);
+            if (bal == 0u) {
+                start += 32u;  // the answer is above the window, so start + 32 <= answer <= hi
+            } else if (bal & 1u) {
+                if (start == lo) return lo;
+                start = start - lo > 31u ? start - 31u : lo;  // the new window ends at the old start
+            } else {
+                return start + static_cast<uint32_t>(__ffs(bal) - 1);
+            }
+        }
+        return first_key_bin_le(bb);
+    };
     // First bin with CG >= t (the last bin when there is none), by every warp: a 64-way step over
     // the chunk ends, then a 2-way step within the chunk. CG is non-decreasing.
     static_assert(kABins == 2048, "two-level search over 32 x 64 bins");
@@ -1742,11 +1791,12 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     const uint32_t gseg = static_cast<uint32_t>(kGCap) / C;
     auto gather = [&](int bA, int bufA, int bBlo, int bBhi, int bufB, unsigned long long lowb) {
         // key intervals: bin bA, and bins bBlo..bBhi (empty when bBlo < 0); the four boundaries are
-        // computed at once by lane 0 of warps 0-3
-        if (tid < 128 && lane == 0) {
+        // computed at once by warps 0-3
+        if (tid < 128) {
             const int w = tid >> 5;
             const int bb = w == 0 ? bA : (w == 1 ? bA - 1 : (w == 2 ? bBhi : bBlo - 1));
-            ls->bc[4 + w] = (w < 2 || bBlo >= 0) ? first_key_bin_le(bb) : 0ull;
+            const unsigned long long kb = (w < 2 || bBlo >= 0) ? first_key_bin_le_warp(bb) : 0ull;
+            if (lane == 0) ls->bc[4 + w] = kb;
         }
         if (tid == 0) {
             ls->gfill[0] = 0u;

@@ -1898,9 +1898,11 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         }
         __syncthreads();
         unsigned long long before = 0ull, beforec = 0ull;
-        for (int w = 0; w < (tid >> 5); ++w) {
-            before += ls->red[w];
-            beforec += ls->red[kNW + w];
+#pragma unroll
+        for (int w = 0; w < kNW; ++w) {  // independent loads, predicated adds
+            const unsigned long long t = ls->red[w], tc = ls->red[kNW + w];
+            before += (w < (tid >> 5)) ? t : 0ull;
+            beforec += (w < (tid >> 5)) ? tc : 0ull;
         }
         unsigned long long run = before + inc - s;
         uint32_t runc = static_cast<uint32_t>(beforec) + incc - sc;

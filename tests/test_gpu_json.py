@@ -172,3 +172,62 @@ def test_constrained_decoding_produces_json_objects(setup):
             chk = np.zeros(32, np.uint8)
             assert B.json_feed(B.port(), chk, text) and (chk == fin[r]).all()
     assert done >= rows // 2, done
+
+
+def test_speculative_step_with_grammar_masks(setup):
+    """expand_drafts -> fill_masks -> sixi_smp_verify (masked target rows) -> advance by the
+    committed tokens: a drafted token that breaks the grammar is rejected at its position, and
+    every committed token keeps the answer a JSON prefix (the oracle checks each)."""
+    import sixi_smp as S
+
+    s = setup
+    torch = s["torch"]
+    rows_s, k = 8, 4
+    host, dev = _states(s, rows_s, 9)
+    rng = np.random.default_rng(10)
+    o = B.port()
+    drafts = np.zeros((rows_s, k), np.int32)
+    bad_at = np.full(rows_s, -1)
+    for r in range(rows_s):
+        st = host[r].copy()
+        for j in range(k):
+            m = B.json_fill_masks(o, s["v"], st[None])[0]
+            allowed = np.nonzero(np.unpackbits(m.view(np.uint8), bitorder="little")[:V])[0]
+            if r % 2 == 1 and j == 2 and bad_at[r] < 0:  # a draft the grammar refuses
+                refused = np.setdiff1d(np.arange(V), allowed)
+                drafts[r, j] = int(rng.choice(refused))
+                bad_at[r] = j
+            elif bad_at[r] < 0:
+                drafts[r, j] = int(rng.choice(allowed))
+                if drafts[r, j] != s["eos"]:
+                    B.json_feed(o, st, s["toks"][drafts[r, j]])
+            else:
+                drafts[r, j] = int(rng.integers(0, V))
+    d_drafts = torch.from_numpy(drafts).cuda()
+    row_states = s["g"].expand_drafts(dev, d_drafts)
+    masks = s["g"].fill_masks(row_states)
+    # target logits that favour each draft strongly, so that only the grammar rejects
+    tgt = torch.randn((rows_s * (k + 1), V), device="cuda")
+    for r in range(rows_s):
+        for j in range(k):
+            tgt[r * (k + 1) + j, int(drafts[r, j])] += 30.0
+    params = S.make_params(rows_s, temperature=0.0, flags=S.ROW_MASKED)
+    smp = S.Sampler(0, rows_s * (k + 1), V)
+    out = smp.verify(tgt, d_drafts, torch.from_numpy(params.view(np.uint8)).cuda(), masks=masks)
+    acc = out["accepted"].cpu().numpy()
+    ntok = out["n_tokens"].cpu().numpy()
+    toks = out["tokens"].cpu().numpy()
+    assert (out["status"].cpu().numpy() == 0).all()
+    for r in range(rows_s):
+        if bad_at[r] >= 0:
+            assert acc[r] <= bad_at[r], (r, acc[r], bad_at[r])
+    # commit and advance; the oracle must accept every committed token
+    st = s["g"].advance(dev, out["tokens"], n_tokens=out["n_tokens"])
+    assert (st.cpu().numpy() == 0).all()
+    for r in range(rows_s):
+        chk = host[r].copy()
+        for j in range(ntok[r]):
+            if toks[r, j] != s["eos"]:
+                assert B.json_feed(o, chk, s["toks"][toks[r, j]]), (r, j)
+        assert (chk[:6] == dev.cpu().numpy()[r, :6]).all()
+    smp.close()

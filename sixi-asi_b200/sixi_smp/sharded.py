@@ -4,9 +4,14 @@ vocabulary of every row (logits produced vocab-parallel). One step is
   stage 1   sixi_smp_shard_candidates on this rank's slice -> per-row best top_n and stats
   exchange  all-gather of both arrays (NCCL over NVLink on GPUs; rank-major layout)
   stage 2   sixi_smp_merge_shards, identical on every rank -> the token of every row
+  round 2   only for rows whose kept set or draw reaches past the gathered candidates (stage 2
+            reports SIXI_OUT_OF_BOUNDS, which can happen for top_k = 0 or top_k > top_n): their
+            slices are all-gathered, every rank rebuilds the full rows and samples them with
+            sixi_smp_sample
 
-so every rank ends with the same tokens, as sixi_smp_sample on the full rows would draw them (exact
-for top_k <= top_n; see the header for the rows that report SIXI_OUT_OF_BOUNDS).
+so every rank ends with the same tokens, as sixi_smp_sample on the full rows draws them, for every
+row. The flagged rows are the same on every rank (stage 2 is deterministic on identical data), so
+every rank makes the same collective calls.
 The stage functions are parameters so that the collective plumbing can be exercised on CPU
 ranks (gloo) with host restatements of the two stages.
 """
@@ -34,14 +39,43 @@ class ShardLayout:
         return r * base + min(r, extra)
 
 
+OUT_OF_BOUNDS = 2
+
+
+def _subset_csr(hist, hist_off, rows):
+    """The history lists of `rows` (device tensors): (tokens, offsets) of the subset."""
+    import torch
+
+    lens = (hist_off[1:] - hist_off[:-1])[rows]
+    off = torch.zeros(rows.numel() + 1, dtype=hist_off.dtype, device=hist_off.device)
+    off[1:] = torch.cumsum(lens, 0)
+    total = int(off[-1])
+    if total == 0:
+        return hist[:0], off
+    start = torch.repeat_interleave(hist_off[:-1][rows], lens)
+    within = torch.arange(total, device=hist.device, dtype=hist_off.dtype) - torch.repeat_interleave(off[:-1], lens)
+    return hist[start + within], off
+
+
 def sample_vocab_sharded(shard_logits, layout: ShardLayout, rank: int, params, *, top_n: int = 64,
                          masks=None, hist=None, hist_off=None, uniforms=None, step: int = 0,
-                         stage1: Callable | None = None, stage2: Callable | None = None, group=None,
-                         sampler=None, stream=None):
+                         stage1: Callable | None = None, stage2: Callable | None = None,
+                         full_rows: Callable | None = None, group=None, sampler=None, stream=None):
     """One sharded sampling step on this rank. `shard_logits` are this rank's columns
-    [n_rows, width(rank)] (a view into wider rows is fine). Returns (tokens, statuses)."""
+    [n_rows, width(rank)] (a view into wider rows is fine). Returns (tokens, statuses).
+    `full_rows(logits, rows)` samples rebuilt full rows `rows` (round 2); by default
+    sixi_smp_sample on this rank's sampler with the rows' parameters, masks, histories and
+    uniforms."""
     import torch
     import torch.distributed as dist
+
+    if full_rows is None:
+        def full_rows(full, rows):
+            p = params.view(-1, params.numel() // shard_logits.shape[0])[rows].contiguous()
+            m = None if masks is None else masks[rows].contiguous()
+            h, ho = (None, None) if hist is None else _subset_csr(hist, hist_off, rows)
+            uu = None if uniforms is None else uniforms[rows].contiguous()
+            return sampler.sample(full, p, masks=m, hist=h, hist_off=ho, uniforms=uu, step=step, stream=stream)
 
     if stage1 is None:
         def stage1(x, off, width):
@@ -59,4 +93,21 @@ def sample_vocab_sharded(shard_logits, layout: ShardLayout, rank: int, params, *
                           device=stats.device)
     dist.all_gather_into_tensor(g_cand, cand.contiguous(), group=group)
     dist.all_gather_into_tensor(g_stats, stats.contiguous(), group=group)
-    return stage2(g_cand.view((world,) + tuple(cand.shape)), g_stats.view((world,) + tuple(stats.shape)))
+    tok, sts = stage2(g_cand.view((world,) + tuple(cand.shape)), g_stats.view((world,) + tuple(stats.shape)))
+    # round 2: the rows stage 2 could not certify, sampled from their rebuilt full rows
+    rows = (sts == OUT_OF_BOUNDS).nonzero().flatten()
+    n_f = int(rows.numel())
+    if n_f:
+        wmax = max(layout.width(r) for r in range(world))
+        part = torch.zeros((n_f, wmax), dtype=shard_logits.dtype, device=shard_logits.device)
+        part[:, :layout.width(rank)] = shard_logits[rows.to(shard_logits.device)]
+        g_rows = torch.empty((world * n_f, wmax), dtype=part.dtype, device=part.device)
+        dist.all_gather_into_tensor(g_rows, part, group=group)
+        g_rows = g_rows.view(world, n_f, wmax)
+        full = torch.cat([g_rows[r, :, :layout.width(r)] for r in range(world)], dim=1).contiguous()
+        t2, s2 = full_rows(full, rows)
+        tok = tok.clone()
+        sts = sts.clone()
+        tok[rows] = t2.to(tok.device)
+        sts[rows] = s2.to(sts.device)
+    return tok, sts

@@ -1,8 +1,10 @@
 """The vocab-sharded step's collective plumbing on CPU ranks (gloo, world size 2): each rank holds
 half of the vocabulary of every row, runs a host restatement of stage 1 on its slice, the
 candidates and statistics are all-gathered by sixi_smp.sharded.sample_vocab_sharded, and each rank
-merges them with a host stage 2 (the oracle applied to the merged candidates). Both ranks must
-reach the oracle's tokens for the full rows (rows with top_k <= top_n, where the merge is exact).
+merges them with a host stage 2 (the oracle applied to the merged candidates). Rows whose top_k
+exceeds top_n (or is 0) cannot be certified from the candidates: the host stage 2 flags them
+SIXI_OUT_OF_BOUNDS, and the second exchange round rebuilds their full rows from all ranks' slices
+and samples them there. Both ranks must reach the oracle's tokens for every row.
 """
 
 from __future__ import annotations
@@ -27,7 +29,7 @@ def _rows():
     rng = np.random.default_rng(5)
     logits = rng.normal(0, 2.0, size=(N_ROWS, VOCAB)).astype(np.float32)
     params = S.make_params(N_ROWS, temperature=rng.choice([0.0, 0.7, 1.3], size=N_ROWS).astype(np.float32),
-                           top_k=rng.choice(np.array([1, 5, 16], np.int32), size=N_ROWS),
+                           top_k=rng.choice(np.array([1, 5, 16, 0, 40], np.int32), size=N_ROWS),
                            top_p=rng.choice(np.array([1.0, 0.8], np.float32), size=N_ROWS))
     u = rng.random(N_ROWS)
     return logits, params, u
@@ -74,8 +76,20 @@ def _stage2(g_cand, g_stats, params, u, port):
                     row[i] = gc[s, r, j, 0:1].view(np.float32)[0]
                     allowed[i] = True
         p = params[r:r + 1].copy()
+        k = int(p["top_k"][0])
+        if float(p["temperature"][0]) > 0 and (k == 0 or k > TOP_N):
+            st[r], tok[r] = 2, -1  # the candidates cannot certify this row: second round
+            continue
         p["flags"] = S.ROW_MASKED
         st[r], tok[r] = port.sample(row, p, None, W.pack_mask(allowed[None])[0], float(u[r]))
+    return torch.from_numpy(tok), torch.from_numpy(st)
+
+
+def _full_rows(full, rows, params, u, port):
+    import torch
+
+    rows = rows.numpy()
+    tok, st = port.sample_batch(full.numpy(), params[rows], None, None, None, u[rows])
     return torch.from_numpy(tok), torch.from_numpy(st)
 
 
@@ -102,7 +116,9 @@ def _worker(rank: int, port_no: int, errq):
         tok, st = sample_vocab_sharded(
             mine, lay, rank, params, top_n=TOP_N,
             stage1=lambda x, off, w: _stage1(x, off, w, params),
-            stage2=lambda gc, gs: _stage2(gc, gs, params, u, port))
+            stage2=lambda gc, gs: _stage2(gc, gs, params, u, port),
+            full_rows=lambda full, rows: _full_rows(full, rows, params, u, port))
+        assert ((params["top_k"] == 0) | (params["top_k"] > TOP_N)).sum() >= 2  # round 2 is exercised
         otok, ost = port.sample_batch(logits, params, None, None, None, u)
         assert np.array_equal(st.numpy(), ost), (st, ost)
         assert np.array_equal(tok.numpy(), otok), (rank, tok, otok)

@@ -1477,36 +1477,67 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         }
         __syncthreads();
     }
-    // list path: CTA 0 (softmax terms by all threads, then warp 0 with 8 candidates per lane,
-    // candidate order = lane-major); the other CTAs of such rows are finished
+    // list path: CTA 0 (the other CTAs of such rows are finished). Softmax terms by all threads;
+    // sums and the top-p decision by warp 0 with 8 candidates per lane (candidate order =
+    // lane-major); each division by a sum by its own thread (an fp64 division is a long dependent
+    // sequence: eight in a row per lane would dominate the phase).
+    const bool use_top_p = P->top_p > 0.0f && P->top_p < 1.0f;
     if (crank == 0 && path == 1) {
         const uint32_t n = fl_n;
         // fp64 softmax terms over the k candidates (core_execution.cpp:538-549)
         if (static_cast<uint32_t>(tid) < n) FP[tid] = exp(static_cast<double>(kval(comp_key(FL[tid]))) * invT - maxs);
         __syncthreads();
+        if (tid < 32) {
+            double lsum = 0.0;
+#pragma unroll
+            for (int j = 0; j < kPL; ++j) {
+                const uint32_t idx = lane * kPL + j;
+                lsum += idx < n ? FP[idx] : 0.0;
+            }
+            const double sum_exp = warp_sum_f64(lsum);
+            if (lane == 0) ls->bc[8] = static_cast<unsigned long long>(__double_as_longlong(sum_exp));
+        }
+        __syncthreads();
+        const double sum_exp = __longlong_as_double(static_cast<long long>(ls->bc[8]));
+        if (sum_exp > 0.0 && static_cast<uint32_t>(tid) < n) FP[tid] /= sum_exp;
+        __syncthreads();
+        if (use_top_p) {
+            // top-p: keep through the first index with cumulative >= top_p, renormalise
+            // (core_execution.cpp:551-575)
+            if (tid < 32) {
+                double pr[kPL];
+#pragma unroll
+                for (int j = 0; j < kPL; ++j) {
+                    const uint32_t idx = lane * kPL + j;
+                    pr[j] = idx < n ? FP[idx] : 0.0;
+                }
+                const uint32_t f = lane_first_cum_ge(pr, static_cast<double>(P->top_p), n, lane);
+                const uint32_t keep = (f == 0xFFFFFFFFu) ? n : f + 1u;
+                double ks = 0.0;
+#pragma unroll
+                for (int j = 0; j < kPL; ++j) ks += (lane * kPL + j < keep) ? pr[j] : 0.0;
+                const double r = warp_sum_f64(ks);
+                if (lane == 0) {
+                    ls->bc[8] = static_cast<unsigned long long>(__double_as_longlong(r));
+                    ls->bc[9] = keep;
+                }
+            }
+            __syncthreads();
+            const uint32_t keep = static_cast<uint32_t>(ls->bc[9]);
+            const double r = __longlong_as_double(static_cast<long long>(ls->bc[8]));
+            if (keep < n && r > 0.0 && static_cast<uint32_t>(tid) < n) FP[tid] /= r;
+            __syncthreads();
+        }
     }
     if (crank == 0 && path == 1 && tid < 32) {
         const uint32_t n = fl_n;
         double pr[kPL];
-        double lsum = 0.0;
 #pragma unroll
         for (int j = 0; j < kPL; ++j) {
             const uint32_t idx = lane * kPL + j;
             pr[j] = idx < n ? FP[idx] : 0.0;
-            lsum += pr[j];
         }
-        const double sum_exp = warp_sum_f64(lsum);
-        if (sum_exp > 0.0) {
-#pragma unroll
-            for (int j = 0; j < kPL; ++j) pr[j] /= sum_exp;
-        }
-        uint32_t keep = n;
-        if (P->top_p > 0.0f && P->top_p < 1.0f) {
-            // top-p: keep through the first index with cumulative >= top_p (core_execution.cpp:551-575)
-            const uint32_t f = lane_first_cum_ge(pr, static_cast<double>(P->top_p), n, lane);
-            keep = (f == 0xFFFFFFFFu) ? n : f + 1u;
-            if (keep < n) lane_renorm(pr, keep, lane);
-        }
+        uint32_t keep = use_top_p ? static_cast<uint32_t>(ls->bc[9]) : n;
         if (P->min_p > 0.0f) {
             // min-p extension: keep prob >= min_p * max prob, renormalise
             const double thr = static_cast<double>(P->min_p) * __shfl_sync(0xFFFFFFFFu, pr[0], 0);

@@ -102,6 +102,7 @@ struct LocalShared {
     unsigned int red32[kNW];
     unsigned long long bc[16];  // broadcast scalars
     double bcd[kNW];
+    unsigned long long cge[32];  // mass path: CG at the end of each 64-bin chunk
     unsigned int lcount;        // local list fill counter
     unsigned int gfill[2];      // this CTA's fill of its segment in each gather buffer
     unsigned int pad;
@@ -391,18 +392,17 @@ __device__ __forceinline__ unsigned long long block_select_small(const unsigned 
     if (valid && (pos & 1u) == 0u && pos + 1u == n) L[n] = 0ull;  // pad the list to an even length
     __syncthreads();
     // Entries are unique: rank = number of larger entries. `tpe` threads share one entry, each
-    // scanning a slice of the list two composites per load, and add their counts.
+    // scanning every tpe-th pair of the list (two composites per load; the group's loads are
+    // contiguous), and add their counts.
     const uint32_t tpe = n <= kNT / 8 ? 8u : (n <= kNT / 4 ? 4u : (n <= kNT / 2 ? 2u : 1u));
     uint32_t rank = 0;
     {
         const uint32_t me = static_cast<uint32_t>(tid) / tpe, part = static_cast<uint32_t>(tid) % tpe;
         const unsigned long long c = me < n ? L[me] : ~0ull;
         const uint32_t half = (n + 1u) / 2u;  // pairs
-        const uint32_t per = (half + tpe - 1u) / tpe;
-        const uint32_t j0 = part * per, j1 = (j0 + per < half) ? j0 + per : half;
         uint32_t r = 0;
         const ulonglong2* L2 = reinterpret_cast<const ulonglong2*>(L);
-        for (uint32_t j = j0; j < j1; ++j) {
+        for (uint32_t j = part; j < half; j += tpe) {
             const ulonglong2 v = L2[j];
             r += (v.x > c ? 1u : 0u) + (v.y > c ? 1u : 0u);
         }
@@ -424,7 +424,8 @@ __device__ __forceinline__ unsigned long long block_select_small(const unsigned 
     if (lane == 31) ls->red[w] = inc;
     __syncthreads();
     unsigned long long cum = inc;
-    for (int i = 0; i < w; ++i) cum += ls->red[i];
+#pragma unroll
+    for (int i = 0; i < kNW; ++i) cum += (i < w) ? ls->red[i] : 0ull;
     if (static_cast<uint32_t>(tid) < n && ws > 0ull && cum >= target && cum - ws < target) {
         ls->bc[3] = L[tid];  // the one entry whose prefix first reaches the target
         ls->bc[4] = cum;
@@ -771,8 +772,9 @@ static __device__ __noinline__ unsigned long long mass_histogram(const uint32_t*
     for (int m = 0; m < it8; ++m) {  // 8 keys per iteration: independent chains
         const int q = tid + m * kNT;
         if (q >= nq8) break;
-        const uint4 va = reinterpret_cast<const uint4*>(K)[2 * q];
-        const uint4 vb = (2 * q + 1 < nq) ? reinterpret_cast<const uint4*>(K)[2 * q + 1] : make_uint4(0u, 0u, 0u, 0u);
+        // groups q and q + nq8: a warp's 16-byte loads are contiguous (no bank conflicts)
+        const uint4 va = reinterpret_cast<const uint4*>(K)[q];
+        const uint4 vb = (q + nq8 < nq) ? reinterpret_cast<const uint4*>(K)[q + nq8] : make_uint4(0u, 0u, 0u, 0u);
         const uint32_t k8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -1804,16 +1806,18 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         }
         return first_key_bin_le(bb);
     };
-    // First bin with CG >= t (the last bin when there is none), by every warp: a 64-way step over
-    // the chunk ends, then a 2-way step within the chunk. CG is non-decreasing.
+    // First bin with CG >= t (the last bin when there is none), by every warp: a ballot over the
+    // ends of the 32 chunks of 64 bins (a contiguous copy), then over the chunk's two halves. CG is
+    // non-decreasing.
     static_assert(kABins == 2048, "two-level search over 32 x 64 bins");
     auto bin_of_target = [&](unsigned long long t) -> int {
-        const unsigned b1 = __ballot_sync(0xFFFFFFFFu, CG[lane * 64 + 63] >= t);
+        const unsigned b1 = __ballot_sync(0xFFFFFFFFu, ls->cge[lane] >= t);  // chunk ends, contiguous
         if (b1 == 0u) return kABins - 1;
         const int base = (__ffs(b1) - 1) * 64;
-        const unsigned b2 = __ballot_sync(0xFFFFFFFFu, CG[base + 2 * lane + 1] >= t);
-        const int j = base + 2 * (__ffs(b2) - 1);
-        return CG[j] >= t ? j : j + 1;
+        const unsigned lo = __ballot_sync(0xFFFFFFFFu, CG[base + lane] >= t);
+        if (lo != 0u) return base + __ffs(lo) - 1;
+        const unsigned hi = __ballot_sync(0xFFFFFFFFu, CG[base + 32 + lane] >= t);  // non-zero: CG[base + 63] >= t
+        return base + 32 + __ffs(hi) - 1;
     };
     // Pushes my entries of bin bA (and of bins bBlo..bBhi when bBlo >= 0) whose composite is >= lowb
     // into my segment of gather buffer bufA (bufB) in every CTA of the cluster, then publishes how many I
@@ -1853,9 +1857,11 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
 #pragma unroll 1
         for (int m = 0; m < it8; ++m) {  // warp-uniform trip count
             const int q = tid + m * kNT;
+            // groups q and q + nq8 (contiguous 16-byte loads across the warp); key i of the
+            // iteration is element 4 q + i (i < 4) or 4 (q + nq8) + i - 4
             uint4 va = make_uint4(0u, 0u, 0u, 0u), vb = make_uint4(0u, 0u, 0u, 0u);
-            if (2 * q < nq) va = reinterpret_cast<const uint4*>(K)[2 * q];
-            if (2 * q + 1 < nq) vb = reinterpret_cast<const uint4*>(K)[2 * q + 1];
+            if (q < nq8) va = reinterpret_cast<const uint4*>(K)[q];
+            if (q < nq8 && q + nq8 < nq) vb = reinterpret_cast<const uint4*>(K)[q + nq8];
             const uint32_t k8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
             uint32_t mA = 0u, mB = 0u;
 #pragma unroll
@@ -1867,7 +1873,8 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             if (use_lowb) {  // k-bound rows: drop entries below the composite bound
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    if (comp_of(k8[i], static_cast<uint32_t>(c0 + 8 * q + i)) < lowb) {
+                    const int e = i < 4 ? 4 * q + i : 4 * (q + nq8) + i - 4;
+                    if (comp_of(k8[i], static_cast<uint32_t>(c0 + e)) < lowb) {
                         mA &= ~(1u << i);
                         mB &= ~(1u << i);
                     }
@@ -1879,7 +1886,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             while (mk != 0u) {
                 const int i = __ffs(mk) - 1;
                 mk &= mk - 1u;
-                const int e = 8 * q + i;
+                const int e = i < 4 ? 4 * q + i : 4 * (q + nq8) + i - 4;
                 const unsigned long long cp = comp_of(K[e], static_cast<uint32_t>(c0 + e));
                 if ((mA >> i) & 1u) {
                     if (pA < gseg) {
@@ -1906,20 +1913,37 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         }
     };
 
-    // every CTA assembles the same global cumulative histograms (CG/CGC overwrite H/HC)
+    // every CTA assembles the same global cumulative histograms (CG/CGC overwrite H/HC). Each
+    // thread owns 4 consecutive bins and moves them with 16-byte accesses (4-byte or 8-byte ones at
+    // a 16- or 32-byte thread stride would conflict on the shared-memory banks).
     {
         constexpr int PER = kABins / kNT;
+        static_assert(PER == 4, "16-byte accesses of 4 bins");
         unsigned long long v[PER];
         uint32_t vc[PER];
         unsigned long long s = 0ull;
         uint32_t sc = 0;
+        {
+            const uint32_t i0 = tid * PER;  // the PER bins lie in one segment (seg % PER == 0)
+            const ulonglong2* rs = reinterpret_cast<const ulonglong2*>(cluster.map_shared_rank(R, i0 / lay.seg) +
+                                                                        i0 % lay.seg);
+            const ulonglong2 v01 = rs[0], v23 = rs[1];
+            v[0] = v01.x;
+            v[1] = v01.y;
+            v[2] = v23.x;
+            v[3] = v23.y;
+            uint4 c4 = make_uint4(0u, 0u, 0u, 0u);
+            if (need_counts)
+                c4 = *reinterpret_cast<const uint4*>(cluster.map_shared_rank(RC, i0 / lay.seg) + i0 % lay.seg);
+            vc[0] = c4.x;
+            vc[1] = c4.y;
+            vc[2] = c4.z;
+            vc[3] = c4.w;
 #pragma unroll
-        for (int q = 0; q < PER; ++q) {
-            const uint32_t i = tid * PER + q;
-            v[q] = cluster.map_shared_rank(R, i / lay.seg)[i % lay.seg];
-            vc[q] = need_counts ? cluster.map_shared_rank(RC, i / lay.seg)[i % lay.seg] : 0u;
-            s += v[q];
-            sc += vc[q];
+            for (int q = 0; q < PER; ++q) {
+                s += v[q];
+                sc += vc[q];
+            }
         }
         const unsigned long long inc = warp_incl_u64(s);
         const uint32_t incc = warp_incl_u32(sc);
@@ -1937,13 +1961,20 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         }
         unsigned long long run = before + inc - s;
         uint32_t runc = static_cast<uint32_t>(beforec) + incc - sc;
+        unsigned long long p[PER];
+        uint32_t pc[PER];
 #pragma unroll
         for (int q = 0; q < PER; ++q) {
             run += v[q];
             runc += vc[q];
-            CG[tid * PER + q] = run;
-            CGC[tid * PER + q] = runc;
+            p[q] = run;
+            pc[q] = runc;
         }
+        ulonglong2* cg2 = reinterpret_cast<ulonglong2*>(CG + tid * PER);
+        cg2[0] = make_ulonglong2(p[0], p[1]);
+        cg2[1] = make_ulonglong2(p[2], p[3]);
+        *reinterpret_cast<uint4*>(CGC + tid * PER) = make_uint4(pc[0], pc[1], pc[2], pc[3]);
+        if ((tid & 15) == 15) ls->cge[tid >> 4] = p[3];  // CG[64 w + 63]: the ends of the 64-bin chunks
         __syncthreads();
     }
 

@@ -328,15 +328,23 @@ __device__ __forceinline__ unsigned long long block_select_tiny(const unsigned l
             if (e < lowb || e == excl) e = 0ull;  // 0 sorts below every entry and weighs nothing
         }
         const unsigned long long w = e ? (weighted ? weight_of(kval(comp_key(e)), wc) : 1ull) : 0ull;
-        uint32_t rank = 0;  // unique: equal zeros are ordered by lane
-#pragma unroll 8
-        for (int j = 0; j < 32; ++j) {
-            const unsigned long long o = __shfl_sync(0xFFFFFFFFu, e, j);
-            rank += (o > e || (o == e && j < lane)) ? 1u : 0u;
+        // rank among the first `n` lanes (the others hold 0 and weigh nothing): the entries get
+        // distinct ranks below n; zeros may share ranks, which only ever write zeros
+        uint32_t n = 0;
+        for (uint32_t qq = 0; qq < C; ++qq) n += cnt[qq];
+        uint32_t rank = 0;
+        for (uint32_t j = 0; j < n; ++j) {
+            const unsigned long long o = __shfl_sync(0xFFFFFFFFu, e, static_cast<int>(j));
+            rank += (o > e || (o == e && static_cast<int>(j) < lane)) ? 1u : 0u;
         }
         unsigned long long* S = ls->red;  // 64 of its words; the other warps wait at the barrier
-        S[rank] = e;
-        S[32 + rank] = w;
+        S[lane] = 0ull;
+        S[32 + lane] = 0ull;
+        __syncwarp();
+        if (rank < 32u) {
+            S[rank] = e;
+            S[32 + rank] = w;
+        }
         __syncwarp();
         const unsigned long long es = S[lane], ws = S[32 + lane];
         const unsigned long long cum = warp_incl_u64(ws);
@@ -402,7 +410,13 @@ __device__ __forceinline__ unsigned long long block_select_small(const unsigned 
         const uint32_t half = (n + 1u) / 2u;  // pairs
         uint32_t r = 0;
         const ulonglong2* L2 = reinterpret_cast<const ulonglong2*>(L);
-        for (uint32_t j = part; j < half; j += tpe) {
+        uint32_t j = part;
+        for (; j + 3u * tpe < half; j += 4u * tpe) {  // four loads in flight
+            const ulonglong2 v0 = L2[j], v1 = L2[j + tpe], v2 = L2[j + 2u * tpe], v3 = L2[j + 3u * tpe];
+            r += (v0.x > c ? 1u : 0u) + (v0.y > c ? 1u : 0u) + (v1.x > c ? 1u : 0u) + (v1.y > c ? 1u : 0u) +
+                 (v2.x > c ? 1u : 0u) + (v2.y > c ? 1u : 0u) + (v3.x > c ? 1u : 0u) + (v3.y > c ? 1u : 0u);
+        }
+        for (; j < half; j += tpe) {
             const ulonglong2 v = L2[j];
             r += (v.x > c ? 1u : 0u) + (v.y > c ? 1u : 0u);
         }
@@ -455,6 +469,42 @@ __device__ __forceinline__ unsigned long long block_select(const unsigned long l
     {
         uint32_t total = 0;
         for (uint32_t q = 0; q < C; ++q) total += cnt[q];
+        if (total <= 4u) {
+            // a handful of entries: every thread evaluates them (the same broadcast reads), so no
+            // exchange and no barrier is needed
+            unsigned long long e4[4] = {0ull, 0ull, 0ull, 0ull};
+            uint32_t m = 0;
+            for (uint32_t q = 0; q < C; ++q) {
+                for (uint32_t i = 0; i < cnt[q] && m < 4u; ++i) {
+                    const unsigned long long e = g[q * seg + i];
+                    e4[m++] = (e >= lowb && e != excl) ? e : 0ull;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 3; ++i) {  // descending (a 4-element bubble network)
+#pragma unroll
+                for (int j = 0; j < 3 - i; ++j) {
+                    if (e4[j] < e4[j + 1]) {
+                        const unsigned long long t = e4[j];
+                        e4[j] = e4[j + 1];
+                        e4[j + 1] = t;
+                    }
+                }
+            }
+            unsigned long long cum = 0ull, sel = 0ull, through = 0ull;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const unsigned long long w =
+                    e4[i] ? (weighted ? weight_of(kval(comp_key(e4[i])), wc) : 1ull) : 0ull;
+                cum += w;
+                if (sel == 0ull && w > 0ull && cum >= target) {
+                    sel = e4[i];
+                    through = cum;
+                }
+            }
+            *cum_through = through;
+            return sel;
+        }
         if (total <= 32u)
             return block_select_tiny(g, cnt, C, seg, target, wc, weighted, lowb, excl, ls, cum_through);
         if (total <= kSmallSelect)

@@ -1898,6 +1898,14 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         // tested only when it is set (k-bound rows). These loops are bound by the integer pipe.
         const uint32_t wA = static_cast<uint32_t>(khiA1 - kloA);
         const uint32_t wB = bBlo >= 0 ? static_cast<uint32_t>(khiB1 - kloB) : 0u;  // empty set B
+        // When the two sets touch (or B is empty), one test per key against their union screens
+        // the keys; when they are apart, the screen is the pair of exact tests (a screen over the
+        // gap would admit its keys and run the per-hit path for nothing).
+        const bool touch = wB == 0u || (static_cast<unsigned long long>(kloB) <= khiA1 &&
+                                        static_cast<unsigned long long>(kloA) <= khiB1);
+        const uint32_t kloU = (wB != 0u && kloB < kloA) ? kloB : kloA;
+        const unsigned long long khiU1 = (wB != 0u && khiB1 > khiA1) ? khiB1 : khiA1;
+        const uint32_t wU = static_cast<uint32_t>(khiU1 - kloU);
         const bool use_lowb = lowb != 0ull;
         // One pass of 8 keys per iteration: per key only the interval tests; a warp reserves slots
         // (local counter) only on the rare iterations where one of its lanes holds a match. Keys
@@ -1913,6 +1921,15 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             if (q < nq8) va = reinterpret_cast<const uint4*>(K)[q];
             if (q < nq8 && q + nq8 < nq) vb = reinterpret_cast<const uint4*>(K)[q + nq8];
             const uint32_t k8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+            bool hit = false;
+            if (touch) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) hit |= k8[i] - kloU < wU;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) hit |= (k8[i] - kloA < wA) | (k8[i] - kloB < wB);
+            }
+            if (__ballot_sync(0xFFFFFFFFu, hit) == 0u) continue;
             uint32_t mA = 0u, mB = 0u;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {

@@ -2274,7 +2274,9 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 __syncthreads();
             } else if (rf.phase == 2) {
                 // ties of the resolved key: find the owner CTA of the crossing entry (id order)
-                const unsigned long long w = rf.cmode ? 1ull : weight_of(kval(rf.prefix), wc);
+                // w: the selection unit of one tie (1 when counting); wk: its weight, for the mass
+                const unsigned long long wk = weight_of(kval(rf.prefix), wc);
+                const unsigned long long w = rf.cmode ? 1ull : wk;
                 const unsigned long long done_sel = rf.cmode ? rf.above_c : rf.above_w;
                 if (w == 0ull || rf.t <= done_sel) {
                     st.err = 8;
@@ -2294,8 +2296,8 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                         st.err = 9;
                     } else {
                         rf.above_c += idx;  // entries before the crossing tie
-                        rf.above_w += idx * w;
-                        rf.tie_w = w;
+                        rf.above_w += idx * wk;
+                        rf.tie_w = wk;
                         if (owner == static_cast<int>(crank)) {
                             const unsigned long long li = idx - before;
                             unsigned long long taken = 0ull;

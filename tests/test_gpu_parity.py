@@ -277,3 +277,43 @@ def test_full_distribution(port, vocab):
                 assert np.array_equal(got[r], want), (dt, r)
             else:
                 np.testing.assert_allclose(got[r], want, rtol=1e-6, atol=1e-30, err_msg=f"{dt} row {r}")
+
+
+@pytest.mark.parametrize("seed", [41, 42, 43])
+def test_full_vocab_mass_path_sweep(port, seed):
+    """Full-vocabulary rows that mostly take the mass path (top_k = 0 or above the list limit),
+    with ties, heavy tails, masks, min-p and penalties: the exact selections over one to hundreds
+    of entries, the bin-boundary search and the gather pass are all exercised."""
+    vocab = W.QWEN_VOCAB
+    rng = np.random.default_rng(seed)
+    rows = 32
+    kind = rng.integers(0, 3, size=rows)
+    logits = np.empty((rows, vocab), np.float32)
+    for r in range(rows):
+        if kind[r] == 0:
+            logits[r] = rng.normal(0.0, 2.5, size=vocab)
+        elif kind[r] == 1:  # heavy ties: bins far fuller than a gather segment
+            logits[r] = rng.integers(-4, 5, size=vocab)
+        else:
+            logits[r] = rng.standard_cauchy(size=vocab) * 0.7
+    W.boost_rows(rng, logits, n=8, by=6.0)
+    t = rng.choice(np.array([0.0, 0.35, 0.7, 1.0, 1.3, 3.0], np.float32), size=rows)
+    topk = rng.choice(np.array([0, 0, 0, 300, 1000, 40], np.int32), size=rows)
+    topp = rng.choice(np.array([1.0, 0.99, 0.9, 0.75, 0.3], np.float32), size=rows)
+    minp = np.where(rng.random(rows) < 0.25, rng.choice(np.array([0.001, 0.05], np.float32), size=rows), 0.0)
+    params = S.make_params(rows, temperature=t, top_k=topk, top_p=topp, min_p=minp,
+                           repetition_penalty=rng.choice(np.array([1.0, 1.2], np.float32), size=rows),
+                           presence_penalty=np.where(rng.random(rows) < 0.3, 0.4, 0.0).astype(np.float32))
+    allowed = np.stack([W.run_mask(rng, vocab, float(rng.choice([0.02, 0.5])), mean_run=64.0)
+                        for _ in range(rows)])
+    masks = W.pack_mask(allowed)
+    params["flags"] = np.where(rng.random(rows) < 0.3, S.ROW_MASKED, 0)
+    lens = rng.integers(0, 2048, size=rows)
+    off = np.zeros(rows + 1, dtype=np.int64)
+    off[1:] = np.cumsum(lens)
+    hist = rng.integers(0, vocab, size=int(off[-1]), dtype=np.int32)
+    d = dict(logits=logits, params=params, masks=masks, hist=hist, hist_off=off)
+    u = rng.random(rows)
+    tok, st = run_sample(d, u)
+    check_against_oracle(port, d, u, tok, st)
+

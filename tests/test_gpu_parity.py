@@ -317,3 +317,24 @@ def test_full_vocab_mass_path_sweep(port, seed):
     tok, st = run_sample(d, u)
     check_against_oracle(port, d, u, tok, st)
 
+
+
+@pytest.mark.parametrize("seed", [51, 52])
+def test_kbound_inside_overfull_tie_bin(port, seed):
+    """Integer-valued logits put thousands of equal keys in one bin, so the k-th entry of a
+    top_k above the list limit is found by the key-digit refine pass in counting mode. The kept
+    mass that follows must weigh each tie by its own weight, not by one, or every later target
+    (top-p, min-p, the draw) moves."""
+    vocab = W.QWEN_VOCAB
+    rng = np.random.default_rng(seed)
+    rows = 24
+    logits = rng.integers(-3, 4, size=(rows, vocab)).astype(np.float32)
+    W.boost_rows(rng, logits, n=4, by=3.0)
+    t = rng.choice(np.array([0.5, 1.3, 3.0], np.float32), size=rows)
+    topk = rng.choice(np.array([257, 300, 1000, 5000], np.int32), size=rows)
+    topp = rng.choice(np.array([1.0, 0.9, 0.6], np.float32), size=rows)
+    params = S.make_params(rows, temperature=t, top_k=topk, top_p=topp)
+    d = dict(logits=logits, params=params, masks=None, hist=None, hist_off=None)
+    u = rng.random(rows)
+    tok, st = run_sample(d, u)
+    check_against_oracle(port, d, u, tok, st)

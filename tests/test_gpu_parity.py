@@ -279,11 +279,11 @@ def test_full_distribution(port, vocab):
                 np.testing.assert_allclose(got[r], want, rtol=1e-6, atol=1e-30, err_msg=f"{dt} row {r}")
 
 
-@pytest.mark.parametrize("seed", [41, 42, 43])
-def test_full_vocab_mass_path_sweep(port, seed):
-    """Full-vocabulary rows that mostly take the mass path (top_k = 0 or above the list limit),
-    with ties, heavy tails, masks, min-p and penalties: the exact selections over one to hundreds
-    of entries, the bin-boundary search and the gather pass are all exercised."""
+def mass_sweep_case(seed: int, dtype: str = "f32") -> dict:
+    """32 full-vocabulary rows that mostly take the mass path (top_k = 0 or above the list limit):
+    normal rows, integer-valued rows (heavy ties: bins far fuller than a gather segment) and
+    Cauchy rows, each with 8 ids boosted by +6, a temperature / top-k / top-p / min-p mix,
+    penalties, histories and, for 30 % of the rows, a run-structured mask."""
     vocab = W.QWEN_VOCAB
     rng = np.random.default_rng(seed)
     rows = 32
@@ -292,7 +292,7 @@ def test_full_vocab_mass_path_sweep(port, seed):
     for r in range(rows):
         if kind[r] == 0:
             logits[r] = rng.normal(0.0, 2.5, size=vocab)
-        elif kind[r] == 1:  # heavy ties: bins far fuller than a gather segment
+        elif kind[r] == 1:
             logits[r] = rng.integers(-4, 5, size=vocab)
         else:
             logits[r] = rng.standard_cauchy(size=vocab) * 0.7
@@ -312,12 +312,52 @@ def test_full_vocab_mass_path_sweep(port, seed):
     off = np.zeros(rows + 1, dtype=np.int64)
     off[1:] = np.cumsum(lens)
     hist = rng.integers(0, vocab, size=int(off[-1]), dtype=np.int32)
-    d = dict(logits=logits, params=params, masks=masks, hist=hist, hist_off=off)
-    u = rng.random(rows)
-    tok, st = run_sample(d, u)
-    check_against_oracle(port, d, u, tok, st)
+    if dtype == "bf16":
+        logits = W.f32_to_bf16_bits(logits)
+    d = dict(logits=logits, params=params, masks=masks, hist=hist, hist_off=off, vocab=vocab)
+    d["uniforms"] = rng.random(rows)
+    return d
 
 
+@pytest.mark.parametrize("seed", [41, 42, 43])
+def test_full_vocab_mass_path_sweep(port, seed):
+    """The exact selections over one to hundreds of entries, the bin-boundary search, the gather
+    pass and the key-digit refine pass, on full-vocabulary rows."""
+    d = mass_sweep_case(seed)
+    tok, st = run_sample(d, d["uniforms"])
+    check_against_oracle(port, d, d["uniforms"], tok, st)
+
+
+@pytest.mark.parametrize("seed", [44, 45])
+def test_full_vocab_mass_path_sweep_bf16(port, seed):
+    d = mass_sweep_case(seed, "bf16")
+    tok, st = run_sample(d, d["uniforms"])
+    check_against_oracle(port, d, d["uniforms"], tok, st)
+
+
+@pytest.mark.parametrize("seed", [46, 47])
+def test_candidates_full_vocab_mass_path(port, seed):
+    """Candidate lists (ids, order, probabilities and the kept count) of the sweep's rows, the
+    greedy rows given a temperature."""
+    d = mass_sweep_case(seed)
+    d["params"]["temperature"] = np.where(d["params"]["temperature"] <= 0, 0.8, d["params"]["temperature"])
+    rows = d["logits"].shape[0]
+    smp = sampler(d["vocab"])
+    ids, probs, cnt, st = smp.candidates(dev(d["logits"]), dev(d["params"]), max_out=256, masks=dev(d["masks"]),
+                                         hist=dev(d["hist"]), hist_off=dev(d["hist_off"]))
+    ids, probs, cnt, st = (t.cpu().numpy() for t in (ids, probs, cnt, st))
+    masks = d["masks"]
+    for r in range(rows):
+        h = d["hist"][d["hist_off"][r]:d["hist_off"][r + 1]]
+        m_r = masks[r] if d["params"]["flags"][r] & S.ROW_MASKED else None
+        ost, oids, oprobs, on = port.candidates(d["logits"][r], d["params"][r:r + 1], h, mask=m_r)
+        assert st[r] == ost, (r, st[r], ost)
+        if ost != 0:
+            continue
+        assert cnt[r] == on, (r, cnt[r], on, d["params"][r])
+        m = min(on, 256)
+        assert np.array_equal(ids[r, :m], oids[:m]), r
+        np.testing.assert_allclose(probs[r, :m], oprobs[:m], rtol=PROB_RTOL, atol=1e-300)
 
 @pytest.mark.parametrize("seed", [51, 52])
 def test_kbound_inside_overfull_tie_bin(port, seed):

@@ -148,3 +148,29 @@ def test_verify_draft_logits_equals_stored_q(port, dtype):
                     hist=d["hist"], hist_off=d["hist_off"], uniforms=d["uniforms"])
     for kk in KEYS:
         assert np.array_equal(fused[kk], o[kk]), f"{kk}: gpu={fused[kk]} oracle={o[kk]}"
+
+
+@pytest.mark.parametrize("dense", [True, False])
+@pytest.mark.parametrize("seed", [61, 62])
+def test_verify_mass_path_with_heavy_ties(port, dense, seed):
+    """Integer-valued target rows (tens of thousands of equal keys per value) with top_k = 0 or
+    above the list limit: the p of each draft, the residual draw that leaves the draft out (the
+    one-hot case: an excluded composite inside a bin that must be refined by key digits) and the
+    dense residual over all ids run on the mass path, against the oracle bit for bit."""
+    streams, k = 12, 4
+    d = W.config4(streams=streams, k=k, seed=seed, stochastic=True, masked=True)
+    rng = np.random.default_rng(seed + 1000)
+    tgt = W.bf16_bits_to_f32(d["target_bits"])
+    tgt = np.clip(np.rint(tgt / 1.5), -4, 4).astype(np.float32)
+    for s in range(streams):  # drafts on a well-populated value, on the top value, or far above it
+        for i in range(k):
+            tgt[s * (k + 1) + i, d["drafts"][s, i]] = float(rng.choice([2.0, 4.0, 16.0]))
+    d["target_bits"] = W.f32_to_bf16_bits(tgt)
+    p = d["params"]
+    p["top_k"] = rng.choice(np.array([0, 0, 300, 1000, 40], np.int32), size=streams)
+    p["top_p"] = rng.choice(np.array([1.0, 0.95, 0.8], np.float32), size=streams)
+    p["temperature"] = rng.choice(np.array([0.5, 1.0, 2.0], np.float32), size=streams)
+    p["min_p"] = np.where(rng.random(streams) < 0.25, np.float32(0.01), np.float32(0.0))
+    g = check(port, d, dense)
+    assert (g["status"] == 0).all()
+    assert g["accepted"].min() < k  # some rejections, so residual draws run

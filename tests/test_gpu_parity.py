@@ -230,6 +230,23 @@ def test_philox_matches_host():
     assert vals == [p.philox_uniform(123, 7, s) for s in range(4)]
 
 
+@pytest.mark.parametrize("vocab", [262_144, 600_000])
+def test_wide_clusters_heavy_ties(port, vocab):
+    """Clusters of 8 and 16 CTAs per row on integer-valued rows: the key-digit refine pass and the
+    owner search of a crossing tie run over more CTAs."""
+    rng = np.random.default_rng(vocab + 5)
+    rows = 8
+    logits = rng.integers(-3, 4, size=(rows, vocab)).astype(np.float32)
+    W.boost_rows(rng, logits, n=4, by=3.0)
+    params = S.make_params(rows, temperature=rng.choice(np.array([0.5, 1.0, 3.0], np.float32), size=rows),
+                           top_k=np.array([0, 0, 300, 1000, 5000, 0, 257, 0], np.int32),
+                           top_p=rng.choice(np.array([1.0, 0.9, 0.6], np.float32), size=rows))
+    d = dict(logits=logits, params=params, masks=None, hist=None, hist_off=None, vocab=vocab)
+    u = rng.random(rows)
+    tok, st = run_sample(d, u)
+    check_against_oracle(port, d, u, tok, st)
+
+
 @pytest.mark.parametrize("vocab", [200_003, 262_144, 600_000])
 def test_large_vocab_wide_clusters(port, vocab):
     """Vocabularies that need clusters of 8 (262,144) and 16 (600,000) CTAs per row."""

@@ -139,3 +139,27 @@ def test_sharded_statuses(port):
     assert st[1] == 16 and st[2] == 1 and st[0] == 0 and st[3] == 0
     check(port, d, tok, st, u, 16)
     smp.close()
+
+
+@pytest.mark.parametrize("n_shards", [2, 8])
+def test_sharded_heavy_ties_across_shards(port, n_shards):
+    """Integer-valued rows: every shard's best top_n are equal keys, so the merge must order the
+    gathered candidates by id across shards, exactly as the full row orders them."""
+    rng = np.random.default_rng(900 + n_shards)
+    vocab, n = W.QWEN_VOCAB, 16
+    logits = rng.integers(-4, 5, size=(n, vocab)).astype(np.float32)
+    logits[: n // 2] = np.minimum(logits[: n // 2], 2.0)  # half the rows: a third of the ids tie at the top
+    params = S.make_params(n, temperature=rng.choice(np.array([0.0, 0.5, 1.0, 2.0], np.float32), size=n),
+                           top_k=rng.choice(np.array([1, 5, 20, 64, 0], np.int32), size=n),
+                           top_p=rng.choice(np.array([1.0, 0.9, 0.5], np.float32), size=n),
+                           repetition_penalty=np.float32(1.2))
+    lens = rng.integers(0, 1024, size=n)
+    off = np.zeros(n + 1, dtype=np.int64)
+    off[1:] = np.cumsum(lens)
+    d = dict(logits=logits, params=params, masks=None, hist=rng.integers(0, vocab, size=int(off[-1]), dtype=np.int32),
+             hist_off=off)
+    u = rng.random(n)
+    smp = S.Sampler(0, 64, vocab)
+    tok, st = run_sharded(smp, d, n_shards, 64, u)
+    check(port, d, tok, st, u, 64)
+    smp.close()

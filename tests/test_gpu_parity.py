@@ -395,3 +395,31 @@ def test_kbound_inside_overfull_tie_bin(port, seed):
     u = rng.random(rows)
     tok, st = run_sample(d, u)
     check_against_oracle(port, d, u, tok, st)
+
+
+@pytest.mark.parametrize("seed", [71, 72])
+def test_full_vocab_extreme_parameters(port, seed):
+    """Temperatures from 1e-3 (every weight but the largest rounds to zero) to 1,000 (every weight
+    close to the largest), top_p and min_p at their limits, top_k at 1, just above the list limit
+    and at the vocabulary size, on normal, integer-valued and Cauchy rows."""
+    vocab = W.QWEN_VOCAB
+    rng = np.random.default_rng(seed)
+    rows = 32
+    logits = np.empty((rows, vocab), np.float32)
+    for r in range(rows):
+        if r % 3 == 0:
+            logits[r] = rng.normal(0.0, 2.5, size=vocab)
+        elif r % 3 == 1:
+            logits[r] = rng.integers(-2, 3, size=vocab)
+        else:
+            logits[r] = rng.standard_cauchy(size=vocab) * 3.0
+    t = rng.choice(np.array([1e-3, 0.05, 20.0, 1000.0], np.float32), size=rows)
+    topk = rng.choice(np.array([0, 0, 1, 257, vocab - 1, vocab], np.int32), size=rows)
+    topp = rng.choice(np.array([1.0, 0.999999, 1e-6, 0.5], np.float32), size=rows)
+    minp = rng.choice(np.array([0.0, 0.0, 1e-9, 0.999], np.float32), size=rows)
+    params = S.make_params(rows, temperature=t, top_k=topk, top_p=topp, min_p=minp)
+    d = dict(logits=logits, params=params, masks=None, hist=None, hist_off=None)
+    u = rng.random(rows)
+    u[:4] = [0.0, 1.0 - 2.0 ** -53, 0.5, 1e-12]  # the ends of the unit interval
+    tok, st = run_sample(d, u)
+    check_against_oracle(port, d, u, tok, st)

@@ -174,3 +174,27 @@ def test_verify_mass_path_with_heavy_ties(port, dense, seed):
     g = check(port, d, dense)
     assert (g["status"] == 0).all()
     assert g["accepted"].min() < k  # some rejections, so residual draws run
+
+
+def test_verify_extreme_parameters(port):
+    """Temperatures of 1e-3 and 1,000, top_p at its limits, drafts whose q is exactly zero (the
+    accept ratio's 1e-12 floor) or one, and uniforms at the ends of the unit interval."""
+    streams, k = 12, 4
+    d = W.config4(streams=streams, k=k, seed=81, stochastic=True, masked=False)
+    rng = np.random.default_rng(82)
+    p = d["params"]
+    p["temperature"] = rng.choice(np.array([1e-3, 0.05, 20.0, 1000.0], np.float32), size=streams)
+    p["top_k"] = rng.choice(np.array([0, 1, 257, 40], np.int32), size=streams)
+    p["top_p"] = rng.choice(np.array([1.0, 0.999999, 1e-6], np.float32), size=streams)
+    q = d["q"].reshape(streams, k, -1)
+    for s in range(0, streams, 3):
+        q[s, 0, d["drafts"][s, 0]] = 0.0  # a draft the drafter gave no mass
+    for s in range(1, streams, 3):
+        q[s, 1] = 0.0
+        q[s, 1, d["drafts"][s, 1]] = 1.0  # a one-hot draft distribution, stored densely
+    d["q"] = q.reshape(streams * k, -1)
+    u = d["uniforms"]
+    u[:3, 0] = [0.0, 1.0 - 2.0 ** -53, 1e-12]
+    for dense in (True, False):
+        g = check(port, d, dense)
+        assert (g["status"] == 0).all()

@@ -826,6 +826,7 @@ static __device__ __noinline__ unsigned long long mass_histogram(const uint32_t*
         const uint4 va = reinterpret_cast<const uint4*>(K)[q];
         const uint4 vb = (q + nq8 < nq) ? reinterpret_cast<const uint4*>(K)[q + nq8] : make_uint4(0u, 0u, 0u, 0u);
         const uint32_t k8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+        uint32_t am8[8], ah8[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const uint32_t k = k8[i];
@@ -834,18 +835,17 @@ static __device__ __noinline__ unsigned long long mass_histogram(const uint32_t*
             const uint32_t b = static_cast<uint32_t>(abin_of(x, wc));
             const uint32_t c = static_cast<uint32_t>(w) & 0xFFFFu;
             const uint32_t bm = static_cast<uint32_t>(w) >> 16;
-            const uint32_t am = static_cast<uint32_t>(w >> 32);
             const uint32_t alo = lo_base + 4u * b, ahi = hi_base + 4u * b;
+            am8[i] = k != 0u ? static_cast<uint32_t>(w >> 32) : 0u;
+            ah8[i] = ahi;
             asm volatile(
                 "{\n\t.reg .pred pk, p;\n\t"
                 "setp.ne.u32 pk, %0, 0;\n\t"
                 "setp.ne.and.u32 p, %3, 0, pk;\n\t"
                 "@p red.shared.add.u32 [%1], %3;\n\t"
                 "setp.ne.and.u32 p, %4, 0, pk;\n\t"
-                "@p red.shared.add.u32 [%2], %4;\n\t"
-                "setp.ne.and.u32 p, %5, 0, pk;\n\t"
-                "@p red.shared.add.u32 [%2+8192], %5;\n\t}" ::"r"(k),
-                "r"(alo), "r"(ahi), "r"(c), "r"(bm), "r"(am)
+                "@p red.shared.add.u32 [%2], %4;\n\t}" ::"r"(k),
+                "r"(alo), "r"(ahi), "r"(c), "r"(bm)
                 : "memory");
             if (need_counts) {
                 asm volatile(
@@ -856,6 +856,20 @@ static __device__ __noinline__ unsigned long long mass_histogram(const uint32_t*
                     : "memory");
             }
             if (use_minp) wp += (k != 0u && x >= x_minp) ? w : 0ull;
+        }
+        // The high parts are non-zero only for keys within 2^-11 of the row's largest weight, so
+        // in nearly every warp all eight are zero: one vote skips their reductions.
+        const uint32_t any_hi = am8[0] | am8[1] | am8[2] | am8[3] | am8[4] | am8[5] | am8[6] | am8[7];
+        if (__any_sync(__activemask(), any_hi != 0u)) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                asm volatile(
+                    "{\n\t.reg .pred p;\n\t"
+                    "setp.ne.u32 p, %1, 0;\n\t"
+                    "@p red.shared.add.u32 [%0+8192], %1;\n\t}" ::"r"(ah8[i]),
+                    "r"(am8[i])
+                    : "memory");
+            }
         }
     }
     return wp;

@@ -727,7 +727,8 @@ struct GatherReq {  // the bins a round gathers: bin bA, and bins bBlo..bBhi (bB
     unsigned long long lowb;
 };
 
-constexpr int kPreBins = 4;  // widest bin range gathered ahead of time for the draw
+constexpr int kPreBins = 4;  // bin ranges this narrow are gathered ahead of time for the draw; wider
+                             // ones when their key count is bounded by the gather segment
 
 struct LState {
     int stage;
@@ -1888,6 +1889,16 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     // have (a count above the segment size marks the bin overfull). Slots come from a local
     // counter, so the remote traffic is plain stores.
     const uint32_t gseg = static_cast<uint32_t>(kGCap) / C;
+    // True when bins lo..hi provably hold at most gseg keys, so that gathering them cannot overflow
+    // any CTA's segment. Every key of bin b weighs at least 2^(43 - (b + 1) / bin_scale), less the
+    // errors of the exponential and of the rounding (far below the 0.1 % margin while that weight
+    // is at least 1,024), so the bins' mass bounds their count.
+    auto bins_fit = [&](int lo, int hi) -> bool {
+        const double wmin = exp2(43.0 - static_cast<double>(hi + 1) / static_cast<double>(wc.bin_scale));
+        if (!(wmin >= 1024.0)) return false;
+        const double mass = static_cast<double>(CG[hi] - (lo > 0 ? CG[lo - 1] : 0ull));
+        return mass <= 0.999 * wmin * static_cast<double>(gseg);
+    };
     auto gather = [&](int bA, int bufA, int bBlo, int bBhi, int bufB, unsigned long long lowb) {
         // key intervals: bin bA, and bins bBlo..bBhi (empty when bBlo < 0); the four boundaries are
         // computed at once by warps 0-3
@@ -2506,7 +2517,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                         if (zlo > 0ull) {
                             blo = bin_of_target(scale_mass(rc.u_draw, zlo) + 1ull);
                             bhi = bin_of_target(scale_mass(rc.u_draw, zhi) + 1ull);
-                            if (bhi - blo >= kPreBins) blo = bhi = -1;
+                            if (bhi - blo >= kPreBins && !bins_fit(blo, bhi)) blo = bhi = -1;
                         }
                     }
                     if (blo >= 0 && !(blo == b && bhi == b)) {

@@ -231,7 +231,8 @@ def _graph_ms(step, steps: int, warmup: int, stream) -> float:
 def run_workload(args) -> int:
     """The other configurations of the path on one GPU (reported beside the config-2 line):
     config1 single-row latency, config3 grammar-masked batch, config4 speculative verification,
-    grammar: the JSON-constrained step with device-produced masks."""
+    grammar: the JSON-constrained step with device-produced masks, numeric: the NaN / Inf policy
+    pass over config-2 rows."""
     import torch
 
     import sixi_smp as S
@@ -425,6 +426,40 @@ def run_workload(args) -> int:
             extra["cpu_baseline"] = {"value": n / el, "unit": "mask rows/s", "cores": thr, "kind": "port",
                                      "sample": f"{n} rows of JSON-grammar masks (oracle automaton, {thr} threads)"}
         gram_obj = gram
+    elif args.workload == "numeric":
+        nbuf = NBUF
+        rng = np.random.default_rng(51)
+        logits = [t(W.config2_logits(rng, ROWS, VOCAB)) for _ in range(nbuf)]
+        smp = S.Sampler(0, 64, VOCAB)
+        rep = torch.empty((ROWS, 32), dtype=torch.uint8, device=dev)
+
+        def step(i):
+            smp.numeric_policy(logits[i % nbuf], S.NUMERIC_FAIL, 0.0, out=rep, stream=torch.cuda.current_stream())
+
+        ms = _graph_ms(step, args.steps, args.warmup, stream)
+        torch.cuda.synchronize()
+        assert (S.numeric_reports(rep)["healthy"] == 1).all()
+        nbytes = ROWS * VOCAB * 4 + ROWS * 32  # every logit read once, one report written per row
+        unit, value = "rows/s", ROWS * args.steps / (ms / 1e3)
+        metric = ("NaN/Inf policy rows/s at B=32, V=151,936 fp32 (inspect_and_apply_numeric_policy, "
+                  "fail policy, read-only pass)")
+        data = "synthetic; 16 rotating batches (311 MB > L2)"
+        launches = args.steps
+        extra = {}
+        if not args.no_cpu:
+            from oracle import binding as OB
+
+            o = OB.reference() or OB.port()
+            host = [x.cpu().numpy() for x in logits[:2]]
+            n = 0
+            t0 = time.perf_counter()
+            while time.perf_counter() - t0 < min(args.cpu_budget, 5.0):
+                row = host[n % 2][n % ROWS].copy()
+                o.numeric_policy(row, 0, 0.0)
+                n += 1
+            el = time.perf_counter() - t0
+            extra["cpu_baseline"] = {"value": n / el, "unit": "rows/s", "cores": 1, "kind": o.kind,
+                                     "sample": f"{n} rows of {VOCAB} fp32 (the engine's function, 1 thread)"}
     else:
         raise SystemExit(f"unknown workload {args.workload}")
     per_launch_s = ms / 1e3 / args.steps
@@ -439,7 +474,7 @@ def run_workload(args) -> int:
                      "peak_source": peak_kind, "bytes_per_launch": int(nbytes)},
         "gpu_launches": launches,
     }
-    if args.workload in ("grammar", "config4f"):
+    if args.workload in ("grammar", "config4f", "numeric"):
         line.update(extra)
     if args.workload == "grammar":
         gram_obj.close()
@@ -458,7 +493,7 @@ def main() -> int:
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload", default="config2", choices=["config2", "config1", "config3", "config4", "config4f",
-                                                                 "grammar"],
+                                                                 "grammar", "numeric"],
                     help="config2 is the headline line; the others are reported beside it (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

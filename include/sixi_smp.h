@@ -272,6 +272,39 @@ SIXI_SMP_API int32_t sixi_smp_merge_shards(sixi_smp* h, uint32_t n_rows, uint32_
                               const sixi_smp_params* params, const double* uniforms, uint64_t step,
                               int32_t* out_tokens, int32_t* out_status, void* stream);
 
+/*
+ * NaN / Inf inspection and policy of logits rows, in place: inspect_and_apply_numeric_policy
+ * (src/core/numeric.cpp:628-699; NumericPolicy and NumericHealthReport,
+ * include/sixi_asi/numeric.hpp:126-140), batched over device rows. The engine applies it to a row's
+ * logits before sampling (src/core/core_execution.cpp:2127-2135, src/server/server.cpp:2351-2366).
+ * For each of n_rows rows of vocab fp32 logits (rows + r * row_stride; 4-byte aligned):
+ *   - counts NaNs and infinities and finds the first index holding either (-1 when none);
+ *   - SIXI_SMP_NUMERIC_FAIL leaves the row unchanged; a row with any NaN or Inf reports
+ *     healthy = 0, request_corrupted = state_invalidated = 1, emergency_clamped = 0 and status
+ *     SIXI_NUMERIC_NAN_OR_INF;
+ *   - SIXI_SMP_NUMERIC_CLAMP writes NaN -> +0, +-Inf -> +-|clamp_abs_max| and, when
+ *     |clamp_abs_max| > 0, finite values beyond it -> +-|clamp_abs_max|; a row with any NaN or Inf
+ *     reports healthy = 0, and emergency_clamped = 1 when it was bad or a finite value was clamped;
+ *     status SIXI_OK.
+ * out_reports [n_rows] is device memory. Asynchronous on `stream`; the return value covers the
+ * arguments and the launch only.
+ */
+#define SIXI_SMP_NUMERIC_FAIL 0u  /* NumericPolicy::FailAndInvalidate */
+#define SIXI_SMP_NUMERIC_CLAMP 1u /* NumericPolicy::EmergencyClampAndReport */
+typedef struct sixi_smp_numeric_report {
+    uint8_t healthy;
+    uint8_t request_corrupted;
+    uint8_t state_invalidated;
+    uint8_t emergency_clamped;
+    int32_t status;          /* SIXI_OK or SIXI_NUMERIC_NAN_OR_INF */
+    uint64_t nan_count;
+    uint64_t inf_count;
+    int64_t first_bad_index; /* -1 when every value is finite */
+} sixi_smp_numeric_report;   /* 32 bytes */
+SIXI_SMP_API int32_t sixi_smp_numeric_policy(sixi_smp* h, float* rows, uint32_t n_rows, uint64_t row_stride,
+                                             uint32_t policy, float clamp_abs_max,
+                                             sixi_smp_numeric_report* out_reports, void* stream);
+
 /* Philox4x32-10 uniform used when `uniforms` is NULL (host copy of the device function). */
 SIXI_SMP_API double sixi_smp_philox_uniform(uint64_t seed, uint64_t counter, uint32_t slot);
 

@@ -35,6 +35,7 @@ _SIGS = {
     "orc_candidates": (_I32, [_P, _U32, _U64, _P, _P, _U64, _P, _U64, _P, _P, _P]),
     "orc_sample": (_I32, [_P, _U32, _U64, _P, _P, _U64, _P, ctypes.c_double, _P]),
     "orc_sample_batch": (_I32, [_P, _U32, _U32, _U64, _U64, _P, _P, _P, _P, _P, _U64, _P, _P, _I32]),
+    "orc_numeric_policy": (_I32, [_P, ctypes.c_int64, _U32, ctypes.c_float, _P]),
     "orc_verify": (_I32, [_P, _U32, _U64, _U64, _P, _P, _P, _U32, _U32, _P, _P, _P, _P, _P, _U64,
                           _P, _P, _P, _P, _P, _P, _I32]),
     # JSON-object grammar automaton (sixi_json_oracle.c)
@@ -43,6 +44,11 @@ _SIGS = {
     "orc_json_advance": (None, [_P, _P, _P, _U32, _I32, _P, _U32, _P, _U64, _P, _P]),
     "orc_json_expand": (None, [_P, _P, _P, _U32, _I32, _P, _U32, _P, _U32, _P, _P]),
 }
+
+
+NUMERIC_REPORT = np.dtype([("healthy", "u1"), ("request_corrupted", "u1"), ("state_invalidated", "u1"),
+                           ("emergency_clamped", "u1"), ("status", "<i4"), ("nan_count", "<u8"),
+                           ("inf_count", "<u8"), ("first_bad_index", "<i8")])  # sixi_smp_numeric_report
 
 
 def build() -> None:
@@ -69,6 +75,13 @@ class Oracle:
             fn.restype = res
             fn.argtypes = args
         self.kind = "reference" if self.lib.orc_kind() == 1 else "port"
+
+    def numeric_policy(self, data: np.ndarray, policy: int, clamp_abs_max: float) -> tuple[int, np.void]:
+        """inspect_and_apply_numeric_policy on one fp32 row, in place: (status, report record)."""
+        assert data.dtype == np.float32 and data.flags.c_contiguous
+        rep = np.zeros(1, dtype=NUMERIC_REPORT)
+        st = self.lib.orc_numeric_policy(_p(data), data.size, policy, clamp_abs_max, _p(rep))
+        return int(st), rep[0]
 
     def philox_uniform(self, seed: int, counter: int, slot: int) -> float:
         return float(self.lib.orc_philox_uniform(seed, counter, slot))

@@ -192,6 +192,28 @@ EXPORT void orc_full_distribution(const void* row, uint32_t dtype, uint64_t voca
     for (uint64_t i = 0; i < vocab; ++i) out[i] = i < probs.size() ? probs[i] : 0.0f;
 }
 
+// The engine's own inspect_and_apply_numeric_policy (src/core/numeric.cpp:628-699), its report
+// copied field by field into the sixi_smp_numeric_report layout.
+EXPORT int32_t orc_numeric_policy(float* data, int64_t n, uint32_t policy, float clamp_abs_max,
+                                  sixi_smp_numeric_report* out) {
+    sixi_asi::NumericHealthReport rep{};
+    const sixi_asi::NumericPolicy pol = policy == SIXI_SMP_NUMERIC_CLAMP ? sixi_asi::NumericPolicy::EmergencyClampAndReport
+                                                                          : sixi_asi::NumericPolicy::FailAndInvalidate;
+    const sixi_asi::Status st = sixi_asi::inspect_and_apply_numeric_policy(data, n, pol, clamp_abs_max, &rep);
+    const int32_t code = static_cast<int32_t>(st.code);
+    if (out != nullptr) {
+        out->healthy = rep.healthy ? 1 : 0;
+        out->request_corrupted = rep.request_corrupted ? 1 : 0;
+        out->state_invalidated = rep.state_invalidated ? 1 : 0;
+        out->emergency_clamped = rep.emergency_clamped ? 1 : 0;
+        out->status = code;
+        out->nan_count = rep.nan_count;
+        out->inf_count = rep.inf_count;
+        out->first_bad_index = rep.first_bad_index;
+    }
+    return code;
+}
+
 EXPORT int32_t orc_greedy_row(const void* row, uint32_t dtype, uint64_t vocab,
                               const uint32_t* mask, int32_t* out_token) {
     return greedy_row(row, dtype, vocab, mask, out_token);

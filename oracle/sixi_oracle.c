@@ -103,6 +103,58 @@ int32_t orc_greedy_argmax(const float* logits, uint64_t vocab) {
     return best_id;
 }
 
+/* inspect_and_apply_numeric_policy (numeric.cpp:628-699): one forward scan; NaN and infinity are
+ * counted and the first of either is remembered; the clamp policy rewrites NaN as 0, infinities as
+ * the signed bound |clamp_abs_max|, and (bound > 0) finite values beyond the bound; the report's
+ * flags follow numeric.cpp:674-692. */
+int32_t orc_numeric_policy(float* data, int64_t n, uint32_t policy, float clamp_abs_max,
+                           sixi_smp_numeric_report* out) {
+    sixi_smp_numeric_report r;
+    memset(&r, 0, sizeof(r));
+    r.healthy = 1;
+    r.first_bad_index = -1;
+    if (n < 0 || (n > 0 && data == NULL)) {
+        r.status = SIXI_INVALID_ARGUMENT;
+        if (out) *out = r;
+        return SIXI_INVALID_ARGUMENT;
+    }
+    const int clamp = policy == SIXI_SMP_NUMERIC_CLAMP;
+    const float limit = fabsf(clamp_abs_max);
+    for (int64_t i = 0; i < n; ++i) {
+        const float v = data[i];
+        if (isnan(v)) {
+            ++r.nan_count;
+            if (r.first_bad_index < 0) r.first_bad_index = i;
+            if (clamp) data[i] = 0.0f;
+        } else if (isinf(v)) {
+            ++r.inf_count;
+            if (r.first_bad_index < 0) r.first_bad_index = i;
+            if (clamp) data[i] = (v > 0.0f) ? limit : -limit;
+        } else if (clamp && limit > 0.0f) {
+            if (v > limit) {
+                data[i] = limit;
+                r.emergency_clamped = 1;
+            } else if (v < -limit) {
+                data[i] = -limit;
+                r.emergency_clamped = 1;
+            }
+        }
+    }
+    if (r.nan_count > 0 || r.inf_count > 0) {
+        r.healthy = 0;
+        if (!clamp) {
+            r.request_corrupted = 1;
+            r.state_invalidated = 1;
+            r.emergency_clamped = 0;
+            r.status = SIXI_NUMERIC_NAN_OR_INF;
+        } else {
+            r.emergency_clamped = 1;
+        }
+    }
+    if (out) *out = r;
+    return r.status;
+}
+
 /* compute_full_distribution (core_execution.cpp:409-447): the scaled maximum ignores NaN; a NaN
  * or +inf logit makes the sum NaN and every probability 0. Built with -ffp-contract=off like the
  * engine, so x * inv_temp - max is a multiply then a subtract. */

@@ -65,6 +65,12 @@ int32_t orc_sample_batch(const void* logits, uint32_t dtype, uint32_t n_rows, ui
  * one-hot at the raw argmax; otherwise float(exp(x/T - max) / sum) with fp64 terms. */
 void orc_full_distribution(const void* row, uint32_t dtype, uint64_t vocab, float temperature, float* out);
 
+/* inspect_and_apply_numeric_policy (numeric.cpp:628-699) on one fp32 row, in place. Returns the
+ * engine's status (SIXI_NUMERIC_NAN_OR_INF for a bad row under SIXI_SMP_NUMERIC_FAIL) and fills
+ * `out` in the layout of sixi_smp_numeric_report (whose status field repeats the return value). */
+int32_t orc_numeric_policy(float* data, int64_t n, uint32_t policy, float clamp_abs_max,
+                           sixi_smp_numeric_report* out);
+
 /* Speculative verification, same layout and semantics as sixi_smp_verify (host memory). */
 int32_t orc_verify(const void* target, uint32_t dtype, uint64_t row_stride, uint64_t vocab,
                    const float* draft_probs, const int32_t* drafts, const int32_t* n_drafts,

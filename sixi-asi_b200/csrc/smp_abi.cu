@@ -438,6 +438,20 @@ int32_t sixi_smp_full_distribution(sixi_smp* h, const sixi_smp_rows* rows, const
     return from_cuda(sixi_b200::launch_full_distribution(a, plan, static_cast<cudaStream_t>(stream)));
 }
 
+int32_t sixi_smp_numeric_policy(sixi_smp* h, float* rows, uint32_t n_rows, uint64_t row_stride, uint32_t policy,
+                                float clamp_abs_max, sixi_smp_numeric_report* out_reports, void* stream) {
+    if (h == nullptr || out_reports == nullptr || (n_rows > 0 && rows == nullptr) || row_stride < h->vocab ||
+        (policy != SIXI_SMP_NUMERIC_FAIL && policy != SIXI_SMP_NUMERIC_CLAMP) ||
+        (reinterpret_cast<uintptr_t>(rows) & 3u) != 0 || (reinterpret_cast<uintptr_t>(out_reports) & 7u) != 0)
+        return SIXI_INVALID_ARGUMENT;
+    if (n_rows == 0) return SIXI_OK;
+    DeviceGuard g(h->device);
+    // numeric.cpp:641: the clamp bound is the magnitude of clamp_abs_max
+    const float limit = fabsf(clamp_abs_max);
+    return from_cuda(sixi_b200::launch_numeric_policy(rows, n_rows, row_stride, h->vocab, policy, limit, out_reports,
+                                                      static_cast<cudaStream_t>(stream)));
+}
+
 int32_t sixi_smp_verify_static(int32_t device, uint32_t vocab, const sixi_smp_rows* target,
                                const float* draft_probs, const int32_t* drafts, const int32_t* n_drafts,
                                uint32_t n_streams, uint32_t k, const sixi_smp_params* params,

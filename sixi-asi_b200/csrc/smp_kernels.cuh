@@ -89,6 +89,10 @@ cudaError_t launch_verify_finalize(const RowArgs& a, uint32_t n_streams, int32_t
                                    int32_t* out_status, cudaStream_t stream);
 cudaError_t prepare_kernels(int device);
 
+// ---- NaN / Inf policy (smp_numeric.cu) -------------------------------------------------------
+cudaError_t launch_numeric_policy(float* data, uint32_t n_rows, uint64_t row_stride, uint32_t vocab, uint32_t policy,
+                                  float limit, sixi_smp_numeric_report* out, cudaStream_t stream);
+
 // ---- vocab-sharded mode (smp_shard.cu) ---------------------------------------------------------
 struct ShardCand {  // one candidate of a shard (8 bytes, the layout of include/sixi_smp.h)
     float logit;    // adjusted logit (mask, penalties applied)

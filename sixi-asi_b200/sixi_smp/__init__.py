@@ -57,6 +57,22 @@ PARAMS_DTYPE = np.dtype(
 )
 assert PARAMS_DTYPE.itemsize == 56
 
+NUMERIC_FAIL = 0   # SIXI_SMP_NUMERIC_FAIL (NumericPolicy::FailAndInvalidate)
+NUMERIC_CLAMP = 1  # SIXI_SMP_NUMERIC_CLAMP (NumericPolicy::EmergencyClampAndReport)
+NUMERIC_REPORT_DTYPE = np.dtype(
+    [
+        ("healthy", "u1"),
+        ("request_corrupted", "u1"),
+        ("state_invalidated", "u1"),
+        ("emergency_clamped", "u1"),
+        ("status", "<i4"),
+        ("nan_count", "<u8"),
+        ("inf_count", "<u8"),
+        ("first_bad_index", "<i8"),
+    ]
+)
+assert NUMERIC_REPORT_DTYPE.itemsize == 32
+
 
 class Rows(ctypes.Structure):
     _fields_ = [
@@ -86,6 +102,7 @@ SIGNATURES = {
     "sixi_smp_verify": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32, _P, _P, _P, _P, _P,
                                _U64, _P, _P, _P, _P, _P, _P, _P]),
     "sixi_smp_full_distribution": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _U64, _P]),
+    "sixi_smp_numeric_policy": (_I32, [_P, _P, _U32, _U64, _U32, ctypes.c_float, _P, _P]),
     "sixi_smp_verify_draft_logits": (_I32, [_P, ctypes.POINTER(Rows), ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32,
                                             _P, _P, _P, _P, _P, _U64, _P, _P, _P, _P, _P, _P, _P]),
     "sixi_smp_verify_static": (_I32, [_I32, _U32, ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32, _P, _P, _P,
@@ -305,6 +322,22 @@ class Sampler:
         _check("sixi_smp_full_distribution", st)
         return out
 
+    def numeric_policy(self, logits, policy: int = NUMERIC_FAIL, clamp_abs_max: float = 0.0, out=None, stream=None):
+        """inspect_and_apply_numeric_policy per row of fp32 `logits` [n_rows, >= vocab] (a row view
+        of wider rows is fine), in place under NUMERIC_CLAMP. Returns the reports as a uint8 device
+        tensor [n_rows, 32] (numeric_reports() views them as NUMERIC_REPORT_DTYPE records)."""
+        import torch
+
+        if logits.dtype != torch.float32 or logits.dim() != 2 or logits.stride(1) != 1:
+            raise ValueError("numeric_policy takes fp32 rows [n_rows, >= vocab] with unit column stride")
+        n = logits.shape[0]
+        if out is None:
+            out = torch.empty((n, 32), dtype=torch.uint8, device=logits.device)
+        st = _lib().sixi_smp_numeric_policy(self.h, _ptr(logits), n, logits.stride(0), policy, clamp_abs_max,
+                                            _ptr(out), self._stream(stream))
+        _check("sixi_smp_numeric_policy", st)
+        return out
+
     # -- vocab-sharded mode ----------------------------------------------------------------------
     def shard_candidates(self, shard_logits, vocab_offset: int, shard_vocab: int, params, top_n: int = 64,
                          masks=None, hist=None, hist_off=None, stream=None):
@@ -382,3 +415,8 @@ def verify_static(vocab: int, target, drafts, params, draft_probs=None, n_drafts
                                        _ptr(used), _ptr(sts), Sampler._stream(stream))
     _check("sixi_smp_verify_static", st)
     return dict(accepted=acc, tokens=toks, n_tokens=ntok, first_reject=frej, uniforms_used=used, status=sts)
+
+
+def numeric_reports(t) -> np.ndarray:
+    """The uint8 [n_rows, 32] report tensor of Sampler.numeric_policy as NUMERIC_REPORT_DTYPE records."""
+    return np.ascontiguousarray(t.cpu().numpy()).view(NUMERIC_REPORT_DTYPE).reshape(-1)

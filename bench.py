@@ -470,7 +470,8 @@ def run_workload(args) -> int:
         "dtype": "bf16" if args.workload.startswith("config4") else "f32", "data": data,
         "config": {"workload": args.workload},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": profiled_traffic("verify_config4_traffic.md") if args.workload == "config4" else None,
+                     "traffic": ({"config4": profiled_traffic("verify_config4_traffic.md"),
+                                  "numeric": profiled_traffic("numeric_kernel_config2.md")}.get(args.workload)),
                      "peak_source": peak_kind, "bytes_per_launch": int(nbytes)},
         "gpu_launches": launches,
     }

@@ -28,6 +28,7 @@ constexpr int kNumNT = 256;      // threads per CTA (two CTAs per SM: a 32-row b
 constexpr int kNumUnroll = 10;   // 16-byte loads in flight per thread
 constexpr uint32_t kNumMaxCpr = 8;
 constexpr uint32_t kNumPerCta = 8192;  // elements per CTA that justify another CTA of the cluster
+constexpr uint32_t kNumFillCtas = 2u * 148u;  // CTAs that fill a B200 (two per SM)
 constexpr uint32_t kNumStageMax = 96u * 1024u;  // largest chunk staged in shared memory (bytes)
 constexpr uint32_t kNumPiece = 32768u;          // bytes per bulk copy
 constexpr uint32_t kNumWaitIters = 1u << 24;    // bound of the staging wait (never expected to run out)
@@ -196,8 +197,17 @@ __global__ void __launch_bounds__(kNumNT, 2) numeric_kernel(float* __restrict__ 
 cudaError_t launch_numeric_policy(float* data, uint32_t n_rows, uint64_t row_stride, uint32_t vocab, uint32_t policy,
                                   float limit, sixi_smp_numeric_report* out, cudaStream_t stream) {
     if (n_rows == 0) return cudaSuccess;
+    // CTAs per row: one per kNumPerCta elements, at most kNumMaxCpr, so that a row's chunks fit the
+    // staged path. A batch of at least half a GPU's worth of CTAs in rows takes just enough CTAs per
+    // row to fill the GPU (one per row from kNumFillCtas rows): there, clusters of 8 measured slower
+    // (202 against 153 us at 1,024 rows, 55 against 44 us at 256 rows), while below it the staged
+    // 8-CTA split is the faster one (16 against 20 us at 64 rows).
     uint32_t cpr = (vocab + kNumPerCta - 1) / kNumPerCta;
     cpr = cpr < 1u ? 1u : (cpr > kNumMaxCpr ? kNumMaxCpr : cpr);
+    if (n_rows >= kNumFillCtas / 2) {
+        const uint32_t want = (kNumFillCtas + n_rows - 1) / n_rows;
+        cpr = cpr < want ? cpr : want;
+    }
     const uint32_t per = (((vocab + cpr - 1) / cpr) + 3u) & ~3u;
     const uint32_t vec = ((reinterpret_cast<uintptr_t>(data) & 15u) == 0 && (row_stride & 3u) == 0) ? 1u : 0u;
     const uint32_t staged = (vec && 4u * per <= kNumStageMax) ? 1u : 0u;

@@ -91,6 +91,15 @@ def test_vocab_sizes_and_unaligned_rows(vocab):
         check(x, vocab + 4, vocab, policy, 0.0, offset=4)
 
 
+def test_large_batch_one_cta_per_row():
+    """A batch that fills the GPU by itself runs one CTA per row (no cluster, 16-byte loads)."""
+    rng = np.random.default_rng(77)
+    vocab = W.QWEN_VOCAB
+    x = make_rows(rng, 320, vocab)
+    for policy in (S.NUMERIC_FAIL, S.NUMERIC_CLAMP):
+        check(x, vocab, vocab, policy, 60.0)
+
+
 def test_engine_unit_vectors_on_device():
     """The engine's own test rows (test_routing_and_numerics.cpp:415-460), one per policy."""
     rows = np.array([[1.0, 2.5, np.nan, -3.0, np.inf], [1.0, np.nan, np.inf, -np.inf, 500.0]], np.float32)

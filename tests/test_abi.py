@@ -104,3 +104,21 @@ def test_launch_plan_limits(vocab):
     h = ctypes.c_void_p()
     st = sixi_smp.load().sixi_smp_create(-1, 16, vocab, ctypes.byref(h))
     assert st == sixi_smp.INVALID_ARGUMENT  # device -1 is invalid, the vocabulary itself is accepted
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    """No CPU fallback: with the CUDA library absent every entry of the binding raises."""
+    import sys
+
+    code = ("import sixi_smp as S\n"
+            "for f in (lambda: S.Sampler(0, 1, 64), lambda: S.philox_uniform(1, 2, 0), lambda: S.status_string(0)):\n"
+            "    try:\n"
+            "        f()\n"
+            "    except (ImportError, OSError):\n"
+            "        continue\n"
+            "    raise SystemExit('an entry point ran without the library')\n"
+            "print('raised')\n")
+    env = dict(__import__("os").environ, SIXI_SMP_LIB=str(tmp_path / "absent.so"))
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=120,
+                       cwd=str(REPO / "sixi-asi_b200"))
+    assert r.returncode == 0 and "raised" in r.stdout, (r.stdout, r.stderr[-1000:])

@@ -236,6 +236,53 @@ public:
         return r[1] == SIXI_OK ? r[0] : -1;
     }
 
+    // NaN / Inf inspection and policy of one host row, in place, with the engine's signature and
+    // Status (inspect_and_apply_numeric_policy, src/core/numeric.cpp:628-699): `policy` is the
+    // engine's NumericPolicy (0 FailAndInvalidate, 1 EmergencyClampAndReport) and `out_report` any
+    // type with NumericHealthReport's fields (include/sixi_asi/numeric.hpp:131-139). A row with a
+    // NaN or an infinity under the fail policy returns NumericNaNOrInf with the engine's message.
+    // The row is the sampler's vocabulary wide (n == vocab()), or empty.
+    template <class Policy, class Report>
+    Status inspect_and_apply_numeric_policy(float* data, int64_t n, Policy policy, float clamp_abs_max,
+                                            Report* out_report) {
+        if (n < 0 || (n > 0 && data == nullptr))
+            return Status::Error(ErrorCode::InvalidArgument, "invalid data pointer or element count");
+        sixi_smp_numeric_report r{};
+        r.healthy = 1;
+        r.first_bad_index = -1;
+        const uint32_t pol = static_cast<uint32_t>(policy) == 1u ? SIXI_SMP_NUMERIC_CLAMP : SIXI_SMP_NUMERIC_FAIL;
+        if (n > 0) {
+            if (static_cast<uint64_t>(n) != vocab_)
+                return Status::Error(ErrorCode::InvalidArgument, "element count differs from the sampler's vocabulary");
+            detail::DeviceGuard g(device_);
+            if (!stage_logits(data, 1, static_cast<uint64_t>(n)) || !d_rep_.ensure(sizeof r)) return oom();
+            const int32_t rc = sixi_smp_numeric_policy(h_, d_logits_.as<float>(), 1, static_cast<uint64_t>(n), pol,
+                                                       clamp_abs_max, d_rep_.as<sixi_smp_numeric_report>(), stream_);
+            if (rc != SIXI_OK) return detail::status_of(rc, "sixi_smp_numeric_policy");
+            cudaError_t e = cudaMemcpyAsync(&r, d_rep_.p, sizeof r, cudaMemcpyDeviceToHost, stream_);
+            if (e == cudaSuccess && pol == SIXI_SMP_NUMERIC_CLAMP)
+                e = cudaMemcpyAsync(data, d_logits_.p, static_cast<size_t>(n) * sizeof(float), cudaMemcpyDeviceToHost,
+                                    stream_);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+            if (e != cudaSuccess) return Status::Error(ErrorCode::BackendError, cudaGetErrorString(e));
+        }
+        if (out_report != nullptr) {
+            out_report->healthy = r.healthy != 0;
+            out_report->request_corrupted = r.request_corrupted != 0;
+            out_report->state_invalidated = r.state_invalidated != 0;
+            out_report->emergency_clamped = r.emergency_clamped != 0;
+            out_report->nan_count = r.nan_count;
+            out_report->inf_count = r.inf_count;
+            out_report->first_bad_index = r.first_bad_index;
+        }
+        if (r.status != SIXI_OK)
+            return Status::Error(ErrorCode::NumericNaNOrInf,
+                                 "NaN/Inf detected at index " + std::to_string(r.first_bad_index) +
+                                     " (nan_count=" + std::to_string(r.nan_count) +
+                                     ", inf_count=" + std::to_string(r.inf_count) + ")");
+        return Status::Ok();
+    }
+
     // The sparse normalised distribution sample_token draws from (penalties -> top-k ->
     // temperature softmax -> top-p [-> min-p]); greedy yields one candidate with prob 1
     // (src/core/core_execution.cpp:449-584). `mask_words` (host, ceil(V/32) words) is optional.
@@ -460,7 +507,7 @@ private:
     uint32_t vocab_ = 0;
     cudaStream_t stream_ = nullptr;
     detail::DeviceBuffer d_logits_, d_params_, d_mask_, d_hist_, d_hoff_, d_u_, d_out_, d_cand_, d_q_, d_drafts_,
-        d_vout_;
+        d_vout_, d_rep_;
 };
 
 // Device-side grammar masks for `response_format: {"type": "json_object"}` answers

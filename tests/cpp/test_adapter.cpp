@@ -15,11 +15,15 @@
 //   json_constrained        JsonMaskProducer + masked sample_rows: a greedy constrained decode
 //                           writes the intended JSON object although a disallowed token scores
 //                           higher, and every mask equals the CPU automaton's (sixi_json_oracle.h)
+//   numeric_policy          inspect_and_apply_numeric_policy through the adapter vs the oracle
+//                           (both policies, the engine's unit vectors of
+//                           tests/test_routing_and_numerics.cpp:415-460, and a 151,936-wide row)
 // Exit status 0 when every check passes. Needs a CUDA device.
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <numeric>
 #include <string>
 #include <vector>
@@ -432,6 +436,58 @@ bool json_constrained() {
 
 }  // namespace
 
+// the engine's NumericPolicy / NumericHealthReport shapes (include/sixi_asi/numeric.hpp:127-139)
+enum class EnginePolicy : uint8_t { FailAndInvalidate = 0, EmergencyClampAndReport = 1 };
+struct EngineReport {
+    bool healthy = true, request_corrupted = false, state_invalidated = false, emergency_clamped = false;
+    uint64_t nan_count = 0, inf_count = 0;
+    int64_t first_bad_index = -1;
+};
+
+bool numeric_policy() {
+    const float nan = std::nanf(""), inf = INFINITY;
+    {  // the engine's unit vectors
+        auto made = DeviceSampler::create(0, 1, 5);
+        CHECK(made.ok());
+        DeviceSampler& s = *made.value();
+        std::vector<float> d = {1.0f, 2.5f, nan, -3.0f, inf};
+        EngineReport r;
+        Status st = s.inspect_and_apply_numeric_policy(d.data(), 5, EnginePolicy::FailAndInvalidate, 100.0f, &r);
+        CHECK(!st.ok() && st.code == ErrorCode::NumericNaNOrInf);
+        CHECK(!r.healthy && r.request_corrupted && r.state_invalidated && !r.emergency_clamped);
+        CHECK(r.nan_count == 1 && r.inf_count == 1 && r.first_bad_index == 2 && std::isnan(d[2]));
+        std::vector<float> c = {1.0f, nan, inf, -inf, 500.0f};
+        st = s.inspect_and_apply_numeric_policy(c.data(), 5, EnginePolicy::EmergencyClampAndReport, 100.0f, &r);
+        CHECK(st.ok() && r.emergency_clamped && r.nan_count == 1 && r.inf_count == 2);
+        CHECK(c == std::vector<float>({1.0f, 0.0f, 100.0f, -100.0f, 100.0f}));
+    }
+    const uint32_t V = 151936;
+    auto made = DeviceSampler::create(0, 1, V);
+    CHECK(made.ok());
+    DeviceSampler& s = *made.value();
+    TestRng rng(41);
+    for (int it = 0; it < 6; ++it) {
+        std::vector<float> x = normal_row(rng, V, 40.0f);
+        for (int k = 0; k < it * 3; ++k) x[rng.next_u64() % V] = (k % 3 == 0) ? nan : ((k % 3 == 1) ? inf : -inf);
+        for (int pol = 0; pol < 2; ++pol) {
+            std::vector<float> a = x, b = x;
+            EngineReport r;
+            const Status st = s.inspect_and_apply_numeric_policy(a.data(), V, static_cast<EnginePolicy>(pol), 50.0f, &r);
+            sixi_smp_numeric_report o{};
+            const int32_t ost = orc_numeric_policy(b.data(), V, static_cast<uint32_t>(pol), 50.0f, &o);
+            CHECK(static_cast<int32_t>(st.code) == ost);
+            CHECK(r.healthy == (o.healthy != 0) && r.request_corrupted == (o.request_corrupted != 0));
+            CHECK(r.state_invalidated == (o.state_invalidated != 0) && r.emergency_clamped == (o.emergency_clamped != 0));
+            CHECK(r.nan_count == o.nan_count && r.inf_count == o.inf_count && r.first_bad_index == o.first_bad_index);
+            CHECK(std::memcmp(a.data(), b.data(), V * sizeof(float)) == 0);
+        }
+    }
+    EngineReport r;
+    CHECK(s.inspect_and_apply_numeric_policy(static_cast<float*>(nullptr), 0, EnginePolicy::FailAndInvalidate, 0.0f, &r).ok());
+    CHECK(!s.inspect_and_apply_numeric_policy(static_cast<float*>(nullptr), 5, EnginePolicy::FailAndInvalidate, 0.0f, &r).ok());
+    return true;
+}
+
 int main() {
     struct {
         const char* name;
@@ -442,7 +498,8 @@ int main() {
                  {"errors", errors},
                  {"verify_random", verify_random},
                  {"verify_forced_rejection", verify_forced_rejection},
-                 {"json_constrained", json_constrained}};
+                 {"json_constrained", json_constrained},
+                 {"numeric_policy", numeric_policy}};
     int passed = 0, n = 0;
     for (auto& t : tests) {
         ++n;

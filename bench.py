@@ -232,7 +232,7 @@ def run_workload(args) -> int:
     """The other configurations of the path on one GPU (reported beside the config-2 line):
     config1 single-row latency, config3 grammar-masked batch, config4 speculative verification,
     grammar: the JSON-constrained step with device-produced masks, numeric: the NaN / Inf policy
-    pass over config-2 rows."""
+    pass over config-2 rows, drafter: batched suffix n-gram drafting."""
     import torch
 
     import sixi_smp as S
@@ -460,6 +460,51 @@ def run_workload(args) -> int:
             el = time.perf_counter() - t0
             extra["cpu_baseline"] = {"value": n / el, "unit": "rows/s", "cores": 1, "kind": o.kind,
                                      "sample": f"{n} rows of {VOCAB} fp32 (the engine's function, 1 thread)"}
+    elif args.workload == "drafter":
+        # 32 streams of 16,384-token histories: every fourth repeats a phrase (a match is found
+        # early), the rest are random over the vocabulary (the engine then runs its exact-tail search
+        # over the whole window)
+        streams, hlen, k = ROWS, 16384, 8
+        rng = np.random.default_rng(61)
+        hs = []
+        for i in range(streams):
+            h = rng.integers(0, VOCAB, size=hlen).astype(np.int32)
+            if i % 4 == 0:
+                h[6000:6012] = h[-12:]
+            hs.append(h)
+        off = np.zeros(streams + 1, np.int64)
+        off[1:] = np.cumsum([h.size for h in hs])
+        d_hist, d_off = t(np.concatenate(hs)), t(off)
+        smp = S.Sampler(0, 64, VOCAB)
+        drafts = torch.empty((streams, k), dtype=torch.int32, device=dev)
+        mlen = torch.empty(streams, dtype=torch.int32, device=dev)
+
+        def step(i):
+            smp.suffix_draft(d_hist, d_off, k=k, min_match_len=3, max_window_tokens=16384, out=drafts, out_match=mlen,
+                             stream=torch.cuda.current_stream())
+
+        ms = _graph_ms(step, args.steps, args.warmup, stream)
+        torch.cuda.synchronize()
+        assert (mlen.cpu().numpy()[::4] > 0).all()
+        nbytes = 4 * int(off[-1])  # every history token read once
+        unit, value = "stream-steps/s", streams * args.steps / (ms / 1e3)
+        metric = ("suffix n-gram drafts per second: SuffixDrafter(3, 16384).propose for 32 streams of 16,384-token "
+                  "histories, k = 8")
+        data = "synthetic; random token histories, a quarter with a repeated 12-token phrase"
+        launches = args.steps
+        extra = {}
+        if not args.no_cpu:
+            from oracle import binding as OB
+
+            o = OB.reference() or OB.port()
+            n = 0
+            t0 = time.perf_counter()
+            while time.perf_counter() - t0 < min(args.cpu_budget, 5.0):
+                o.suffix_draft(hs[n % streams], 3, 16384, k)
+                n += 1
+            el = time.perf_counter() - t0
+            extra["cpu_baseline"] = {"value": n / el, "unit": "stream-steps/s", "cores": 1, "kind": o.kind,
+                                     "sample": f"{n} proposals of the engine's SuffixDrafter on these histories, 1 thread"}
     else:
         raise SystemExit(f"unknown workload {args.workload}")
     per_launch_s = ms / 1e3 / args.steps
@@ -467,7 +512,8 @@ def run_workload(args) -> int:
     line = {
         "metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": unit != "us/step", "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16" if args.workload.startswith("config4") else "f32", "data": data,
+        "dtype": ("bf16" if args.workload.startswith("config4") else ("int32" if args.workload == "drafter" else "f32")),
+        "data": data,
         "config": {"workload": args.workload},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": ({"config4": profiled_traffic("verify_config4_traffic.md"),
@@ -475,7 +521,7 @@ def run_workload(args) -> int:
                      "peak_source": peak_kind, "bytes_per_launch": int(nbytes)},
         "gpu_launches": launches,
     }
-    if args.workload in ("grammar", "config4f", "numeric"):
+    if args.workload in ("grammar", "config4f", "numeric", "drafter"):
         line.update(extra)
     if args.workload == "grammar":
         gram_obj.close()
@@ -494,7 +540,7 @@ def main() -> int:
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload", default="config2", choices=["config2", "config1", "config3", "config4", "config4f",
-                                                                 "grammar", "numeric"],
+                                                                 "grammar", "numeric", "drafter"],
                     help="config2 is the headline line; the others are reported beside it (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

@@ -305,6 +305,25 @@ SIXI_SMP_API int32_t sixi_smp_numeric_policy(sixi_smp* h, float* rows, uint32_t 
                                              uint32_t policy, float clamp_abs_max,
                                              sixi_smp_numeric_report* out_reports, void* stream);
 
+/*
+ * Suffix n-gram drafting for a batch of streams on the device: SuffixDrafter::propose and
+ * SuffixDrafter::propose_anchored (src/speculative/speculative.cpp:24-176;
+ * include/sixi_asi/speculative.hpp:33-54), the engine's first drafter in SpeculativeDecoder
+ * (speculative.cpp:329, 340-360). Histories are CSR like the penalty histories: stream s owns
+ * hist_tokens[hist_offsets[s] .. hist_offsets[s + 1]) (device memory).
+ *   anchors == NULL: propose - the most recent, longest match (at most 16 tokens, at least
+ *     min_match_len) of the history's suffix within its last max_window_tokens tokens;
+ *   anchors != NULL: propose_anchored - the same with anchors[s] as the pattern's last token.
+ * The k drafts continue the history after the match, repeating the continuation when it is
+ * shorter than k. out_drafts [n_streams][k] (-1 for a stream without a proposal); out_match_len
+ * [n_streams]: the engine's match_len, 0 when the engine returns no proposal. The drafts are
+ * one-hot (sixi_smp_verify with draft_probs = NULL). min_match_len <= 64, k <= 4096.
+ */
+SIXI_SMP_API int32_t sixi_smp_suffix_draft(sixi_smp* h, const int32_t* hist_tokens, const int64_t* hist_offsets,
+                                           uint32_t n_streams, uint32_t min_match_len, uint32_t max_window_tokens,
+                                           const int32_t* anchors, uint32_t k, int32_t* out_drafts,
+                                           int32_t* out_match_len, void* stream);
+
 /* Philox4x32-10 uniform used when `uniforms` is NULL (host copy of the device function). */
 SIXI_SMP_API double sixi_smp_philox_uniform(uint64_t seed, uint64_t counter, uint32_t slot);
 

@@ -36,6 +36,7 @@ _SIGS = {
     "orc_sample": (_I32, [_P, _U32, _U64, _P, _P, _U64, _P, ctypes.c_double, _P]),
     "orc_sample_batch": (_I32, [_P, _U32, _U32, _U64, _U64, _P, _P, _P, _P, _P, _U64, _P, _P, _I32]),
     "orc_numeric_policy": (_I32, [_P, ctypes.c_int64, _U32, ctypes.c_float, _P]),
+    "orc_suffix_draft": (_I32, [_P, _U64, _U32, _U32, _I32, _I32, _U32, _P]),
     "orc_verify": (_I32, [_P, _U32, _U64, _U64, _P, _P, _P, _U32, _U32, _P, _P, _P, _P, _P, _U64,
                           _P, _P, _P, _P, _P, _P, _I32]),
     # JSON-object grammar automaton (sixi_json_oracle.c)
@@ -82,6 +83,16 @@ class Oracle:
         rep = np.zeros(1, dtype=NUMERIC_REPORT)
         st = self.lib.orc_numeric_policy(_p(data), data.size, policy, clamp_abs_max, _p(rep))
         return int(st), rep[0]
+
+    def suffix_draft(self, hist: np.ndarray, min_match_len: int, max_window_tokens: int, k: int,
+                     anchor: int | None = None) -> tuple[int, np.ndarray]:
+        """SuffixDrafter(min_match_len, max_window_tokens).propose(hist, k) (or propose_anchored with
+        `anchor`): (match_len, 0 without a proposal; drafts int32 [k], -1 without one)."""
+        h = np.ascontiguousarray(hist, dtype=np.int32)
+        out = np.zeros(max(k, 1), dtype=np.int32)
+        m = self.lib.orc_suffix_draft(_p(h), h.size, min_match_len, max_window_tokens, 0 if anchor is None else 1,
+                                      0 if anchor is None else int(anchor), k, _p(out))
+        return int(m), out[:k]
 
     def philox_uniform(self, seed: int, counter: int, slot: int) -> float:
         return float(self.lib.orc_philox_uniform(seed, counter, slot))

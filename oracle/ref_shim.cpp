@@ -14,6 +14,7 @@
 // Inputs the engine cannot express (min_p, frequency penalty) return ORC_UNSUPPORTED.
 #include "sixi_asi/core_execution.hpp"
 #include "sixi_asi/numeric.hpp"
+#include "sixi_asi/speculative.hpp"
 
 #include <algorithm>
 #include <cmath>
@@ -190,6 +191,16 @@ EXPORT void orc_full_distribution(const void* row, uint32_t dtype, uint64_t voca
     std::vector<float> probs;
     DeterministicSampler::compute_full_distribution(x.data(), vocab, temperature, probs);
     for (uint64_t i = 0; i < vocab; ++i) out[i] = i < probs.size() ? probs[i] : 0.0f;
+}
+
+// The engine's own SuffixDrafter (src/speculative/speculative.cpp:24-176).
+EXPORT int32_t orc_suffix_draft(const int32_t* hist, uint64_t n, uint32_t min_match_len, uint32_t max_window_tokens,
+                                int32_t use_anchor, int32_t anchor, uint32_t k, int32_t* out_drafts) {
+    const std::vector<int32_t> h(hist, hist + n);
+    const sixi_asi::speculative::SuffixDrafter d(min_match_len, max_window_tokens);
+    const auto p = use_anchor ? d.propose_anchored(h, anchor, k) : d.propose(h, k, 0);
+    for (uint32_t i = 0; i < k; ++i) out_drafts[i] = p.has_value() ? p->draft_tokens[i] : -1;
+    return p.has_value() ? static_cast<int32_t>(p->match_len) : 0;
 }
 
 // The engine's own inspect_and_apply_numeric_policy (src/core/numeric.cpp:628-699), its report

@@ -103,6 +103,74 @@ int32_t orc_greedy_argmax(const float* logits, uint64_t vocab) {
     return best_id;
 }
 
+/* SuffixDrafter::propose (speculative.cpp:28-113): positions from the most recent backwards, the
+ * suffix compared from the end of a window of up to 16 tokens ending at pos + L - 1; a strictly
+ * longer match replaces the best. Without one of min_match_len, exact matches of the history's
+ * tail, longest first, most recent first. propose_anchored (speculative.cpp:115-176): the pattern
+ * is the history's tail followed by the anchor, matched backwards from each occurrence of the
+ * anchor. The k drafts repeat the continuation after the match. */
+int32_t orc_suffix_draft(const int32_t* h, uint64_t n, uint32_t min_match_len, uint32_t max_window_tokens,
+                         int32_t use_anchor, int32_t anchor, uint32_t k, int32_t* out_drafts) {
+    uint64_t best_len = 0, best_cont = 0;
+    int ok = 0;
+    const uint64_t ws = n > max_window_tokens ? n - max_window_tokens : 0;
+    if (!use_anchor) {
+        if (k != 0 && min_match_len != 0 && n > min_match_len) {
+            const uint64_t maxp = (n - 1) < 16 ? (n - 1) : 16;
+            for (uint64_t pos = n - min_match_len - 1;; --pos) {
+                if (pos < ws) break;
+                uint64_t m = 0;
+                const uint64_t L = maxp < n - 1 - pos ? maxp : n - 1 - pos;
+                while (m < L && h[pos + L - 1 - m] == h[n - 1 - m]) ++m;
+                if (m >= min_match_len && m > best_len) {
+                    best_len = m;
+                    best_cont = pos + L;
+                }
+                if (pos == ws) break;
+            }
+            if (best_len < min_match_len) {
+                for (uint64_t len = maxp; len >= min_match_len; --len) {
+                    if (len >= n) continue;
+                    const int32_t* tail = h + (n - len);
+                    for (uint64_t pos = n - len - 1;; --pos) {
+                        if (pos < ws) break;
+                        uint64_t i = 0;
+                        while (i < len && h[pos + i] == tail[i]) ++i;
+                        if (i == len) {
+                            best_len = len;
+                            best_cont = pos + len;
+                            break;
+                        }
+                        if (pos == ws) break;
+                    }
+                    if (best_len >= min_match_len) break;
+                    if (len == min_match_len) break;
+                }
+            }
+            ok = best_len >= min_match_len && best_cont < n;
+        }
+    } else if (k != 0 && n >= 2) {
+        const uint64_t min_total = (uint64_t)min_match_len + 1 > 2 ? (uint64_t)min_match_len + 1 : 2;
+        const uint64_t max_total = n < 16 ? n : 16;
+        for (uint64_t pos = n - 1;; --pos) {
+            if (pos < ws) break;
+            if (h[pos] == anchor && pos + 1 < n) {
+                uint64_t m = 1;
+                const uint64_t max_here = max_total < pos + 1 ? max_total : pos + 1;
+                while (m < max_here && h[pos - m] == h[n - m]) ++m;
+                if (m >= min_total && m > best_len) {
+                    best_len = m;
+                    best_cont = pos + 1;
+                }
+            }
+            if (pos == ws) break;
+        }
+        ok = best_len >= min_total && best_cont < n;
+    }
+    for (uint32_t i = 0; i < k; ++i) out_drafts[i] = ok ? h[best_cont + (i % (n - best_cont))] : -1;
+    return ok ? (int32_t)best_len : 0;
+}
+
 /* inspect_and_apply_numeric_policy (numeric.cpp:628-699): one forward scan; NaN and infinity are
  * counted and the first of either is remembered; the clamp policy rewrites NaN as 0, infinities as
  * the signed bound |clamp_abs_max|, and (bound > 0) finite values beyond the bound; the report's

@@ -65,6 +65,12 @@ int32_t orc_sample_batch(const void* logits, uint32_t dtype, uint32_t n_rows, ui
  * one-hot at the raw argmax; otherwise float(exp(x/T - max) / sum) with fp64 terms. */
 void orc_full_distribution(const void* row, uint32_t dtype, uint64_t vocab, float temperature, float* out);
 
+/* SuffixDrafter::propose (use_anchor = 0) or ::propose_anchored (use_anchor = 1, anchor) with
+ * SuffixDrafter(min_match_len, max_window_tokens) (speculative.cpp:24-176) on one history of n
+ * tokens. Returns the proposal's match_len, 0 when there is none; writes k drafts (-1 when none). */
+int32_t orc_suffix_draft(const int32_t* hist, uint64_t n, uint32_t min_match_len, uint32_t max_window_tokens,
+                         int32_t use_anchor, int32_t anchor, uint32_t k, int32_t* out_drafts);
+
 /* inspect_and_apply_numeric_policy (numeric.cpp:628-699) on one fp32 row, in place. Returns the
  * engine's status (SIXI_NUMERIC_NAN_OR_INF for a bad row under SIXI_SMP_NUMERIC_FAIL) and fills
  * `out` in the layout of sixi_smp_numeric_report (whose status field repeats the return value). */

@@ -452,6 +452,19 @@ int32_t sixi_smp_numeric_policy(sixi_smp* h, float* rows, uint32_t n_rows, uint6
                                                       static_cast<cudaStream_t>(stream)));
 }
 
+int32_t sixi_smp_suffix_draft(sixi_smp* h, const int32_t* hist_tokens, const int64_t* hist_offsets, uint32_t n_streams,
+                              uint32_t min_match_len, uint32_t max_window_tokens, const int32_t* anchors, uint32_t k,
+                              int32_t* out_drafts, int32_t* out_match_len, void* stream) {
+    if (h == nullptr || hist_offsets == nullptr || out_match_len == nullptr || (k > 0 && out_drafts == nullptr) ||
+        min_match_len > 64u || k > 4096u)
+        return SIXI_INVALID_ARGUMENT;
+    if (n_streams == 0) return SIXI_OK;
+    DeviceGuard g(h->device);
+    return from_cuda(sixi_b200::launch_suffix_draft(hist_tokens, hist_offsets, n_streams, min_match_len,
+                                                    max_window_tokens, anchors, k, out_drafts, out_match_len,
+                                                    static_cast<cudaStream_t>(stream)));
+}
+
 int32_t sixi_smp_verify_static(int32_t device, uint32_t vocab, const sixi_smp_rows* target,
                                const float* draft_probs, const int32_t* drafts, const int32_t* n_drafts,
                                uint32_t n_streams, uint32_t k, const sixi_smp_params* params,

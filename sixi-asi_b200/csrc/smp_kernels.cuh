@@ -93,6 +93,11 @@ cudaError_t prepare_kernels(int device);
 cudaError_t launch_numeric_policy(float* data, uint32_t n_rows, uint64_t row_stride, uint32_t vocab, uint32_t policy,
                                   float limit, sixi_smp_numeric_report* out, cudaStream_t stream);
 
+// ---- suffix n-gram drafting (smp_suffix.cu) --------------------------------------------------
+cudaError_t launch_suffix_draft(const int32_t* hist, const int64_t* off, uint32_t n_streams, uint32_t min_match,
+                                uint32_t window, const int32_t* anchors, uint32_t k, int32_t* out_drafts,
+                                int32_t* out_match, cudaStream_t stream);
+
 // ---- vocab-sharded mode (smp_shard.cu) ---------------------------------------------------------
 struct ShardCand {  // one candidate of a shard (8 bytes, the layout of include/sixi_smp.h)
     float logit;    // adjusted logit (mask, penalties applied)

@@ -103,6 +103,7 @@ SIGNATURES = {
                                _U64, _P, _P, _P, _P, _P, _P, _P]),
     "sixi_smp_full_distribution": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _U64, _P]),
     "sixi_smp_numeric_policy": (_I32, [_P, _P, _U32, _U64, _U32, ctypes.c_float, _P, _P]),
+    "sixi_smp_suffix_draft": (_I32, [_P, _P, _P, _U32, _U32, _U32, _P, _U32, _P, _P, _P]),
     "sixi_smp_verify_draft_logits": (_I32, [_P, ctypes.POINTER(Rows), ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32,
                                             _P, _P, _P, _P, _P, _U64, _P, _P, _P, _P, _P, _P, _P]),
     "sixi_smp_verify_static": (_I32, [_I32, _U32, ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32, _P, _P, _P,
@@ -337,6 +338,25 @@ class Sampler:
                                             _ptr(out), self._stream(stream))
         _check("sixi_smp_numeric_policy", st)
         return out
+
+    def suffix_draft(self, hist, hist_off, k: int = 8, min_match_len: int = 3, max_window_tokens: int = 16384,
+                     anchors=None, out=None, out_match=None, stream=None):
+        """SuffixDrafter::propose (or ::propose_anchored with `anchors` [n_streams]) for the CSR
+        histories (hist int32, hist_off int64 [n_streams + 1], device tensors). Returns
+        (drafts int32 [n_streams, k], match_len int32 [n_streams]; 0 and -1 drafts without a proposal)."""
+        import torch
+
+        n = hist_off.numel() - 1
+        dev = hist_off.device
+        if out is None:
+            out = torch.empty((n, k), dtype=torch.int32, device=dev)
+        if out_match is None:
+            out_match = torch.empty(n, dtype=torch.int32, device=dev)
+        st = _lib().sixi_smp_suffix_draft(self.h, _ptr(hist), _ptr(hist_off), n, min_match_len, max_window_tokens,
+                                          _ptr(anchors), k, _ptr(out) if k else None, _ptr(out_match),
+                                          self._stream(stream))
+        _check("sixi_smp_suffix_draft", st)
+        return out, out_match
 
     # -- vocab-sharded mode ----------------------------------------------------------------------
     def shard_candidates(self, shard_logits, vocab_offset: int, shard_vocab: int, params, top_n: int = 64,

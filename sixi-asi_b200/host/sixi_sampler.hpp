@@ -103,6 +103,13 @@ struct VerifyResult {
     uint32_t uniforms_used = 0;
 };
 
+// Draft fields of DraftProposal (include/sixi_asi/speculative.hpp:24-30) for the suffix drafter.
+struct SuffixProposal {
+    std::vector<int32_t> draft_tokens;              // length k
+    std::vector<std::vector<float>> draft_probs;    // [k][vocab_size] one-hot (empty when vocab_size == 0)
+    uint32_t match_len = 0;
+};
+
 namespace detail {
 
 template <class P, class = void>
@@ -281,6 +288,22 @@ public:
                                      " (nan_count=" + std::to_string(r.nan_count) +
                                      ", inf_count=" + std::to_string(r.inf_count) + ")");
         return Status::Ok();
+    }
+
+    // SuffixDrafter::propose / ::propose_anchored on one host history (src/speculative/
+    // speculative.cpp:28-176), with the engine's defaults SuffixDrafter(3, 16384): an empty optional
+    // where the engine returns none. propose fills one-hot draft_probs when vocab_size > 0, as the
+    // engine does. For many streams at once call sixi_smp_suffix_draft on device histories.
+    std::optional<SuffixProposal> suffix_propose(const std::vector<int32_t>& token_history, uint32_t k,
+                                                 uint64_t vocab_size, uint32_t min_match_len = 3,
+                                                 uint32_t max_window_tokens = 16384) {
+        return suffix_call(token_history, nullptr, k, vocab_size, min_match_len, max_window_tokens);
+    }
+    std::optional<SuffixProposal> suffix_propose_anchored(const std::vector<int32_t>& token_history,
+                                                          int32_t anchor_token, uint32_t k,
+                                                          uint32_t min_match_len = 3,
+                                                          uint32_t max_window_tokens = 16384) {
+        return suffix_call(token_history, &anchor_token, k, 0, min_match_len, max_window_tokens);
     }
 
     // The sparse normalised distribution sample_token draws from (penalties -> top-k ->
@@ -470,6 +493,41 @@ private:
     }
 
     static Status oom() { return Status::Error(ErrorCode::OutOfMemoryVRAM, "device staging allocation failed"); }
+
+    std::optional<SuffixProposal> suffix_call(const std::vector<int32_t>& hist, const int32_t* anchor, uint32_t k,
+                                              uint64_t vocab_size, uint32_t min_match_len, uint32_t window) {
+        if (k == 0 || k > 4096u || min_match_len > 64u) return std::nullopt;
+        detail::DeviceGuard g(device_);
+        const int64_t off[2] = {0, static_cast<int64_t>(hist.size())};
+        if (!d_hist_.ensure(hist.size() * 4 + 4) || !d_hoff_.ensure(sizeof off) || !d_drafts_.ensure((k + 2) * 4))
+            return std::nullopt;
+        int32_t* d_out = d_drafts_.as<int32_t>();
+        cudaError_t e = cudaSuccess;
+        if (!hist.empty()) e = cudaMemcpyAsync(d_hist_.p, hist.data(), hist.size() * 4, cudaMemcpyHostToDevice, stream_);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(d_hoff_.p, off, sizeof off, cudaMemcpyHostToDevice, stream_);
+        if (e == cudaSuccess && anchor != nullptr)
+            e = cudaMemcpyAsync(d_out + k + 1, anchor, 4, cudaMemcpyHostToDevice, stream_);
+        if (e != cudaSuccess) return std::nullopt;
+        if (sixi_smp_suffix_draft(h_, d_hist_.as<int32_t>(), d_hoff_.as<int64_t>(), 1, min_match_len, window,
+                                  anchor != nullptr ? d_out + k + 1 : nullptr, k, d_out, d_out + k,
+                                  stream_) != SIXI_OK)
+            return std::nullopt;
+        std::vector<int32_t> res(k + 1);
+        if (cudaMemcpyAsync(res.data(), d_out, (k + 1) * 4, cudaMemcpyDeviceToHost, stream_) != cudaSuccess ||
+            cudaStreamSynchronize(stream_) != cudaSuccess || res[k] == 0)
+            return std::nullopt;
+        SuffixProposal p;
+        p.match_len = static_cast<uint32_t>(res[k]);
+        p.draft_tokens.assign(res.begin(), res.begin() + k);
+        if (vocab_size > 0) {
+            p.draft_probs.assign(k, std::vector<float>(vocab_size, 0.0f));
+            for (uint32_t i = 0; i < k; ++i) {
+                const int32_t t = p.draft_tokens[i];
+                if (t >= 0 && static_cast<uint64_t>(t) < vocab_size) p.draft_probs[i][static_cast<size_t>(t)] = 1.0f;
+            }
+        }
+        return p;
+    }
 
     Status check_row(const float* logits, uint64_t vocab_size) const {
         if (logits == nullptr || vocab_size == 0)

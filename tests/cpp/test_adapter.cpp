@@ -18,6 +18,8 @@
 //   numeric_policy          inspect_and_apply_numeric_policy through the adapter vs the oracle
 //                           (both policies, the engine's unit vectors of
 //                           tests/test_routing_and_numerics.cpp:415-460, and a 151,936-wide row)
+//   suffix_drafter          suffix_propose / suffix_propose_anchored vs orc_suffix_draft (match
+//                           length, drafts, one-hot draft_probs)
 // Exit status 0 when every check passes. Needs a CUDA device.
 #include <algorithm>
 #include <cmath>
@@ -488,6 +490,40 @@ bool numeric_policy() {
     return true;
 }
 
+bool suffix_drafter() {
+    auto made = DeviceSampler::create(0, 1, 64);
+    CHECK(made.ok());
+    DeviceSampler& s = *made.value();
+    TestRng rng(17);
+    int found = 0;
+    for (int it = 0; it < 40; ++it) {
+        const size_t n = static_cast<size_t>(rng.next_u64() % 3000);
+        const uint64_t vocab = (it % 3 == 0) ? 4 : 64;
+        std::vector<int32_t> h(n);
+        for (auto& t : h) t = static_cast<int32_t>(rng.next_u64() % vocab);
+        if (n > 100 && it % 2 == 0) {  // a repeated tail
+            for (size_t i = 0; i < 10; ++i) h[n / 3 + i] = h[n - 10 + i];
+        }
+        const uint32_t k = 1 + static_cast<uint32_t>(rng.next_u64() % 9);
+        for (int anchored = 0; anchored < 2; ++anchored) {
+            const int32_t anchor = n ? h[rng.next_u64() % n] : 1;
+            auto p = anchored ? s.suffix_propose_anchored(h, anchor, k) : s.suffix_propose(h, k, 64);
+            std::vector<int32_t> od(k);
+            const int32_t om = orc_suffix_draft(h.data(), n, 3, 16384, anchored, anchor, k, od.data());
+            CHECK(p.has_value() == (om > 0));
+            if (!p.has_value()) continue;
+            ++found;
+            CHECK(static_cast<int32_t>(p->match_len) == om && p->draft_tokens == od);
+            if (!anchored) {
+                CHECK(p->draft_probs.size() == k);
+                for (uint32_t i = 0; i < k; ++i) CHECK(p->draft_probs[i][static_cast<size_t>(od[i])] == 1.0f);
+            }
+        }
+    }
+    CHECK(found > 10);
+    return true;
+}
+
 int main() {
     struct {
         const char* name;
@@ -499,7 +535,8 @@ int main() {
                  {"verify_random", verify_random},
                  {"verify_forced_rejection", verify_forced_rejection},
                  {"json_constrained", json_constrained},
-                 {"numeric_policy", numeric_policy}};
+                 {"numeric_policy", numeric_policy},
+                 {"suffix_drafter", suffix_drafter}};
     int passed = 0, n = 0;
     for (auto& t : tests) {
         ++n;

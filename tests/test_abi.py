@@ -66,6 +66,25 @@ def test_status_strings_and_create_without_gpu():
     assert lib.sixi_smp_create(0, 16, 10_000_000, ctypes.byref(h)) == sixi_smp.INVALID_ARGUMENT
     assert lib.sixi_smp_sample(None, None, None, None, None, None, None, 0, None, None, None) == \
         sixi_smp.INVALID_ARGUMENT
+    # NaN / Inf policy and suffix drafting: null handle, unknown policy, out-of-range sizes
+    assert lib.sixi_smp_numeric_policy(None, None, 0, 0, 0, 0.0, None, None) == sixi_smp.INVALID_ARGUMENT
+    assert lib.sixi_smp_suffix_draft(None, None, None, 1, 3, 16384, None, 8, None, None, None) == \
+        sixi_smp.INVALID_ARGUMENT
+
+
+def test_numeric_report_layout():
+    """sixi_smp_numeric_report is 32 bytes with the fields where the binding and the oracle read them."""
+    import numpy as np
+
+    import sixi_smp
+    from oracle import binding
+
+    assert sixi_smp.NUMERIC_REPORT_DTYPE == binding.NUMERIC_REPORT
+    r = np.zeros(2, sixi_smp.NUMERIC_REPORT_DTYPE)
+    r["first_bad_index"] = [-1, 7]
+    import torch
+
+    assert sixi_smp.numeric_reports(torch.from_numpy(r.view(np.uint8).reshape(2, 32)))["first_bad_index"].tolist() == [-1, 7]
 
 
 def test_struct_layouts(tmp_path):
@@ -79,6 +98,10 @@ def test_struct_layouts(tmp_path):
         int main(void) {{
             printf("%zu %zu %zu %zu %zu\\n", sizeof(sixi_smp_params), offsetof(sixi_smp_params, seed),
                    offsetof(sixi_smp_params, counter), sizeof(sixi_smp_rows), offsetof(sixi_smp_rows, row_stride));
+            printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(sixi_smp_numeric_report),
+                   offsetof(sixi_smp_numeric_report, emergency_clamped), offsetof(sixi_smp_numeric_report, status),
+                   offsetof(sixi_smp_numeric_report, nan_count), offsetof(sixi_smp_numeric_report, inf_count),
+                   offsetof(sixi_smp_numeric_report, first_bad_index));
             return 0;
         }}
     """))
@@ -91,6 +114,9 @@ def test_struct_layouts(tmp_path):
     assert vals[2] == pd.fields["counter"][1]
     assert vals[3] == __import__("ctypes").sizeof(sixi_smp.Rows)
     assert vals[4] == sixi_smp.Rows.row_stride.offset
+    nd = sixi_smp.NUMERIC_REPORT_DTYPE
+    assert vals[5:] == [nd.itemsize] + [nd.fields[f][1] for f in ("emergency_clamped", "status", "nan_count",
+                                                                   "inf_count", "first_bad_index")]
 
 
 @pytest.mark.parametrize("vocab", [1, 31, 5000, 151_936, 262_144])

@@ -208,6 +208,7 @@ cudaError_t launch_numeric_policy(float* data, uint32_t n_rows, uint64_t row_str
         const uint32_t want = (kNumFillCtas + n_rows - 1) / n_rows;
         cpr = cpr < want ? cpr : want;
     }
+    if (static_cast<uint64_t>(n_rows) * cpr > 0x7FFFFFFFull) return cudaErrorInvalidValue;  // grid limit
     const uint32_t per = (((vocab + cpr - 1) / cpr) + 3u) & ~3u;
     const uint32_t vec = ((reinterpret_cast<uintptr_t>(data) & 15u) == 0 && (row_stride & 3u) == 0) ? 1u : 0u;
     const uint32_t staged = (vec && 4u * per <= kNumStageMax) ? 1u : 0u;

@@ -168,6 +168,7 @@ cudaError_t launch_suffix_draft(const int32_t* hist, const int64_t* off, uint32_
                                 uint32_t window, const int32_t* anchors, uint32_t k, int32_t* out_drafts,
                                 int32_t* out_match, cudaStream_t stream) {
     if (n_streams == 0) return cudaSuccess;
+    if (n_streams > 0x7FFFFFFFu) return cudaErrorInvalidValue;  // grid limit
     // the staged span is at most window + 16 tokens (and the history itself)
     const uint64_t span = static_cast<uint64_t>(window) + kSdMaxPattern;
     const uint32_t cap_tokens = kSdStageMax / 4u;

@@ -313,6 +313,31 @@ def run_workload(args) -> int:
         metric = "speculative verify stream-steps/s (config 4: S=32, k=8, V=151,936, bf16 target, fp32 q)"
         data = "synthetic; 2 rotating batches (491 MB > L2)"
         launches = 2 * args.steps  # row kernel + per-stream finalize
+        extra = {}
+        if not args.no_cpu:
+            # the engine's own SpeculativeDecoder::step (slow path, dense q) per stream, on all host
+            # threads, through the reference build's replay backend and fixed-draft drafter
+            from oracle import binding as OB
+
+            o = OB.reference()
+            if o is not None and hasattr(o.lib, "orc_ref_spec_step_batch"):
+                thr = os.cpu_count() or 1
+                rs = np.stack([o.rng_seed(1000 + s) for s in range(streams)])
+                n, i = 0, 0
+                t0 = time.perf_counter()
+                while time.perf_counter() - t0 < min(args.cpu_budget, 10.0):
+                    x = ds[i % nbuf]
+                    r = o.spec_step_batch(x["target_bits"], x["drafts"], ds[0]["params"], ds[0]["hist"],
+                                          ds[0]["hist_off"], x["q"], rs, n_threads=thr)
+                    assert (r["status"] == 0).all(), r["status"]
+                    n += streams
+                    i += 1
+                el = time.perf_counter() - t0
+                extra["cpu_baseline"] = {
+                    "value": n / el, "unit": "stream-steps/s", "cores": thr, "kind": "reference",
+                    "sample": (f"{i} batches of {streams} streams: the engine's SpeculativeDecoder::step (slow path, "
+                               f"dense q, its own RNG) on the same target rows, drafts and q, {thr} threads; "
+                               "the engine's step takes no grammar masks, so none are applied")}
     elif args.workload == "config4f":
         # the drafter -> verifier pipeline from draft logits: q = full_distribution(draft logits)
         # evaluated inside the verifier (sixi_smp_verify_draft_logits), beside the two-launch
@@ -521,11 +546,308 @@ def run_workload(args) -> int:
                      "peak_source": peak_kind, "bytes_per_launch": int(nbytes)},
         "gpu_launches": launches,
     }
-    if args.workload in ("grammar", "config4f", "numeric", "drafter"):
+    if args.workload in ("grammar", "config4", "config4f", "numeric", "drafter"):
         line.update(extra)
     if args.workload == "grammar":
         gram_obj.close()
     print(json.dumps(line), flush=True)
+    smp.close()
+    return 0
+
+
+def _init_dist(local: int, world: int):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    return dev
+
+
+def _max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_config5(args) -> int:
+    """BASELINE config 5, rows partitioned: 8,192 rows x V = 151,936 fp32 (4.98 GB) with the
+    config-2 parameter mix, split into N equal row ranges, one per rank (strong scaling: the total
+    is fixed). A step is one sixi_smp_sample launch per rank over its rows; there is no collective
+    in the timed region. The logits are drawn on the device (one buffer per rank, 622 MB at N = 8,
+    larger than L2, so every step reads them from HBM)."""
+    import torch
+    import torch.distributed as dist
+
+    import sixi_smp as S
+    from sixi_smp import workloads as W
+
+    rank, world, local = dist_env()
+    dev = _init_dist(local, world)
+    total = args.rows
+    if total % world:
+        raise SystemExit(f"--rows {total} is not a multiple of the {world} ranks")
+    R = total // world
+    mix = W.config2_mix(total, VOCAB, seed=5)
+    prm = np.ascontiguousarray(mix["params"][rank * R:(rank + 1) * R])
+    off = mix["hist_off"][rank * R:(rank + 1) * R + 1]
+    hist = np.ascontiguousarray(mix["hist"][off[0]:off[-1]])
+    off = off - off[0]
+    logits = W.config2_logits_device(R, VOCAB, seed=5000 + rank, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(77 + rank)
+    u = torch.rand(R, dtype=torch.float64, device=dev, generator=g)
+    d_params = torch.from_numpy(prm.view(np.uint8)).to(dev)
+    d_hist, d_hoff = torch.from_numpy(hist).to(dev), torch.from_numpy(off).to(dev)
+    smp = S.Sampler(local, R, VOCAB)
+    tok = torch.empty(R, dtype=torch.int32, device=dev)
+    sts = torch.empty(R, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(i):
+        smp.sample(logits, d_params, hist=d_hist, hist_off=d_hoff, uniforms=u, step=i, out_tokens=tok,
+                   out_status=sts, stream=torch.cuda.current_stream())
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    stream.synchronize()
+    assert int((sts != 0).sum()) == 0, "non-zero statuses"
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(args.steps):
+            step(i)
+    with torch.cuda.stream(stream):
+        graph.replay()
+    stream.synchronize()
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.05)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+    e1.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    ms_max = _max_over_ranks(ms, world, dev)
+    value = total * args.steps / (ms_max / 1e3)
+    nbytes = R * VOCAB * 4 + 4 * int(off[-1])
+    achieved = nbytes / (ms / args.steps / 1e3) / 1e9
+    peak, peak_kind = peaks()
+
+    # end to end through the host entry point: this rank's rows from pinned host memory
+    e2e = None
+    n_e2e = min(args.e2e_steps, 3)
+    if n_e2e > 0:
+        h_logits = torch.empty((R, VOCAB), dtype=torch.float32).pin_memory()
+        h_logits.copy_(logits)
+        h_np = h_logits.numpy()
+        pin = lambda a: torch.from_numpy(a).pin_memory().numpy()  # noqa: E731
+        h_params = pin(prm.view(np.uint8)).view(S.PARAMS_DTYPE)
+        h_hist, h_hoff, h_u = pin(hist), pin(off), pin(u.cpu().numpy())
+        h_tok = pin(np.empty(R, np.int32))
+        h_st = pin(np.empty(R, np.int32))
+        smp.sample_host(h_np, h_params, hist=h_hist, hist_off=h_hoff, uniforms=h_u, out_tokens=h_tok,
+                        out_status=h_st, stream=stream)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            smp.sample_host(h_np, h_params, hist=h_hist, hist_off=h_hoff, uniforms=h_u, out_tokens=h_tok,
+                            out_status=h_st, stream=stream)
+        el = _max_over_ranks(time.perf_counter() - t0, world, dev)
+        e2e = {"value": total * n_e2e / el, "unit": "rows/s",
+               "h2d_bytes_per_step": int(h_np.nbytes + h_params.nbytes + h_hist.nbytes + h_hoff.nbytes + h_u.nbytes),
+               "d2h_bytes_per_step": int(h_tok.nbytes + h_st.nbytes)}
+        del h_logits
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        base, lg, us = make_batches(1000)
+        v, kind, threads, sample = cpu_reference_rows_per_s(base, lg, us, args.cpu_budget)
+        cpu = {"value": v, "unit": "rows/s", "cores": threads, "kind": kind,
+               "sample": sample + "; config-2 batches (the same parameter mix)"}
+    if world > 1:
+        del graph
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        line = {
+            "metric": "sampled rows/s, 8,192 rows x V=151,936 fp32 partitioned over N GPUs (config 5)",
+            "value": value, "unit": "rows/s", "tokens_per_s": value, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic; logits drawn on the device (N(0, 2.5^2), 16 ids per row +8), config-2 mix",
+            "config": {"workload": "config5 rows partitioned", "rows_total": total, "rows_per_gpu": R,
+                       "vocab": VOCAB, "parallelism": f"rows partitioned, {world} GPU(s), no collective",
+                       "l2": f"inputs larger than L2: {R * VOCAB * 4 / 1e6:.0f} MB of logits per GPU"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+                         "bytes_per_launch": int(nbytes)},
+            "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": args.steps, "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    smp.close()
+    return 0
+
+
+def run_config5_sharded(args) -> int:
+    """BASELINE config 5, vocab-sharded variant: B = 256 rows whose vocabulary is split into equal
+    slices (8 on one GPU, emulated as 8 slices of the rows; one per rank on N > 1 GPUs). A step is
+    stage 1 on each slice (per-slice top-64 candidates and softmax statistics), the exchange
+    (NCCL all-gather over NVLink on N > 1; a stack of the slices' outputs on one GPU), stage 2 (the
+    merge, identical on every rank) and round 2 for the rows the merge cannot certify. CUDA events
+    split each step into those four parts; the reported time is their sum, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import sixi_smp as S
+    from sixi_smp import workloads as W
+    from sixi_smp.sharded import ShardLayout, sample_vocab_sharded
+
+    rank, world, local = dist_env()
+    dev = _init_dist(local, world)
+    B, top_n = 256, 64
+    n_shards = 8 if world == 1 else world
+    lay = ShardLayout(VOCAB, n_shards)
+    mix = W.config2_mix(B, VOCAB, seed=6)
+    full = W.config2_logits_device(B, VOCAB, seed=6000, device=dev)
+    params = torch.from_numpy(mix["params"].view(np.uint8)).to(dev)
+    hist, hoff = torch.from_numpy(mix["hist"]).to(dev), torch.from_numpy(mix["hist_off"]).to(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(99)
+    u = torch.rand(B, dtype=torch.float64, device=dev, generator=g)
+    smp = S.Sampler(local, 4096, VOCAB)
+    stream = torch.cuda.Stream(device=dev)
+    parts = ("stage1", "exchange", "stage2", "round2")
+    if world > 1:
+        mine = full[:, lay.offset(rank):lay.offset(rank) + lay.width(rank)].contiguous()
+        del full
+    else:
+        slices = [full[:, lay.offset(r):lay.offset(r) + lay.width(r)].contiguous() for r in range(n_shards)]
+
+    def one_step(i, ev):
+        def mark(name):
+            ev[name].record(torch.cuda.current_stream())
+
+        if world > 1:
+            return sample_vocab_sharded(mine, lay, rank, params, top_n=top_n, hist=hist, hist_off=hoff, uniforms=u,
+                                        step=i, sampler=smp, stream=torch.cuda.current_stream(), mark=mark)
+        cs = torch.cuda.current_stream()
+        cands, stats = [], []
+        for r in range(n_shards):
+            c, s = smp.shard_candidates(slices[r], lay.offset(r), lay.width(r), params, top_n=top_n, hist=hist,
+                                        hist_off=hoff, stream=cs)
+            cands.append(c)
+            stats.append(s)
+        mark("stage1")
+        gc, gs = torch.stack(cands), torch.stack(stats)
+        mark("exchange")
+        tok, sts = smp.merge_shards(gc, gs, params, uniforms=u, step=i, stream=cs)
+        mark("stage2")
+        rows = (sts == 2).nonzero().flatten()
+        if rows.numel():
+            fr = torch.cat(slices, dim=1)[rows].contiguous()
+            p = params.view(B, -1)[rows].contiguous()
+            from sixi_smp.sharded import _subset_csr
+
+            h, ho = _subset_csr(hist, hoff, rows)
+            t2, s2 = smp.sample(fr, p, hist=h, hist_off=ho, uniforms=u[rows].contiguous(), step=i, stream=cs)
+            tok[rows] = t2
+            sts[rows] = s2
+        mark("round2")
+        return tok, sts
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            ev = {k: torch.cuda.Event(enable_timing=True) for k in ("start",) + parts}
+            ev["start"].record(stream)
+            tok, sts = one_step(i, ev)
+    stream.synchronize()
+    n_round2 = int((sts == 2).sum())  # should be 0 after round 2
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.05)
+    evs = []
+    flagged = []
+    with torch.cuda.stream(stream):
+        for i in range(args.steps):
+            ev = {k: torch.cuda.Event(enable_timing=True) for k in ("start",) + parts}
+            ev["start"].record(stream)
+            tok, sts = one_step(i, ev)
+            evs.append(ev)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    split = {k: 0.0 for k in parts}
+    for ev in evs:
+        prev = ev["start"]
+        for k in parts:
+            split[k] += prev.elapsed_time(ev[k])
+            prev = ev[k]
+    split = {k: v / args.steps for k, v in split.items()}
+    ms_step = sum(split.values())
+    ms_max = _max_over_ranks(ms_step, world, dev)
+    # rows the merge sent to round 2 in the last step (recounted without round 2)
+    with torch.cuda.stream(stream):
+        ev = {k: torch.cuda.Event(enable_timing=True) for k in ("start",) + parts}
+        if world > 1:
+            c, s = smp.shard_candidates(mine, lay.offset(rank), lay.width(rank), params, top_n=top_n, hist=hist,
+                                        hist_off=hoff, stream=stream)
+            gc = torch.empty((world,) + tuple(c.shape), dtype=c.dtype, device=dev)
+            gs = torch.empty((world,) + tuple(s.shape), dtype=s.dtype, device=dev)
+            dist.all_gather_into_tensor(gc.view(-1, *c.shape[1:]), c)
+            dist.all_gather_into_tensor(gs.view(-1, *s.shape[1:]), s)
+        else:
+            cs_ = [smp.shard_candidates(slices[r], lay.offset(r), lay.width(r), params, top_n=top_n, hist=hist,
+                                        hist_off=hoff, stream=stream) for r in range(n_shards)]
+            gc, gs = torch.stack([c for c, _ in cs_]), torch.stack([s for _, s in cs_])
+        _, s1 = smp.merge_shards(gc, gs, params, uniforms=u, stream=stream)
+    stream.synchronize()
+    flagged = int((s1 == 2).sum())
+    payload = int(gc[0].numel() * gc.element_size() + gs[0].numel() * gs.element_size())
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        w = lay.width(0)
+        nbytes = B * w * 4 + 4 * int(mix["hist_off"][-1])
+        line = {
+            "metric": "vocab-sharded sampled rows/s, B=256, V=151,936 fp32 split into equal slices (config 5)",
+            "value": B / (ms_max / 1e3), "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic; config-2 mix, logits drawn on the device",
+            "config": {"workload": "config5 vocab-sharded", "rows": B, "vocab": VOCAB, "slices": n_shards,
+                       "top_n": top_n, "parallelism": (f"vocab-sharded over {world} GPUs, NCCL all-gather" if world > 1
+                                                       else "8 slices emulated on 1 GPU, no collective")},
+            "split_ms_per_step": split, "rows_to_round2_per_step": flagged,
+            "exchange_payload_bytes_per_rank": payload, "unresolved_after_round2": n_round2,
+            "roofline": {"bound": "hbm", "achieved": nbytes / (ms_step / 1e3) / 1e9 if world > 1 else
+                         n_shards * nbytes / (ms_step / 1e3) / 1e9, "unit": "GB/s",
+                         "note": "stage-1 bytes of this rank's slice (all slices on 1 GPU) over the whole step"},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
     smp.close()
     return 0
 
@@ -540,12 +862,19 @@ def main() -> int:
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload", default="config2", choices=["config2", "config1", "config3", "config4", "config4f",
-                                                                 "grammar", "numeric", "drafter"],
-                    help="config2 is the headline line; the others are reported beside it (1 GPU)")
+                                                                 "config5", "config5s", "grammar", "numeric",
+                                                                 "drafter"],
+                    help="config2 is the headline line; the others are reported beside it (config5 and config5s "
+                         "also under torchrun on N GPUs)")
+    ap.add_argument("--rows", type=int, default=8192, help="config5: total rows over all ranks")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "config5":
+        return run_config5(args)
+    if args.workload == "config5s":
+        return run_config5_sharded(args)
     if args.workload != "config2":
         return run_workload(args)
 

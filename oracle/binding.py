@@ -39,6 +39,12 @@ _SIGS = {
     "orc_suffix_draft": (_I32, [_P, _U64, _U32, _U32, _I32, _I32, _U32, _P]),
     "orc_verify": (_I32, [_P, _U32, _U64, _U64, _P, _P, _P, _U32, _U32, _P, _P, _P, _P, _P, _U64,
                           _P, _P, _P, _P, _P, _P, _I32]),
+    # the engine's own SpeculativeDecoder::step and DeterministicRng (reference build only)
+    "orc_ref_rng_uniform": (ctypes.c_double, [_P]),
+    "orc_ref_rng_seed": (None, [_U64, _U64, _P]),
+    "orc_ref_spec_step": (_I32, [_I32, _P, _P, _U64, _P, _P, _U32, _P, _P, _U64, _P, _P, _P, _P, _P]),
+    "orc_ref_spec_step_batch": (_I32, [_P, _U32, _U64, _P, _P, _U32, _U32, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                       _I32]),
     # JSON-object grammar automaton (sixi_json_oracle.c)
     "orc_json_feed": (_I32, [_P, _P, _U64]),
     "orc_json_fill_masks": (None, [_P, _P, _P, _U32, _I32, _P, _U32, _P, _U64, _I32]),
@@ -72,6 +78,8 @@ class Oracle:
         for name, (res, args) in _SIGS.items():
             if name.startswith("orc_json_") and not hasattr(self.lib, name):
                 continue  # the grammar automaton exists only in the port (the engine's is binary-only)
+            if name.startswith("orc_ref_") and not hasattr(self.lib, name):
+                continue  # the engine's decoder and RNG exist only in the reference build
             fn = getattr(self.lib, name)
             fn.restype = res
             fn.argtypes = args
@@ -93,6 +101,50 @@ class Oracle:
         m = self.lib.orc_suffix_draft(_p(h), h.size, min_match_len, max_window_tokens, 0 if anchor is None else 1,
                                       0 if anchor is None else int(anchor), k, _p(out))
         return int(m), out[:k]
+
+    # -- the engine's SpeculativeDecoder::step (reference build) ------------------------------------
+    def rng_seed(self, seed: int, seq: int = 54) -> np.ndarray:
+        """(state, inc) of the engine's DeterministicRng(seed, seq)."""
+        st = np.zeros(2, dtype=np.uint64)
+        self.lib.orc_ref_rng_seed(seed, seq, _p(st))
+        return st
+
+    def rng_uniforms(self, state: np.ndarray, n: int) -> np.ndarray:
+        """n uniforms of the engine's RNG from `state` (advanced in place)."""
+        return np.array([self.lib.orc_ref_rng_uniform(_p(state)) for _ in range(n)])
+
+    def spec_step(self, rows: np.ndarray, drafts: np.ndarray, params: np.ndarray, hist=None, draft_probs=None,
+                  rng_state=None, fast: bool = False, anchor_row=None) -> dict:
+        """One SpeculativeDecoder::step of the engine (slow path; fast path with `fast`, see
+        orc_ref_spec_step) on fp32 rows [k+1, V]. `rng_state` (state, inc) is advanced in place."""
+        rows = np.ascontiguousarray(rows, dtype=np.float32)
+        d = np.ascontiguousarray(drafts, dtype=np.int32)
+        k, v = d.size, rows.shape[1]
+        q = None if draft_probs is None else np.ascontiguousarray(draft_probs, dtype=np.float32)
+        h = None if hist is None else np.ascontiguousarray(hist, dtype=np.int32)
+        a = None if anchor_row is None else np.ascontiguousarray(anchor_row, dtype=np.float32)
+        st = self.rng_seed(1) if rng_state is None else rng_state
+        toks = np.full(k + 2, -1, dtype=np.int32)
+        n, acc, fr = (np.zeros(1, dtype=np.int32) for _ in range(3))
+        rc = self.lib.orc_ref_spec_step(1 if fast else 0, _p(a), _p(rows), v, _p(q), _p(d), k, _p(params), _p(h),
+                                        0 if h is None else h.size, _p(st), _p(toks), _p(n), _p(acc), _p(fr))
+        return dict(status=int(rc), tokens=toks[:int(n[0])].copy(), accepted=int(acc[0]), first_reject=int(fr[0]),
+                    rng=st.copy())
+
+    def spec_step_batch(self, rows: np.ndarray, drafts: np.ndarray, params: np.ndarray, hist, hist_off,
+                        draft_probs, rng_states: np.ndarray, n_threads: int = 0) -> dict:
+        """The slow-path step for S streams: rows [S*(k+1), V] (fp32 or bf16 bits), drafts [S, k],
+        draft_probs [S*k, V]; rng_states [S, 2] advanced in place."""
+        rows = np.ascontiguousarray(rows)
+        S, k = drafts.shape
+        v = rows.shape[1]
+        toks = np.full((S, k + 2), -1, dtype=np.int32)
+        n, acc, fr, sts = (np.zeros(S, dtype=np.int32) for _ in range(4))
+        self.lib.orc_ref_spec_step_batch(_p(rows), _dtype_of(rows), v, _p(draft_probs),
+                                         _p(np.ascontiguousarray(drafts, dtype=np.int32)), S, k, _p(params),
+                                         _p(hist), _p(hist_off), _p(rng_states), _p(toks), _p(n), _p(acc), _p(fr),
+                                         _p(sts), n_threads)
+        return dict(tokens=toks, n_tokens=n, accepted=acc, first_reject=fr, status=sts)
 
     def philox_uniform(self, seed: int, counter: int, slot: int) -> float:
         return float(self.lib.orc_philox_uniform(seed, counter, slot))

@@ -10,7 +10,12 @@
 //     (src/core/core_execution.cpp:586-601), since the engine draws from its own PCG32 stream;
 //   - verification restates SpeculativeDecoder::step's accept/residual/bonus logic
 //     (src/speculative/speculative.cpp:630-692 one-hot, :801-916 dense q) around the engine's
-//     compute_sampling_candidates, taking the uniforms from the supplied slots.
+//     compute_sampling_candidates, taking the uniforms from the supplied slots;
+//   - orc_ref_spec_step runs the engine's real SpeculativeDecoder::step with its own
+//     DeterministicRng, through a replay IBackend (pre-supplied target rows) and a fixed-draft
+//     INeuralDrafter: the slow path (no rollback ring, dense draft probs, :739-976) or the fast
+//     path (O(1) rollback, one-hot drafts after a sampled anchor, :471-737). It pins the restated
+//     verifier and the C++ adapter's RNG contract, and times config 4 on the host cores.
 // Inputs the engine cannot express (min_p, frequency penalty) return ORC_UNSUPPORTED.
 #include "sixi_asi/core_execution.hpp"
 #include "sixi_asi/numeric.hpp"
@@ -31,6 +36,13 @@ using sixi_asi::ExecutionMode;
 using sixi_asi::core::DeterministicSampler;
 using sixi_asi::core::SamplingParams;
 using Cand = DeterministicSampler::Candidate;
+using sixi_asi::Result;
+using sixi_asi::Status;
+using sixi_asi::core::BackendSequenceState;
+using sixi_asi::core::DeterministicRng;
+using sixi_asi::core::IBackend;
+using sixi_asi::core::RngState;
+namespace spec = sixi_asi::speculative;
 
 #define EXPORT extern "C" __attribute__((visibility("default")))
 
@@ -440,6 +452,211 @@ EXPORT int32_t orc_verify(const void* target, uint32_t dtype, uint64_t row_strid
         out_first_reject[s] = first_reject;
         out_uniforms_used[s] = static_cast<int32_t>(used);
         out_status[s] = status;
+    });
+    return SIXI_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
+// The engine's SpeculativeDecoder::step over pre-supplied rows
+
+namespace {
+
+// An IBackend that replays target logits: forward_sequence_all_logits returns the supplied rows
+// (rows 1..k on the slow path, where the caller's current_last_logits is row 0; rows 0..k on the
+// fast path, after the anchor's row). Other forwards return a zero row; the state it checkpoints
+// is the RNG's, as a real backend's checkpoint carries it (core_execution.hpp:184-190).
+class ReplayBackend final : public IBackend {
+public:
+    ReplayBackend(const float* rows, uint32_t n_rows, uint64_t vocab, bool fast, uint32_t window)
+        : rows_(rows), n_rows_(n_rows), vocab_(vocab), fast_(fast), window_(window) {}
+    std::string backend_name() const override { return "replay"; }
+    uint64_t vocab_size() const override { return vocab_; }
+    int32_t eos_token_id() const override { return -1; }
+    Result<std::vector<int32_t>> tokenize(const std::string&, bool) override {
+        return Result<std::vector<int32_t>>(ErrorCode::BackendError, "replay backend has no tokenizer");
+    }
+    Result<std::string> detokenize(const std::vector<int32_t>&) override {
+        return Result<std::string>(ErrorCode::BackendError, "replay backend has no tokenizer");
+    }
+    Status reset_state() override { return Status::Ok(); }
+    Result<BackendSequenceState> checkpoint_state(const DeterministicRng& rng) override {
+        BackendSequenceState st;
+        st.seq_len = seq_len_;
+        st.rng_state = rng.checkpoint();
+        return Result<BackendSequenceState>(std::move(st));
+    }
+    Status restore_state(const BackendSequenceState& ck, DeterministicRng& rng) override {
+        seq_len_ = ck.seq_len;
+        rng.restore(ck.rng_state);
+        return Status::Ok();
+    }
+    Result<std::vector<float>> forward_tokens(const std::vector<int32_t>& t, uint32_t) override {
+        seq_len_ += t.size();
+        return Result<std::vector<float>>(std::vector<float>(vocab_, 0.0f));
+    }
+    Result<std::vector<std::vector<float>>> forward_sequence_all_logits(const std::vector<int32_t>& t) override {
+        using R = Result<std::vector<std::vector<float>>>;
+        const uint32_t first = fast_ ? 0u : 1u;
+        if (first + t.size() > n_rows_) return R(ErrorCode::BackendError, "replay backend: too few rows");
+        std::vector<std::vector<float>> out;
+        for (size_t i = 0; i < t.size(); ++i) {
+            const float* r = rows_ + (first + i) * vocab_;
+            out.emplace_back(r, r + vocab_);
+        }
+        seq_len_ += t.size();
+        return R(std::move(out));
+    }
+    bool supports_fast_prefix_rollback() const noexcept override { return fast_; }
+    uint32_t fast_rollback_window() const noexcept override { return fast_ ? window_ : 0u; }
+    uint64_t current_seq_len() const noexcept override { return seq_len_; }
+    Status rollback_to_position(uint64_t n) override {
+        if (!fast_) return Status::Error(ErrorCode::BackendError, "no rollback ring");
+        seq_len_ = n;
+        return Status::Ok();
+    }
+
+private:
+    const float* rows_;
+    uint32_t n_rows_;
+    uint64_t vocab_;
+    bool fast_;
+    uint32_t window_;
+    uint64_t seq_len_ = 1000;
+};
+
+// An INeuralDrafter that proposes the given drafts, with dense draft probabilities when given.
+class FixedDrafter final : public spec::INeuralDrafter {
+public:
+    FixedDrafter(const int32_t* drafts, uint32_t k, const float* q, uint64_t vocab) {
+        p_.source = spec::DraftSource::NeuralMTP;
+        p_.draft_tokens.assign(drafts, drafts + k);
+        if (q != nullptr)
+            for (uint32_t i = 0; i < k; ++i) p_.draft_probs.emplace_back(q + i * vocab, q + (i + 1) * vocab);
+    }
+    sixi_asi::NeuralDrafterType drafter_type() const noexcept override { return sixi_asi::NeuralDrafterType::MTP; }
+    std::string drafter_name() const override { return "fixed"; }
+    Result<spec::DraftProposal> propose_k(const std::vector<int32_t>&, const std::vector<float>&, uint32_t) override {
+        return Result<spec::DraftProposal>(p_);
+    }
+
+private:
+    spec::DraftProposal p_;
+};
+
+int32_t spec_step(int32_t fast, const float* anchor_row, const float* rows, uint64_t vocab, const float* draft_probs,
+                  const int32_t* drafts, uint32_t k, const sixi_smp_params* p, const int32_t* hist, uint64_t n_hist,
+                  uint64_t* rng_io, int32_t* out_tokens, int32_t* out_n, int32_t* out_accepted,
+                  int32_t* out_first_reject) {
+    *out_n = 0;
+    *out_accepted = 0;
+    *out_first_reject = -1;
+    if (!expressible(p) || k == 0) return ORC_UNSUPPORTED;
+    spec::SpeculativeConfig cfg;
+    cfg.execution_mode = p->mode == SIXI_SMP_ADAPTIVE ? ExecutionMode::Adaptive : ExecutionMode::StrictReplay;
+    cfg.enable_suffix_drafter = false;
+    cfg.neural_drafter = sixi_asi::NeuralDrafterType::MTP;
+    cfg.draft_k = k;
+    cfg.adaptive_k = false;
+    cfg.min_adaptive_k = 1;
+    cfg.max_adaptive_k = k;
+    auto backend = std::make_shared<ReplayBackend>(rows, k + 1, vocab, fast != 0, k);
+    auto drafter = std::make_shared<FixedDrafter>(drafts, k, fast ? nullptr : draft_probs, vocab);
+    spec::SpeculativeDecoder dec(cfg, backend, drafter);
+    std::vector<int32_t> ctx(hist, hist + n_hist);
+    const float* first = fast ? anchor_row : rows;
+    std::vector<float> last(first, first + vocab);
+    DeterministicRng rng;
+    rng.restore(RngState{rng_io[0], rng_io[1]});
+    const SamplingParams sp = to_engine(p);
+    auto r = dec.step(ctx, last, sp, rng);
+    if (!r.ok()) return static_cast<int32_t>(r.code());
+    const auto& res = r.value();
+    std::vector<int32_t> toks = res.committed_tokens;
+    if (fast) {
+        // the fast path keeps the token after the last committed one for the next step: carried for
+        // sampling, the argmax of the returned logits for greedy (speculative.cpp:704-714)
+        if (sp.temperature > 0.0f) {
+            const auto c = dec.carried_token(ctx);
+            toks.push_back(c.has_value() ? *c : -1);
+        } else {
+            toks.push_back(DeterministicSampler::sample_greedy_argmax(last.data(), vocab));
+        }
+    }
+    for (size_t i = 0; i < toks.size(); ++i) out_tokens[i] = toks[i];
+    *out_n = static_cast<int32_t>(toks.size());
+    *out_accepted = static_cast<int32_t>(res.accepted_draft_count);
+    *out_first_reject = res.first_rejected_position;
+    const RngState after = rng.checkpoint();
+    rng_io[0] = after.state;
+    rng_io[1] = after.inc;
+    return SIXI_OK;
+}
+
+}  // namespace
+
+// One uniform of the engine's DeterministicRng from the state (state, inc) in rng_io, which is
+// advanced in place (core_execution.cpp:33-61).
+EXPORT double orc_ref_rng_uniform(uint64_t* rng_io) {
+    DeterministicRng rng;
+    rng.restore(RngState{rng_io[0], rng_io[1]});
+    const double u = rng.next_uniform01();
+    const RngState after = rng.checkpoint();
+    rng_io[0] = after.state;
+    rng_io[1] = after.inc;
+    return u;
+}
+
+// The engine's seeded RNG state: DeterministicRng(seed, seq).
+EXPORT void orc_ref_rng_seed(uint64_t seed, uint64_t seq, uint64_t* rng_out) {
+    const DeterministicRng rng(seed, seq);
+    const RngState st = rng.checkpoint();
+    rng_out[0] = st.state;
+    rng_out[1] = st.inc;
+}
+
+// One SpeculativeDecoder::step (speculative.cpp:367-976) of one stream with fp32 rows.
+//   fast = 0: slow path. rows [k+1][V]: row 0 is current_last_logits, rows 1..k are returned by
+//             forward_sequence_all_logits(drafts); draft_probs [k][V] (dense q) or NULL.
+//             out_tokens = committed_tokens (accepted drafts, then the replacement or the bonus).
+//   fast = 1: fast path. anchor_row is current_last_logits (the anchor is drawn from it), rows
+//             [k+1][V] are the verify batch after the anchor; drafts are one-hot proposals.
+//             out_tokens = committed_tokens (anchor, accepted drafts), then the token the step
+//             determined for the next position (replacement or bonus).
+// rng_io = the engine RNG's (state, inc) before the step, replaced by the state after it.
+// out_tokens needs k + 2 slots. Returns the step's ErrorCode.
+EXPORT int32_t orc_ref_spec_step(int32_t fast, const float* anchor_row, const float* rows, uint64_t vocab,
+                                 const float* draft_probs, const int32_t* drafts, uint32_t k, const sixi_smp_params* p,
+                                 const int32_t* hist, uint64_t n_hist, uint64_t* rng_io, int32_t* out_tokens,
+                                 int32_t* out_n, int32_t* out_accepted, int32_t* out_first_reject) {
+    return spec_step(fast, anchor_row, rows, vocab, draft_probs, drafts, k, p, hist, n_hist, rng_io, out_tokens,
+                     out_n, out_accepted, out_first_reject);
+}
+
+// The slow-path step for S streams (config 4 on the host cores): target rows [S][k+1][V] (fp32,
+// or bf16 converted by the engine's bf16_to_fp32), q [S][k][V], drafts [S][k], one RNG state per
+// stream (rng_io [S][2], advanced in place), out_tokens [S][k+2]; statuses in out_status.
+EXPORT int32_t orc_ref_spec_step_batch(const void* rows, uint32_t dtype, uint64_t vocab, const float* draft_probs,
+                                       const int32_t* drafts, uint32_t n_streams, uint32_t k,
+                                       const sixi_smp_params* params, const int32_t* hist_tokens,
+                                       const int64_t* hist_offsets, uint64_t* rng_io, int32_t* out_tokens,
+                                       int32_t* out_n, int32_t* out_accepted, int32_t* out_first_reject,
+                                       int32_t* out_status, int32_t n_threads) {
+    const size_t esz = dtype == SIXI_SMP_BF16 ? 2 : 4;
+    parallel_for(n_streams, n_threads, [&](uint32_t s) {
+        std::vector<float> x;
+        std::vector<float> tr(static_cast<size_t>(k + 1) * vocab);
+        for (uint32_t i = 0; i <= k; ++i) {
+            load_row(static_cast<const char*>(rows) + (static_cast<size_t>(s) * (k + 1) + i) * vocab * esz, dtype,
+                     vocab, x);
+            std::copy(x.begin(), x.end(), tr.begin() + static_cast<size_t>(i) * vocab);
+        }
+        const int32_t* h = hist_tokens ? hist_tokens + hist_offsets[s] : nullptr;
+        const uint64_t nh = hist_tokens ? static_cast<uint64_t>(hist_offsets[s + 1] - hist_offsets[s]) : 0;
+        out_status[s] = spec_step(0, nullptr, tr.data(), vocab,
+                                  draft_probs ? draft_probs + static_cast<size_t>(s) * k * vocab : nullptr,
+                                  drafts + static_cast<size_t>(s) * k, k, &params[s], h, nh, rng_io + 2 * s,
+                                  out_tokens + static_cast<size_t>(s) * (k + 2), &out_n[s], &out_accepted[s],
+                                  &out_first_reject[s]);
     });
     return SIXI_OK;
 }

@@ -60,12 +60,14 @@ def _subset_csr(hist, hist_off, rows):
 def sample_vocab_sharded(shard_logits, layout: ShardLayout, rank: int, params, *, top_n: int = 64,
                          masks=None, hist=None, hist_off=None, uniforms=None, step: int = 0,
                          stage1: Callable | None = None, stage2: Callable | None = None,
-                         full_rows: Callable | None = None, group=None, sampler=None, stream=None):
+                         full_rows: Callable | None = None, group=None, sampler=None, stream=None,
+                         mark: Callable | None = None):
     """One sharded sampling step on this rank. `shard_logits` are this rank's columns
     [n_rows, width(rank)] (a view into wider rows is fine). Returns (tokens, statuses).
     `full_rows(logits, rows)` samples rebuilt full rows `rows` (round 2); by default
     sixi_smp_sample on this rank's sampler with the rows' parameters, masks, histories and
-    uniforms."""
+    uniforms. `mark(name)`, when given, is called after stage 1, the exchange, stage 2 and round 2
+    (a timer records a CUDA event there)."""
     import torch
     import torch.distributed as dist
 
@@ -85,7 +87,11 @@ def sample_vocab_sharded(shard_logits, layout: ShardLayout, rank: int, params, *
         def stage2(gc, gs):
             return sampler.merge_shards(gc, gs, params, uniforms=uniforms, step=step, stream=stream)
 
+    if mark is None:
+        def mark(name):
+            return None
     cand, stats = stage1(shard_logits, layout.offset(rank), layout.width(rank))
+    mark("stage1")
     world = layout.n_shards
     # gathered along dim 0 (rank-major), then viewed as [world, n_rows, ...]
     g_cand = torch.empty((world * cand.shape[0],) + tuple(cand.shape[1:]), dtype=cand.dtype, device=cand.device)
@@ -93,7 +99,9 @@ def sample_vocab_sharded(shard_logits, layout: ShardLayout, rank: int, params, *
                           device=stats.device)
     dist.all_gather_into_tensor(g_cand, cand.contiguous(), group=group)
     dist.all_gather_into_tensor(g_stats, stats.contiguous(), group=group)
+    mark("exchange")
     tok, sts = stage2(g_cand.view((world,) + tuple(cand.shape)), g_stats.view((world,) + tuple(stats.shape)))
+    mark("stage2")
     # round 2: the rows stage 2 could not certify, sampled from their rebuilt full rows
     rows = (sts == OUT_OF_BOUNDS).nonzero().flatten()
     n_f = int(rows.numel())
@@ -110,4 +118,5 @@ def sample_vocab_sharded(shard_logits, layout: ShardLayout, rank: int, params, *
         sts = sts.clone()
         tok[rows] = t2.to(tok.device)
         sts[rows] = s2.to(sts.device)
+    mark("round2")
     return tok, sts

@@ -93,6 +93,44 @@ def config2(rows: int = 32, vocab: int = QWEN_VOCAB, seed: int = 2, hist_lo: int
     return dict(logits=logits, params=params, hist=hist, hist_off=off, masks=None)
 
 
+def config2_mix(rows: int, vocab: int = QWEN_VOCAB, seed: int = 5, hist_lo: int = 256,
+                hist_hi: int = 8192) -> dict:
+    """The config-2 parameter mix and histories for `rows` rows, without logits (config 5 draws
+    its 8,192 rows of logits on the device: 4.98 GB do not belong in host memory)."""
+    rng = np.random.default_rng(seed)
+    t = rng.uniform(0.3, 1.2, size=rows).astype(np.float32)
+    t[rng.random(rows) < 0.25] = 0.0
+    params = make_params(
+        rows,
+        temperature=t,
+        top_k=rng.choice(np.array([0, 20, 40, 100], dtype=np.int32), size=rows),
+        top_p=rng.uniform(0.7, 1.0, size=rows).astype(np.float32),
+        repetition_penalty=rng.uniform(1.0, 1.3, size=rows).astype(np.float32),
+        mode=ADAPTIVE,
+        seed=rng.integers(0, 2**63, size=rows, dtype=np.uint64),
+    )
+    lens = rng.integers(hist_lo, hist_hi + 1, size=rows)
+    off = np.zeros(rows + 1, dtype=np.int64)
+    off[1:] = np.cumsum(lens)
+    hist = rng.integers(0, vocab, size=int(off[-1]), dtype=np.int32)
+    return dict(params=params, hist=hist, hist_off=off, masks=None)
+
+
+def config2_logits_device(rows: int, vocab: int, seed: int, device):
+    """Config-2 logits drawn on the device: N(0, 2.5^2) with 16 distinct ids per row boosted by +8
+    (ids base + j * stride mod V with stride < V / 16, so the 16 are distinct)."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    x = torch.randn((rows, vocab), generator=g, device=device, dtype=torch.float32).mul_(2.5)
+    base = torch.randint(0, vocab, (rows, 1), generator=g, device=device)
+    stride = torch.randint(1, max(2, vocab // 16), (rows, 1), generator=g, device=device)
+    ids = (base + stride * torch.arange(16, device=device)) % vocab
+    x.scatter_add_(1, ids, torch.full(ids.shape, 8.0, device=device))
+    return x
+
+
 def boost_rows(rng: np.random.Generator, logits: np.ndarray, n: int = 16, by: float = 8.0) -> np.ndarray:
     """Adds `by` to `n` distinct random ids of every row (the boosted tokens of configs 1 and 2)."""
     vocab = logits.shape[1]

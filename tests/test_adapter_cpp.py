@@ -1,8 +1,10 @@
-"""The C++ host adapter (sixi-asi_b200/host/sixi_sampler.hpp) and its C++ parity test.
+"""The C++ host adapter (sixi-asi_b200/host/sixi_sampler.hpp) and its C++ parity tests.
 
-On CPU the test program is compiled (not linked), which checks that the header-only adapter
-builds against the C ABI header. On a GPU it is linked against libsixi_smp.so and the oracle port
-and run: every check of tests/cpp/test_adapter.cpp must pass.
+On CPU the test programs are compiled (not linked), which checks that the header-only adapter
+builds against the C ABI header. On a GPU they are linked and run, and every check must pass:
+  tests/cpp/test_adapter.cpp    against the oracle port (liboracle.so)
+  tests/cpp/test_spec_step.cpp  verify() against the engine's own SpeculativeDecoder::step, run by
+                                the reference build (oracle/_ref/libsixiref.so) with the engine's RNG
 """
 
 from __future__ import annotations
@@ -17,13 +19,15 @@ from conftest import REPO, has_gpu
 
 CUDA = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 SRC = REPO / "tests" / "cpp" / "test_adapter.cpp"
+SRC_STEP = REPO / "tests" / "cpp" / "test_spec_step.cpp"
 INC = ["-I", str(REPO / "include"), "-I", str(REPO / "sixi-asi_b200" / "host"), "-I", str(CUDA / "include")]
 CXX = ["g++", "-std=c++17", "-O2", "-Wall", "-Wextra"]
 
 
-def test_adapter_compiles(tmp_path):
-    obj = tmp_path / "test_adapter.o"
-    r = subprocess.run([*CXX, *INC, "-c", str(SRC), "-o", str(obj)], capture_output=True, text=True)
+@pytest.mark.parametrize("src", [SRC, SRC_STEP], ids=["adapter", "spec_step"])
+def test_adapter_compiles(tmp_path, src):
+    obj = tmp_path / (src.stem + ".o")
+    r = subprocess.run([*CXX, *INC, "-c", str(src), "-o", str(obj)], capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     assert "warning" not in r.stderr, r.stderr
 
@@ -47,5 +51,30 @@ def test_adapter_parity_on_gpu(tmp_path):
     r = subprocess.run(cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=600)
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
+@pytest.mark.gpu
+def test_adapter_verify_equals_engine_step_on_gpu(tmp_path):
+    if not has_gpu():
+        pytest.skip("no CUDA device")
+    import sixi_smp
+    from oracle import binding
+
+    lib = Path(sixi_smp.LIB_PATH)
+    assert lib.exists(), "libsixi_smp.so not built"
+    ref = binding.REF_PATH
+    if not ref.exists():
+        pytest.skip("reference build (oracle/_ref) absent")
+    exe = tmp_path / "test_spec_step"
+    libdirs = [lib.parent, ref.parent, CUDA / "lib64"]
+    cmd = [*CXX, *INC, str(SRC_STEP), "-o", str(exe)]
+    for d in libdirs:
+        cmd += ["-L", str(d), f"-Wl,-rpath,{d}"]
+    cmd += ["-lsixi_smp", "-lsixiref", "-lcudart"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=900)
     print(r.stdout)
     assert r.returncode == 0, r.stdout + r.stderr

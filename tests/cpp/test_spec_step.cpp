@@ -175,13 +175,21 @@ bool fast_path(DeviceSampler& dev, const Stream& s, uint64_t seed) {
     const EngineOut e = engine_step(s, true, nullptr, seed);
     CHECK(e.status == 0);
     EngineRng rng(seed);
-    auto a = dev.sample_token(s.anchor.data(), s.V, s.p, rng, s.hist);
-    CHECK(a.ok());
+    // the anchor: a sampled token, or for greedy the raw argmax without penalties
+    // (speculative.cpp:480-490)
+    int32_t anchor = -1;
+    if (s.p.temperature <= 0.0f) {
+        anchor = dev.sample_greedy_argmax(s.anchor.data(), s.V);
+    } else {
+        auto a = dev.sample_token(s.anchor.data(), s.V, s.p, rng, s.hist);
+        CHECK(a.ok());
+        anchor = a.value();
+    }
     std::vector<int32_t> h2 = s.hist;
-    h2.push_back(a.value());
+    h2.push_back(anchor);
     auto r = dev.verify(s.rows.data(), nullptr, s.drafts, s.p, rng, h2);
     CHECK(r.ok());
-    std::vector<int32_t> mine{a.value()};
+    std::vector<int32_t> mine{anchor};
     mine.insert(mine.end(), r.value().committed_tokens.begin(), r.value().committed_tokens.end());
     CHECK(mine == e.tokens);
     CHECK(static_cast<int32_t>(r.value().accepted_draft_count) == e.accepted);
@@ -243,8 +251,13 @@ int main() {
             for (bool greedy : {false, true}) {
                 const uint64_t seed = V * 31 + static_cast<uint64_t>(i) * 2 + (greedy ? 1 : 0);
                 const Stream s = make_stream(V, k, seed, greedy);
+                const int before = g_fail;
                 slow_path(dev, s, seed + 7);
                 fast_path(dev, s, seed + 9);
+                if (g_fail != before)
+                    std::fprintf(stderr, "  case V=%llu seed=%llu greedy=%d T=%.3f top_k=%d top_p=%.3f\n",
+                                 static_cast<unsigned long long>(V), static_cast<unsigned long long>(seed),
+                                 greedy ? 1 : 0, s.p.temperature, s.p.top_k, s.p.top_p);
                 cases += 2;
             }
         }

@@ -77,7 +77,7 @@ bool rows_ok(const sixi_smp* h, const sixi_smp_rows* rows) {
 RowArgs base_args(const sixi_smp* h, const sixi_smp_rows* rows, LaunchPlan* plan) {
     RowArgs a;
     std::memset(&a, 0, sizeof(a));
-    sixi_b200::plan_rows(h->vocab, rows->n_rows, plan);
+    sixi_b200::plan_rows(h->vocab, rows->n_rows, sixi_b200::device_sm_count(h->device), plan);
     a.data = rows->data;
     a.row_stride = rows->row_stride;
     a.dtype = rows->dtype;
@@ -129,7 +129,8 @@ int32_t verify_impl(sixi_smp* h, const sixi_smp_rows* target, const float* draft
     if (qlog != nullptr) {
         // the draft rows' maxima and sums, with the plan sixi_smp_full_distribution uses for them
         LaunchPlan dplan{};
-        if (!sixi_b200::plan_rows(h->vocab, qlog->n_rows, &dplan)) return SIXI_INVALID_ARGUMENT;
+        if (!sixi_b200::plan_rows(h->vocab, qlog->n_rows, sixi_b200::device_sm_count(h->device), &dplan))
+            return SIXI_INVALID_ARGUMENT;
         sixi_b200::DistArgs d{};
         d.data = qlog->data;
         d.row_stride = qlog->row_stride;
@@ -176,7 +177,7 @@ int32_t sixi_smp_create(int32_t device, uint32_t max_rows, uint32_t vocab, sixi_
     if (out == nullptr) return SIXI_INVALID_ARGUMENT;
     *out = nullptr;
     LaunchPlan plan{};
-    if (vocab == 0 || !sixi_b200::plan_rows(vocab, 1, &plan)) return SIXI_INVALID_ARGUMENT;
+    if (vocab == 0 || !sixi_b200::plan_rows(vocab, 1, 0, &plan)) return SIXI_INVALID_ARGUMENT;
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return SIXI_INVALID_ARGUMENT;
     DeviceGuard g(device);
@@ -424,7 +425,8 @@ int32_t sixi_smp_full_distribution(sixi_smp* h, const sixi_smp_rows* rows, const
     if (rows->n_rows == 0) return SIXI_OK;
     DeviceGuard g(h->device);
     LaunchPlan plan{};
-    if (!sixi_b200::plan_rows(h->vocab, rows->n_rows, &plan)) return SIXI_INVALID_ARGUMENT;
+    if (!sixi_b200::plan_rows(h->vocab, rows->n_rows, sixi_b200::device_sm_count(h->device), &plan))
+        return SIXI_INVALID_ARGUMENT;
     sixi_b200::DistArgs a{};
     a.data = rows->data;
     a.row_stride = rows->row_stride;
@@ -474,7 +476,7 @@ int32_t sixi_smp_verify_static(int32_t device, uint32_t vocab, const sixi_smp_ro
                                int32_t* out_first_reject, int32_t* out_uniforms_used, int32_t* out_status,
                                void* stream) {
     LaunchPlan plan{};
-    if (device < 0 || device >= kMaxDevices || vocab == 0 || !sixi_b200::plan_rows(vocab, 1, &plan))
+    if (device < 0 || device >= kMaxDevices || vocab == 0 || !sixi_b200::plan_rows(vocab, 1, 0, &plan))
         return SIXI_INVALID_ARGUMENT;
     if (target == nullptr || (target->n_rows > 0 && target->data == nullptr) ||
         (target->dtype != SIXI_SMP_F32 && target->dtype != SIXI_SMP_BF16) || target->row_stride < vocab ||
@@ -491,10 +493,12 @@ int32_t sixi_smp_verify_static(int32_t device, uint32_t vocab, const sixi_smp_ro
     if (cudaGetDeviceCount(&n) != cudaSuccess || device >= n) return SIXI_INVALID_ARGUMENT;
     DeviceGuard g(device);
     VerifyRowResult* ws = g_static_ws_addr[device].load(std::memory_order_acquire);
-    if (ws == nullptr) {  // first call on this device: check the architecture, resolve the address
+    if (ws == nullptr) {  // first call on this device: check the architecture, set the launch
+                          // attributes of every kernel instance, resolve the workspace address
         cudaDeviceProp prop;
         if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return SIXI_BACKEND_ERROR;
         if (prop.major < 10) return SIXI_UNSUPPORTED_HARDWARE;
+        if (sixi_b200::prepare_kernels(device) != cudaSuccess) return SIXI_BACKEND_ERROR;
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_static_verify_ws) != cudaSuccess || p == nullptr) return SIXI_BACKEND_ERROR;
         ws = static_cast<VerifyRowResult*>(p);

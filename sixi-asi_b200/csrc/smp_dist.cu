@@ -217,27 +217,37 @@ __global__ void __launch_bounds__(kDT, 4) dist_kernel(const DistArgs a) {
 // at most 48 KB of shared memory, so that four CTAs (256 threads each) share an SM and one CTA's
 // bulk copy and cluster barriers overlap another's fp64 arithmetic. The row engine's plan is not
 // used.
+static std::atomic<uint64_t> g_dist_ready{0};  // attributes set once per device
+
+cudaError_t prepare_full_distribution(int dev) {
+    const uint64_t bit = 1ull << (dev & 63);
+    if (g_dist_ready.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(dist_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(dist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(4u * kDMaxChunk));
+    if (e != cudaSuccess) return e;
+    g_dist_ready.fetch_or(bit, std::memory_order_acq_rel);
+    return cudaSuccess;
+}
+
 cudaError_t launch_full_distribution(const DistArgs& args, const LaunchPlan& plan, cudaStream_t stream) {
     (void)plan;
-    static std::atomic<uint64_t> ready{0};  // attributes set once per device
     int dev = 0;
-    cudaGetDevice(&dev);
-    const uint64_t bit = 1ull << (dev & 63);
-    if (!(ready.load(std::memory_order_acquire) & bit)) {
-        cudaError_t e = cudaFuncSetAttribute(dist_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(dist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(4u * kDMaxChunk));
-        if (e != cudaSuccess) return e;
-        ready.fetch_or(bit, std::memory_order_acq_rel);
-    }
+    cudaError_t pe = cudaGetDevice(&dev);
+    if (pe == cudaSuccess) pe = prepare_full_distribution(dev);
+    if (pe != cudaSuccess) return pe;
     uint32_t c = 1;
     while (c < static_cast<uint32_t>(kDMaxC) && (args.vocab + c - 1) / c > kDChunk) c *= 2;
     DistArgs a = args;
     a.chunk = ((args.vocab + c - 1) / c + 7u) / 8u * 8u;  // 16-byte aligned chunk starts
     if (a.chunk > kDMaxChunk) return cudaErrorInvalidValue;
+    // one CTA per (row, cluster rank): refuse grids beyond the 2^31 - 1 CTAs of gridDim.x
+    const uint64_t ctas = static_cast<uint64_t>(a.n_rows) * c;
+    if (ctas == 0) return cudaSuccess;
+    if (ctas > 0x7FFFFFFFull) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.n_rows * c);
+    cfg.gridDim = dim3(static_cast<uint32_t>(ctas));
     cfg.blockDim = dim3(kDT);
     cfg.dynamicSmemBytes = 4u * a.chunk;
     cfg.stream = stream;

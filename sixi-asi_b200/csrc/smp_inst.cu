@@ -13,25 +13,36 @@
 
 namespace sixi_b200 {
 
-template <int DT, int MODE>
+// The shared-memory opt-in and non-portable cluster sizes of this instance, set once per device
+// (prepare_kernels sets them for every instance up front, so that later launches issue no
+// attribute call: they may be inside a stream capture).
+static std::atomic<uint64_t> g_ready{0};
+
+static cudaError_t prepare_this(int dev) {
+    auto kfn = row_kernel<SIXI_INST_DT, SIXI_INST_MODE>;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (g_ready.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    g_ready.fetch_or(bit, std::memory_order_acq_rel);
+    return cudaSuccess;
+}
+
 static cudaError_t launch_one(const RowArgs& a, const LaunchPlan& plan, cudaStream_t stream) {
-    auto kfn = row_kernel<DT, MODE>;
-    // The shared-memory opt-in (and non-portable cluster sizes) are set once per device, so later
-    // launches issue no attribute call (they may be inside a stream capture).
-    static std::atomic<uint64_t> ready{0};
+    auto kfn = row_kernel<SIXI_INST_DT, SIXI_INST_MODE>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const uint64_t bit = 1ull << (dev & 63);
-    if (!(ready.load(std::memory_order_acquire) & bit)) {
-        e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return e;
-        ready.fetch_or(bit, std::memory_order_acq_rel);
-    }
+    e = prepare_this(dev);
+    if (e != cudaSuccess) return e;
     if (plan.smem > static_cast<size_t>(kMaxSmem)) return cudaErrorInvalidValue;
+    // one CTA per (row, cluster rank): refuse grids beyond the 2^31 - 1 CTAs of gridDim.x
+    const uint64_t ctas = static_cast<uint64_t>(a.n_rows) * plan.cluster;
+    if (ctas == 0) return cudaSuccess;
+    if (ctas > 0x7FFFFFFFull) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.n_rows * plan.cluster, 1, 1);
+    cfg.gridDim = dim3(static_cast<uint32_t>(ctas), 1, 1);
     cfg.blockDim = dim3(kNT, 1, 1);
     cfg.dynamicSmemBytes = plan.smem;
     cfg.stream = stream;
@@ -48,7 +59,12 @@ static cudaError_t launch_one(const RowArgs& a, const LaunchPlan& plan, cudaStre
 template <>
 cudaError_t launch_mode_dt<SIXI_INST_MODE, SIXI_INST_DT>(const RowArgs& a, const LaunchPlan& plan,
                                                          cudaStream_t stream) {
-    return launch_one<SIXI_INST_DT, SIXI_INST_MODE>(a, plan, stream);
+    return launch_one(a, plan, stream);
+}
+
+template <>
+cudaError_t prepare_mode_dt<SIXI_INST_MODE, SIXI_INST_DT>(int device) {
+    return prepare_this(device);
 }
 
 }  // namespace sixi_b200

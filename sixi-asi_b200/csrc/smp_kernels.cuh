@@ -80,14 +80,22 @@ struct LaunchPlan {
 };
 
 // Launch plan for a vocabulary and batch: the smallest cluster whose chunk fits shared memory,
-// widened (up to 8 CTAs) while the batch leaves SMs idle.
-bool plan_rows(uint32_t vocab, uint32_t n_rows, LaunchPlan* plan);
+// widened (up to 8 CTAs) while the batch leaves more than half of the device's `sms` SMs idle
+// (sms = 0: no widening; the plan then only validates the vocabulary).
+bool plan_rows(uint32_t vocab, uint32_t n_rows, uint32_t sms, LaunchPlan* plan);
+// Streaming multiprocessors of `device` (queried once per device; 0 when the query fails).
+uint32_t device_sm_count(int device);
 cudaError_t launch_rows(int mode, const RowArgs& a, const LaunchPlan& plan, cudaStream_t stream);
 cudaError_t launch_verify_finalize(const RowArgs& a, uint32_t n_streams, int32_t* out_accepted,
                                    int32_t* out_tokens, int32_t* out_n_tokens,
                                    int32_t* out_first_reject, int32_t* out_uniforms_used,
                                    int32_t* out_status, cudaStream_t stream);
+// Sets the row engine's launch attributes (shared-memory opt-in, non-portable cluster sizes) for
+// every (mode, dtype) instance on the current device, `device`, so that no later launch issues an
+// attribute call (launches may then run inside a stream capture).
 cudaError_t prepare_kernels(int device);
+template <int MODE, int DT>
+cudaError_t prepare_mode_dt(int device);
 
 // ---- NaN / Inf policy (smp_numeric.cu) -------------------------------------------------------
 cudaError_t launch_numeric_policy(float* data, uint32_t n_rows, uint64_t row_stride, uint32_t vocab, uint32_t policy,
@@ -159,6 +167,7 @@ struct DistArgs {
     DraftStat* stats;     // per-row statistics (nullable)
 };
 cudaError_t launch_full_distribution(const DistArgs& a, const LaunchPlan& plan, cudaStream_t stream);
+cudaError_t prepare_full_distribution(int device);  // its launch attributes, once per device
 cudaError_t launch_shard_candidates(const ShardArgs& a, cudaStream_t stream);
 cudaError_t launch_merge_shards(const MergeArgs& a, cudaStream_t stream);
 

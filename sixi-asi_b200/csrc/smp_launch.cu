@@ -1,4 +1,6 @@
 // smp_launch.cu - host-side launch planning and dispatch of the row-engine kernels.
+#include <atomic>
+
 #include "smp_row.cuh"
 
 namespace sixi_b200 {
@@ -8,13 +10,23 @@ static uint32_t chunk_for(uint32_t vocab, uint32_t c) {
     return (chunk + 7u) / 8u * 8u;
 }
 
-bool plan_rows(uint32_t vocab, uint32_t n_rows, LaunchPlan* plan) {
+uint32_t device_sm_count(int device) {
+    static std::atomic<uint32_t> cache[64];
+    if (device < 0 || device >= 64) return 0;
+    uint32_t n = cache[device].load(std::memory_order_relaxed);
+    if (n != 0) return n;
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0) return 0;
+    cache[device].store(static_cast<uint32_t>(v), std::memory_order_relaxed);
+    return static_cast<uint32_t>(v);
+}
+
+bool plan_rows(uint32_t vocab, uint32_t n_rows, uint32_t sms, LaunchPlan* plan) {
     if (vocab == 0) return false;
     uint32_t c = 1;
     while (c <= 16 && chunk_for(vocab, c) > kMaxChunk) c *= 2;
     if (c > 16) return false;
     // widen the cluster while the batch would leave more than half of the SMs idle
-    const uint32_t sms = 148;
     while (c < 8 && n_rows > 0 && static_cast<uint64_t>(n_rows) * c * 2 <= sms && chunk_for(vocab, 2 * c) >= 2048) c *= 2;
     plan->cluster = c;
     plan->chunk = chunk_for(vocab, c);
@@ -52,8 +64,16 @@ cudaError_t launch_verify_finalize(const RowArgs& a, uint32_t n_streams, int32_t
 }
 
 cudaError_t prepare_kernels(int device) {
-    (void)device;
-    return cudaSuccess;
+    cudaError_t e = prepare_mode_dt<kModeSample, SIXI_SMP_F32>(device);
+    if (e == cudaSuccess) e = prepare_mode_dt<kModeSample, SIXI_SMP_BF16>(device);
+    if (e == cudaSuccess) e = prepare_mode_dt<kModeCandidates, SIXI_SMP_F32>(device);
+    if (e == cudaSuccess) e = prepare_mode_dt<kModeCandidates, SIXI_SMP_BF16>(device);
+    if (e == cudaSuccess) e = prepare_mode_dt<kModeGreedy, SIXI_SMP_F32>(device);
+    if (e == cudaSuccess) e = prepare_mode_dt<kModeGreedy, SIXI_SMP_BF16>(device);
+    if (e == cudaSuccess) e = prepare_mode_dt<kModeVerify, SIXI_SMP_F32>(device);
+    if (e == cudaSuccess) e = prepare_mode_dt<kModeVerify, SIXI_SMP_BF16>(device);
+    if (e == cudaSuccess) e = prepare_full_distribution(device);
+    return e;
 }
 
 }  // namespace sixi_b200

@@ -148,3 +148,43 @@ def test_missing_library_fails_loudly(tmp_path):
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=120,
                        cwd=str(REPO / "sixi-asi_b200"))
     assert r.returncode == 0 and "raised" in r.stdout, (r.stdout, r.stderr[-1000:])
+
+
+def test_verify_static_argument_checks_without_gpu():
+    """sixi_smp_verify_static rejects bad arguments before any device call: device outside [0, 64),
+    an empty vocabulary, k = 0, a row count that is not n_streams * (k + 1), null outputs and a
+    misaligned draft_probs (SIXI_INVALID_ARGUMENT); more rows than its static workspace holds
+    (SIXI_OUT_OF_BOUNDS)."""
+    import ctypes
+
+    import sixi_smp
+
+    lib = sixi_smp.load()
+    INV, OOB = sixi_smp.INVALID_ARGUMENT, sixi_smp.OUT_OF_BOUNDS
+    V, k = 4097, 8
+    fake = ctypes.c_void_p(0x1000)  # never dereferenced: every call below returns before that
+    outs = [fake] * 6
+
+    def rows(n):
+        return sixi_smp.Rows(fake.value, sixi_smp.F32, n, V)
+
+    def call(device=0, vocab=V, n_rows=2 * (k + 1), n_streams=2, kk=k, q=None, outputs=None, target=True):
+        r = rows(n_rows)
+        return lib.sixi_smp_verify_static(device, vocab, ctypes.byref(r) if target else None, q, fake, None,
+                                          n_streams, kk, fake, None, None, None, None, 0,
+                                          *(outputs if outputs is not None else outs), None)
+
+    assert call(device=-1) == INV
+    assert call(device=64) == INV
+    assert call(vocab=0) == INV
+    assert call(kk=0, n_rows=2) == INV
+    assert call(n_rows=2 * (k + 1) + 1) == INV
+    assert call(target=False) == INV
+    for i in range(6):
+        o = list(outs)
+        o[i] = None
+        assert call(outputs=o) == INV, i
+    limit = sixi_smp.STATIC_VERIFY_ROWS
+    s = limit // (k + 1) + 1
+    assert call(n_streams=s, n_rows=s * (k + 1)) == OOB
+    assert call(q=ctypes.c_void_p(0x1002)) == INV

@@ -90,3 +90,68 @@ def test_static_verify_rejects_more_rows_than_the_workspace():
     with pytest.raises(S.SixiError) as ei:
         S.verify_static(vocab, target, drafts, params)
     assert ei.value.status == 2  # SIXI_OUT_OF_BOUNDS
+
+
+def _call_static(vocab, target, drafts, params, outs, draft_probs=None, uniforms=None, device=0):
+    """sixi_smp_verify_static through the C ABI with caller-owned outputs (nothing allocated here)."""
+    import ctypes
+
+    S_, k = drafts.shape
+    rows = S.Sampler._rows(target)
+    ptr = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    return S._lib().sixi_smp_verify_static(device, vocab, ctypes.byref(rows), ptr(draft_probs), ptr(drafts), None,
+                                           S_, k, ptr(params), None, None, None, ptr(uniforms), 0,
+                                           *[ptr(o) for o in outs], None)
+
+
+def test_static_verify_warm_call_allocates_no_device_memory():
+    """A warm call (after the first one on the device) changes nothing in the device's free memory:
+    the workspace is the static array and the caller owns inputs and outputs."""
+    vocab = 4097
+    d = W.config4(streams=8, k=8, vocab=vocab, seed=31, stochastic=True, masked=False)
+    target, drafts, params = dev(d["target_bits"]), dev(d["drafts"]), dev(d["params"])
+    q, u = dev(d["q"]), dev(d["uniforms"])
+    outs = [torch.empty(8, dtype=torch.int32, device=DEV), torch.empty((8, 9), dtype=torch.int32, device=DEV)] + \
+        [torch.empty(8, dtype=torch.int32, device=DEV) for _ in range(4)]
+    assert _call_static(vocab, target, drafts, params, outs, q, u) == 0  # first call: set-up
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(DEV)
+    for _ in range(3):
+        assert _call_static(vocab, target, drafts, params, outs, q, u) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(DEV)
+    assert free1 == free0, (free0, free1)
+    smp = S.Sampler(0, 128, vocab)
+    ref = smp.verify(target, drafts, params, draft_probs=q, uniforms=u)
+    torch.cuda.synchronize()
+    for k_, o in zip(KEYS, outs):
+        assert np.array_equal(ref[k_].cpu().numpy(), o.cpu().numpy()), k_
+    smp.close()
+
+
+def test_static_verify_on_another_device_restores_the_current_one():
+    """With two GPUs: a call for device 1 while device 0 is current runs on device 1 (its own
+    workspace address) and leaves device 0 current."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    vocab = 4097
+    d1 = torch.device("cuda:1")
+    x = W.config4(streams=4, k=8, vocab=vocab, seed=41, stochastic=True, masked=False)
+
+    def on(a, dv):
+        t = dev(a)
+        return None if t is None else t.to(dv)
+
+    target, drafts, params, q, u = (on(x[n], d1) for n in ("target_bits", "drafts", "params", "q", "uniforms"))
+    outs = [torch.empty(4, dtype=torch.int32, device=d1), torch.empty((4, 9), dtype=torch.int32, device=d1)] + \
+        [torch.empty(4, dtype=torch.int32, device=d1) for _ in range(4)]
+    torch.cuda.set_device(0)
+    assert _call_static(vocab, target, drafts, params, outs, q, u, device=1) == 0
+    assert torch.cuda.current_device() == 0
+    torch.cuda.synchronize(d1)
+    smp = S.Sampler(1, 64, vocab)
+    ref = smp.verify(target, drafts, params, draft_probs=q, uniforms=u)
+    torch.cuda.synchronize(d1)
+    for k_, o in zip(KEYS, outs):
+        assert np.array_equal(ref[k_].cpu().numpy(), o.cpu().numpy()), k_
+    smp.close()

@@ -128,6 +128,26 @@ SIXI_SMP_API int32_t sixi_smp_sample_host(sixi_smp* h, const void* host_logits, 
                              int32_t* host_out_status, void* stream);
 
 /*
+ * sixi_smp_sample_host without the final synchronisation, for pipelines over independent batches
+ * (no counterpart in the engine, whose sampler call returns the token). Two device staging slots
+ * alternate between calls: a call copies its inputs into its slot on the handle's own copy stream,
+ * after the kernel of the call that last used that slot has finished, and its kernel on `stream`
+ * waits for that copy; so call i + 1's host->device copy overlaps call i's kernel. Tokens and
+ * statuses are copied back on `stream`. The caller keeps the host inputs unchanged and alive, and
+ * reads the outputs only after synchronising `stream` (or an event recorded on it after the call).
+ * Host buffers must be pinned for the copies to be asynchronous. Calls on one handle must come from
+ * one thread at a time. A call that needs larger staging than its slot has waits for that slot and
+ * reallocates it.
+ */
+SIXI_SMP_API int32_t sixi_smp_sample_host_async(sixi_smp* h, const void* host_logits, uint32_t dtype,
+                                               uint32_t n_rows, uint64_t row_stride,
+                                               const sixi_smp_params* host_params,
+                                               const uint32_t* host_mask_words, const int32_t* host_hist_tokens,
+                                               const int64_t* host_hist_offsets, const double* host_uniforms,
+                                               uint64_t step, int32_t* host_out_tokens, int32_t* host_out_status,
+                                               void* stream);
+
+/*
  * Greedy argmax per row on the raw (optionally masked) logits, lowest id on ties; a NaN at index 0
  * yields 0 and other NaNs never win, exactly as DeterministicSampler::sample_greedy_argmax
  * (src/core/core_execution.cpp:394-407). Replaces the llama.cpp greedy sampler hook

@@ -18,6 +18,23 @@ using sixi_b200::LaunchPlan;
 using sixi_b200::RowArgs;
 using sixi_b200::VerifyRowResult;
 
+// Device staging of the host-buffer entry points: one slot per call in flight.
+struct HostSlot {
+    void* d_logits;
+    size_t logits_cap;  // bytes
+    sixi_smp_params* d_params;
+    uint32_t* d_mask;
+    int32_t* d_hist;
+    size_t hist_cap;    // tokens
+    int64_t* d_hoff;
+    double* d_u;
+    int32_t* d_tok;
+    int32_t* d_status;
+    size_t rows_cap;
+    cudaEvent_t copied;    // its inputs are on the device (recorded on the copy stream)
+    cudaEvent_t consumed;  // the call that used it has read its inputs and written its outputs
+};
+
 struct sixi_smp {
     int32_t device;
     uint32_t max_rows;
@@ -26,18 +43,11 @@ struct sixi_smp {
     VerifyRowResult* ws;         // verifier per-row workspace [max_rows]
     sixi_b200::DraftStat* qstat; // draft-row distribution statistics [max_rows]
     sixi_smp_params* d_default;  // default params (raw argmax entry)
-    // staging of sixi_smp_sample_host
-    void* d_logits;
-    size_t logits_cap;
-    sixi_smp_params* d_params;
-    uint32_t* d_mask;
-    int32_t* d_hist;
-    size_t hist_cap;
-    int64_t* d_hoff;
-    double* d_u;
-    int32_t* d_tok;
-    int32_t* d_status;
-    size_t rows_cap;
+    // staging of sixi_smp_sample_host(_async): two slots used alternately, so that a call's
+    // host->device copy (on copy_stream) overlaps the previous call's kernel
+    HostSlot slot[2];
+    uint32_t next_slot;
+    cudaStream_t copy_stream;
 };
 
 namespace {
@@ -204,6 +214,11 @@ int32_t sixi_smp_create(int32_t device, uint32_t max_rows, uint32_t vocab, sixi_
         e = cudaMemcpy(h->d_default, &p, sizeof(p), cudaMemcpyHostToDevice);
     }
     if (e == cudaSuccess) e = sixi_b200::prepare_kernels(device);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking);
+    for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
+        e = cudaEventCreateWithFlags(&h->slot[i].copied, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->slot[i].consumed, cudaEventDisableTiming);
+    }
     if (e != cudaSuccess) {
         sixi_smp_destroy(h);
         return from_cuda(e);
@@ -215,17 +230,24 @@ int32_t sixi_smp_create(int32_t device, uint32_t max_rows, uint32_t vocab, sixi_
 int32_t sixi_smp_destroy(sixi_smp* h) {
     if (h == nullptr) return SIXI_OK;
     DeviceGuard g(h->device);
+    if (h->copy_stream != nullptr) cudaStreamSynchronize(h->copy_stream);
+    for (HostSlot& sl : h->slot) {
+        if (sl.consumed != nullptr) cudaEventSynchronize(sl.consumed);
+        cudaFree(sl.d_logits);
+        cudaFree(sl.d_params);
+        cudaFree(sl.d_mask);
+        cudaFree(sl.d_hist);
+        cudaFree(sl.d_hoff);
+        cudaFree(sl.d_u);
+        cudaFree(sl.d_tok);
+        cudaFree(sl.d_status);
+        if (sl.copied != nullptr) cudaEventDestroy(sl.copied);
+        if (sl.consumed != nullptr) cudaEventDestroy(sl.consumed);
+    }
+    if (h->copy_stream != nullptr) cudaStreamDestroy(h->copy_stream);
     cudaFree(h->ws);
     cudaFree(h->qstat);
     cudaFree(h->d_default);
-    cudaFree(h->d_logits);
-    cudaFree(h->d_params);
-    cudaFree(h->d_mask);
-    cudaFree(h->d_hist);
-    cudaFree(h->d_hoff);
-    cudaFree(h->d_u);
-    cudaFree(h->d_tok);
-    cudaFree(h->d_status);
     delete h;
     return SIXI_OK;
 }
@@ -273,12 +295,11 @@ int32_t sixi_smp_sample(sixi_smp* h, const sixi_smp_rows* rows, const sixi_smp_p
                                             static_cast<cudaStream_t>(stream)));
 }
 
-int32_t sixi_smp_sample_host(sixi_smp* h, const void* host_logits, uint32_t dtype,
-                             uint32_t n_rows, uint64_t row_stride,
-                             const sixi_smp_params* host_params, const uint32_t* host_mask_words,
-                             const int32_t* host_hist_tokens, const int64_t* host_hist_offsets,
-                             const double* host_uniforms, uint64_t step, int32_t* host_out_tokens,
-                             int32_t* host_out_status, void* stream) {
+int32_t sixi_smp_sample_host_async(sixi_smp* h, const void* host_logits, uint32_t dtype, uint32_t n_rows,
+                                   uint64_t row_stride, const sixi_smp_params* host_params,
+                                   const uint32_t* host_mask_words, const int32_t* host_hist_tokens,
+                                   const int64_t* host_hist_offsets, const double* host_uniforms, uint64_t step,
+                                   int32_t* host_out_tokens, int32_t* host_out_status, void* stream) {
     if (h == nullptr || host_logits == nullptr || host_params == nullptr ||
         host_out_tokens == nullptr || host_out_status == nullptr || row_stride < h->vocab ||
         (dtype != SIXI_SMP_F32 && dtype != SIXI_SMP_BF16) ||
@@ -287,64 +308,88 @@ int32_t sixi_smp_sample_host(sixi_smp* h, const void* host_logits, uint32_t dtyp
     if (n_rows == 0) return SIXI_OK;
     DeviceGuard g(h->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    HostSlot& sl = h->slot[h->next_slot];
     const size_t esz = dtype == SIXI_SMP_BF16 ? 2 : 4;
     const size_t lbytes = static_cast<size_t>(n_rows) * row_stride * esz;
-    size_t cap_bytes = h->logits_cap;
-    cudaError_t e = grow(reinterpret_cast<uint8_t**>(&h->d_logits), &cap_bytes, lbytes);
-    h->logits_cap = cap_bytes;
-    // params, tokens, status, uniforms, masks sized by n_rows (re-allocated when a call needs more)
-    if (e == cudaSuccess && (h->d_params == nullptr || h->rows_cap < n_rows)) {
-        cudaFree(h->d_params);
-        cudaFree(h->d_u);
-        cudaFree(h->d_tok);
-        cudaFree(h->d_status);
-        cudaFree(h->d_mask);
-        cudaFree(h->d_hoff);
-        h->d_params = nullptr;
-        h->d_u = nullptr;
-        h->d_tok = nullptr;
-        h->d_status = nullptr;
-        h->d_mask = nullptr;
-        h->d_hoff = nullptr;
-        e = cudaMalloc(&h->d_params, sizeof(sixi_smp_params) * n_rows);
-        if (e == cudaSuccess) e = cudaMalloc(&h->d_u, sizeof(double) * n_rows);
-        if (e == cudaSuccess) e = cudaMalloc(&h->d_tok, sizeof(int32_t) * n_rows);
-        if (e == cudaSuccess) e = cudaMalloc(&h->d_status, sizeof(int32_t) * n_rows);
-        if (e == cudaSuccess) e = cudaMalloc(&h->d_mask, sizeof(uint32_t) * h->mask_words * n_rows);
-        if (e == cudaSuccess) e = cudaMalloc(&h->d_hoff, sizeof(int64_t) * (n_rows + 1));
-        h->rows_cap = (e == cudaSuccess) ? n_rows : 0;
+    const int64_t nh = host_hist_tokens != nullptr ? host_hist_offsets[n_rows] : 0;
+    cudaError_t e = cudaSuccess;
+    // growth reallocates the slot: wait for the call that last used it first
+    const bool grow_rows = sl.d_params == nullptr || sl.rows_cap < n_rows;
+    if (sl.logits_cap < lbytes || grow_rows || (nh > 0 && sl.hist_cap < static_cast<size_t>(nh)))
+        e = cudaEventSynchronize(sl.consumed);
+    if (e == cudaSuccess) e = grow(reinterpret_cast<uint8_t**>(&sl.d_logits), &sl.logits_cap, lbytes);
+    if (e == cudaSuccess && grow_rows) {
+        cudaFree(sl.d_params);
+        cudaFree(sl.d_u);
+        cudaFree(sl.d_tok);
+        cudaFree(sl.d_status);
+        cudaFree(sl.d_mask);
+        cudaFree(sl.d_hoff);
+        sl.d_params = nullptr;
+        sl.d_u = nullptr;
+        sl.d_tok = nullptr;
+        sl.d_status = nullptr;
+        sl.d_mask = nullptr;
+        sl.d_hoff = nullptr;
+        e = cudaMalloc(&sl.d_params, sizeof(sixi_smp_params) * n_rows);
+        if (e == cudaSuccess) e = cudaMalloc(&sl.d_u, sizeof(double) * n_rows);
+        if (e == cudaSuccess) e = cudaMalloc(&sl.d_tok, sizeof(int32_t) * n_rows);
+        if (e == cudaSuccess) e = cudaMalloc(&sl.d_status, sizeof(int32_t) * n_rows);
+        if (e == cudaSuccess) e = cudaMalloc(&sl.d_mask, sizeof(uint32_t) * h->mask_words * n_rows);
+        if (e == cudaSuccess) e = cudaMalloc(&sl.d_hoff, sizeof(int64_t) * (n_rows + 1));
+        sl.rows_cap = (e == cudaSuccess) ? n_rows : 0;
     }
-    int64_t nh = 0;
-    if (host_hist_tokens != nullptr) nh = host_hist_offsets[n_rows];
-    if (e == cudaSuccess && nh > 0) e = grow(&h->d_hist, &h->hist_cap, static_cast<size_t>(nh));
+    if (e == cudaSuccess && nh > 0) e = grow(&sl.d_hist, &sl.hist_cap, static_cast<size_t>(nh));
     if (e != cudaSuccess) return from_cuda(e);
-    e = cudaMemcpyAsync(h->d_logits, host_logits, lbytes, cudaMemcpyHostToDevice, s);
+    // inputs -> the slot on the copy stream, once the call that last used the slot is done with it
+    cudaStream_t c = h->copy_stream;
+    e = cudaStreamWaitEvent(c, sl.consumed, 0);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(sl.d_logits, host_logits, lbytes, cudaMemcpyHostToDevice, c);
     if (e == cudaSuccess)
-        e = cudaMemcpyAsync(h->d_params, host_params, sizeof(sixi_smp_params) * n_rows, cudaMemcpyHostToDevice, s);
+        e = cudaMemcpyAsync(sl.d_params, host_params, sizeof(sixi_smp_params) * n_rows, cudaMemcpyHostToDevice, c);
     if (e == cudaSuccess && host_mask_words)
-        e = cudaMemcpyAsync(h->d_mask, host_mask_words, sizeof(uint32_t) * h->mask_words * n_rows,
-                            cudaMemcpyHostToDevice, s);
+        e = cudaMemcpyAsync(sl.d_mask, host_mask_words, sizeof(uint32_t) * h->mask_words * n_rows,
+                            cudaMemcpyHostToDevice, c);
     if (e == cudaSuccess && nh > 0) {
-        e = cudaMemcpyAsync(h->d_hist, host_hist_tokens, sizeof(int32_t) * static_cast<size_t>(nh),
-                            cudaMemcpyHostToDevice, s);
+        e = cudaMemcpyAsync(sl.d_hist, host_hist_tokens, sizeof(int32_t) * static_cast<size_t>(nh),
+                            cudaMemcpyHostToDevice, c);
         if (e == cudaSuccess)
-            e = cudaMemcpyAsync(h->d_hoff, host_hist_offsets, sizeof(int64_t) * (n_rows + 1),
-                                cudaMemcpyHostToDevice, s);
+            e = cudaMemcpyAsync(sl.d_hoff, host_hist_offsets, sizeof(int64_t) * (n_rows + 1), cudaMemcpyHostToDevice, c);
     }
     if (e == cudaSuccess && host_uniforms)
-        e = cudaMemcpyAsync(h->d_u, host_uniforms, sizeof(double) * n_rows, cudaMemcpyHostToDevice, s);
+        e = cudaMemcpyAsync(sl.d_u, host_uniforms, sizeof(double) * n_rows, cudaMemcpyHostToDevice, c);
+    if (e == cudaSuccess) e = cudaEventRecord(sl.copied, c);
+    // the kernel and the read-back on the caller's stream, after the copies
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, sl.copied, 0);
     if (e != cudaSuccess) return from_cuda(e);
-    sixi_smp_rows rows{h->d_logits, dtype, n_rows, row_stride};
-    const int32_t st = sixi_smp_sample(h, &rows, h->d_params, host_mask_words ? h->d_mask : nullptr,
-                                       nh > 0 ? h->d_hist : nullptr, nh > 0 ? h->d_hoff : nullptr,
-                                       host_uniforms ? h->d_u : nullptr, step, h->d_tok, h->d_status,
-                                       stream);
-    if (st != SIXI_OK) return st;
-    e = cudaMemcpyAsync(host_out_tokens, h->d_tok, sizeof(int32_t) * n_rows, cudaMemcpyDeviceToHost, s);
+    h->next_slot ^= 1u;
+    sixi_smp_rows rows{sl.d_logits, dtype, n_rows, row_stride};
+    const int32_t st = sixi_smp_sample(h, &rows, sl.d_params, host_mask_words ? sl.d_mask : nullptr,
+                                       nh > 0 ? sl.d_hist : nullptr, nh > 0 ? sl.d_hoff : nullptr,
+                                       host_uniforms ? sl.d_u : nullptr, step, sl.d_tok, sl.d_status, stream);
+    if (st != SIXI_OK) {
+        cudaEventRecord(sl.consumed, s);
+        return st;
+    }
+    e = cudaMemcpyAsync(host_out_tokens, sl.d_tok, sizeof(int32_t) * n_rows, cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess)
-        e = cudaMemcpyAsync(host_out_status, h->d_status, sizeof(int32_t) * n_rows, cudaMemcpyDeviceToHost, s);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-    return from_cuda(e);
+        e = cudaMemcpyAsync(host_out_status, sl.d_status, sizeof(int32_t) * n_rows, cudaMemcpyDeviceToHost, s);
+    const cudaError_t e2 = cudaEventRecord(sl.consumed, s);
+    return from_cuda(e != cudaSuccess ? e : e2);
+}
+
+int32_t sixi_smp_sample_host(sixi_smp* h, const void* host_logits, uint32_t dtype,
+                             uint32_t n_rows, uint64_t row_stride,
+                             const sixi_smp_params* host_params, const uint32_t* host_mask_words,
+                             const int32_t* host_hist_tokens, const int64_t* host_hist_offsets,
+                             const double* host_uniforms, uint64_t step, int32_t* host_out_tokens,
+                             int32_t* host_out_status, void* stream) {
+    const int32_t st = sixi_smp_sample_host_async(h, host_logits, dtype, n_rows, row_stride, host_params,
+                                                  host_mask_words, host_hist_tokens, host_hist_offsets,
+                                                  host_uniforms, step, host_out_tokens, host_out_status, stream);
+    if (st != SIXI_OK || n_rows == 0) return st;
+    DeviceGuard g(h->device);
+    return from_cuda(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
 }
 
 int32_t sixi_smp_greedy_argmax(sixi_smp* h, const sixi_smp_rows* rows, const uint32_t* mask_words,

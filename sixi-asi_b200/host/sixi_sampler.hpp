@@ -318,8 +318,8 @@ public:
         Status st = check_row(logits, vocab_size);
         if (!st.ok()) return R(st);
         detail::DeviceGuard g(device_);
-        st = stage_row(logits, vocab_size, to_smp_params(params, mask_words != nullptr), recent_tokens, mask_words,
-                       nullptr);
+        if (!stage_logits(logits, 1, vocab_size)) return R(oom());
+        st = stage_inputs(to_smp_params(params, mask_words != nullptr), recent_tokens, mask_words, nullptr);
         if (!st.ok()) return R(st);
         const uint32_t max_out = 256;
         if (!d_cand_.ensure(2 * max_out * sizeof(double))) return R(oom());
@@ -353,36 +353,42 @@ public:
     Result<int32_t> sample_token(const float* logits, uint64_t vocab_size, const P& params, Rng& rng,
                                  const std::vector<int32_t>& recent_tokens = {},
                                  const uint32_t* mask_words = nullptr) {
-        using R = Result<int32_t>;
         Status st = check_row(logits, vocab_size);
-        if (!st.ok()) return R(st);
+        if (!st.ok()) return Result<int32_t>(st);
         detail::DeviceGuard g(device_);
-        const auto ck = rng.checkpoint();
-        const bool sampled = params.temperature > 0.0f;
-        const double u = sampled ? rng.next_uniform01() : 0.0;
-        st = stage_row(logits, vocab_size, to_smp_params(params, mask_words != nullptr), recent_tokens, mask_words,
-                       &u);
-        if (!st.ok()) {
-            rng.restore(ck);
-            return R(st);
-        }
+        if (!stage_logits(logits, 1, vocab_size)) return Result<int32_t>(oom());
+        return sample_staged(sixi_smp_rows{d_logits_.p, SIXI_SMP_F32, 1, vocab_size}, params, rng, recent_tokens,
+                             mask_words);
+    }
+
+    // ---- device-resident rows ------------------------------------------------------------------
+    // The same calls on rows the caller already holds in device memory on this sampler's device
+    // (fp32 or bf16, any row stride >= vocab()): the backend's logits buffer for the output
+    // positions, so that the V * 4 bytes of a row never cross PCIe. Only the parameters, the
+    // history and the uniforms go to the device, and a few bytes per row come back. The device
+    // rows must stay valid and unchanged until the call returns (every call here synchronises).
+
+    // sample_token on one device row (`row.n_rows` == 1).
+    template <class P, class Rng>
+    Result<int32_t> sample_token(const sixi_smp_rows& row, const P& params, Rng& rng,
+                                 const std::vector<int32_t>& recent_tokens = {},
+                                 const uint32_t* mask_words = nullptr) {
+        if (row.data == nullptr || row.n_rows != 1 || row.row_stride < vocab_)
+            return Result<int32_t>(ErrorCode::InvalidArgument, "sample_token: one device row of the vocabulary's width");
+        detail::DeviceGuard g(device_);
+        return sample_staged(row, params, rng, recent_tokens, mask_words);
+    }
+
+    // Raw argmax of one device row (sample_greedy_argmax); -1 on any failure.
+    int32_t sample_greedy_argmax(const sixi_smp_rows& row) noexcept {
+        if (row.data == nullptr || row.n_rows != 1 || row.row_stride < vocab_) return -1;
+        detail::DeviceGuard g(device_);
         int32_t* out = d_out_.as<int32_t>();
-        sixi_smp_rows rows{d_logits_.p, SIXI_SMP_F32, 1, vocab_size};
-        const int32_t rc = sixi_smp_sample(h_, &rows, d_params_.as<sixi_smp_params>(),
-                                           mask_words ? d_mask_.as<uint32_t>() : nullptr, d_hist_.as<int32_t>(),
-                                           d_hoff_.as<int64_t>(), d_u_.as<double>(), 0, out, out + 1, stream_);
+        if (sixi_smp_greedy_argmax(h_, &row, nullptr, out, out + 1, stream_) != SIXI_OK) return -1;
         int32_t r[2] = {-1, 0};
-        if (rc == SIXI_OK) {
-            cudaMemcpyAsync(r, out, sizeof r, cudaMemcpyDeviceToHost, stream_);
-            if (cudaStreamSynchronize(stream_) != cudaSuccess) r[1] = SIXI_BACKEND_ERROR;
-        } else {
-            r[1] = rc;
-        }
-        if (r[1] != SIXI_OK) {
-            rng.restore(ck);
-            return R(detail::status_of(r[1], "sample_token"));
-        }
-        return R(r[0]);
+        if (cudaMemcpyAsync(r, out, sizeof r, cudaMemcpyDeviceToHost, stream_) != cudaSuccess) return -1;
+        if (cudaStreamSynchronize(stream_) != cudaSuccess) return -1;
+        return r[1] == SIXI_OK ? r[0] : -1;
     }
 
     // The candidate-list draw of DeterministicSampler::sample_from_candidates
@@ -418,57 +424,28 @@ public:
         detail::DeviceGuard g(device_);
         const uint64_t V = vocab_;
         if (!stage_logits(target_rows, k + 1, V)) return R(oom());
-        const sixi_smp_params pr = to_smp_params(params, mask_words != nullptr);
-        const size_t mw = sixi_smp_mask_words(h_);
-        const auto ck = rng.checkpoint();
-        std::vector<double> u(k + 1);
-        for (double& x : u) x = rng.next_uniform01();
-        const int64_t hoff[2] = {0, static_cast<int64_t>(context_tokens.size())};
-        bool ok = d_params_.ensure(sizeof pr) && d_hist_.ensure(context_tokens.size() * 4 + 4) &&
-                  d_hoff_.ensure(sizeof hoff) && d_u_.ensure(u.size() * 8) && d_drafts_.ensure(k * 4 + 4) &&
-                  d_vout_.ensure((6 + k + 1) * 4);
-        if (ok && draft_probs != nullptr) ok = d_q_.ensure(k * V * 4 + 16);
-        if (ok && mask_words != nullptr) ok = d_mask_.ensure((k + 1) * mw * 4);
-        if (!ok) {
-            rng.restore(ck);
-            return R(oom());
-        }
-        cudaMemcpyAsync(d_params_.p, &pr, sizeof pr, cudaMemcpyHostToDevice, stream_);
-        if (!context_tokens.empty())
-            cudaMemcpyAsync(d_hist_.p, context_tokens.data(), context_tokens.size() * 4, cudaMemcpyHostToDevice,
-                            stream_);
-        cudaMemcpyAsync(d_hoff_.p, hoff, sizeof hoff, cudaMemcpyHostToDevice, stream_);
-        cudaMemcpyAsync(d_u_.p, u.data(), u.size() * 8, cudaMemcpyHostToDevice, stream_);
-        if (k > 0) cudaMemcpyAsync(d_drafts_.p, drafts.data(), k * 4, cudaMemcpyHostToDevice, stream_);
-        if (draft_probs != nullptr && k > 0)
+        if (draft_probs != nullptr && k > 0) {
+            if (!d_q_.ensure(k * V * 4 + 16)) return R(oom());
             cudaMemcpyAsync(d_q_.p, draft_probs, k * V * 4, cudaMemcpyHostToDevice, stream_);
-        if (mask_words != nullptr)
-            cudaMemcpyAsync(d_mask_.p, mask_words, (k + 1) * mw * 4, cudaMemcpyHostToDevice, stream_);
-        int32_t* o = d_vout_.as<int32_t>();  // accepted, n_tokens, first_reject, used, status, tokens[k+1]
-        sixi_smp_rows rows{d_logits_.p, SIXI_SMP_F32, static_cast<uint32_t>(k + 1), V};
-        const int32_t rc = sixi_smp_verify(h_, &rows, draft_probs ? d_q_.as<float>() : nullptr,
-                                           d_drafts_.as<int32_t>(), nullptr, 1, static_cast<uint32_t>(k),
-                                           d_params_.as<sixi_smp_params>(),
-                                           mask_words ? d_mask_.as<uint32_t>() : nullptr, d_hist_.as<int32_t>(),
-                                           d_hoff_.as<int64_t>(), d_u_.as<double>(), 0, o, o + 5, o + 1, o + 2,
-                                           o + 3, o + 4, stream_);
-        std::vector<int32_t> h(5 + k + 1, 0);
-        if (rc == SIXI_OK) {
-            cudaMemcpyAsync(h.data(), o, h.size() * 4, cudaMemcpyDeviceToHost, stream_);
-            if (cudaStreamSynchronize(stream_) != cudaSuccess) h[4] = SIXI_BACKEND_ERROR;
-        } else {
-            h[4] = rc;
         }
-        rng.restore(ck);
-        if (h[4] != SIXI_OK) return R(detail::status_of(h[4], "verify"));
-        for (int32_t i = 0; i < h[3]; ++i) rng.next_uniform01();
-        VerifyResult res;
-        res.proposed_k = static_cast<uint32_t>(k);
-        res.accepted_draft_count = static_cast<uint32_t>(h[0]);
-        res.first_rejected_position = h[2];
-        res.uniforms_used = static_cast<uint32_t>(h[3]);
-        res.committed_tokens.assign(h.begin() + 5, h.begin() + 5 + h[1]);
-        return R(std::move(res));
+        return verify_staged(sixi_smp_rows{d_logits_.p, SIXI_SMP_F32, static_cast<uint32_t>(k + 1), V},
+                             draft_probs != nullptr ? d_q_.as<float>() : nullptr, drafts, params, rng, context_tokens,
+                             mask_words);
+    }
+
+    // verify on k + 1 device rows (`target.n_rows` == drafts.size() + 1: the rows of one stream's
+    // verify pass) with dense draft probabilities in device memory (`d_draft_probs` [k][row_stride]
+    // fp32) or none (one-hot rule).
+    template <class P, class Rng>
+    Result<VerifyResult> verify(const sixi_smp_rows& target, const float* d_draft_probs,
+                                const std::vector<int32_t>& drafts, const P& params, Rng& rng,
+                                const std::vector<int32_t>& context_tokens, const uint32_t* mask_words = nullptr) {
+        using R = Result<VerifyResult>;
+        if (target.data == nullptr || target.n_rows != drafts.size() + 1 || target.row_stride < vocab_)
+            return R(ErrorCode::InvalidArgument, "verify: k + 1 device rows of the vocabulary's width");
+        if (target.n_rows > max_rows_) return R(ErrorCode::OutOfBounds, "verify: k + 1 exceeds max_rows");
+        detail::DeviceGuard g(device_);
+        return verify_staged(target, d_draft_probs, drafts, params, rng, context_tokens, mask_words);
     }
 
     // ---- batched device path -------------------------------------------------------------------
@@ -529,6 +506,92 @@ private:
         return p;
     }
 
+    // sample_token on rows already on the device (staged or the caller's): uniforms drawn in the
+    // engine's order, the RNG restored when the row fails.
+    template <class P, class Rng>
+    Result<int32_t> sample_staged(const sixi_smp_rows& rows, const P& params, Rng& rng,
+                                  const std::vector<int32_t>& recent_tokens, const uint32_t* mask_words) {
+        using R = Result<int32_t>;
+        const auto ck = rng.checkpoint();
+        const bool sampled = params.temperature > 0.0f;
+        const double u = sampled ? rng.next_uniform01() : 0.0;
+        Status st = stage_inputs(to_smp_params(params, mask_words != nullptr), recent_tokens, mask_words, &u);
+        if (!st.ok()) {
+            rng.restore(ck);
+            return R(st);
+        }
+        int32_t* out = d_out_.as<int32_t>();
+        const int32_t rc = sixi_smp_sample(h_, &rows, d_params_.as<sixi_smp_params>(),
+                                           mask_words ? d_mask_.as<uint32_t>() : nullptr, d_hist_.as<int32_t>(),
+                                           d_hoff_.as<int64_t>(), d_u_.as<double>(), 0, out, out + 1, stream_);
+        int32_t r[2] = {-1, 0};
+        if (rc == SIXI_OK) {
+            cudaMemcpyAsync(r, out, sizeof r, cudaMemcpyDeviceToHost, stream_);
+            if (cudaStreamSynchronize(stream_) != cudaSuccess) r[1] = SIXI_BACKEND_ERROR;
+        } else {
+            r[1] = rc;
+        }
+        if (r[1] != SIXI_OK) {
+            rng.restore(ck);
+            return R(detail::status_of(r[1], "sample_token"));
+        }
+        return R(r[0]);
+    }
+
+    // verify on device rows (staged or the caller's), with device draft probabilities or none.
+    template <class P, class Rng>
+    Result<VerifyResult> verify_staged(const sixi_smp_rows& rows, const float* d_q, const std::vector<int32_t>& drafts,
+                                       const P& params, Rng& rng, const std::vector<int32_t>& context_tokens,
+                                       const uint32_t* mask_words) {
+        using R = Result<VerifyResult>;
+        const size_t k = drafts.size();
+        const sixi_smp_params pr = to_smp_params(params, mask_words != nullptr);
+        const size_t mw = sixi_smp_mask_words(h_);
+        const auto ck = rng.checkpoint();
+        std::vector<double> u(k + 1);
+        for (double& x : u) x = rng.next_uniform01();
+        const int64_t hoff[2] = {0, static_cast<int64_t>(context_tokens.size())};
+        const bool ok = d_params_.ensure(sizeof pr) && d_hist_.ensure(context_tokens.size() * 4 + 4) &&
+                        d_hoff_.ensure(sizeof hoff) && d_u_.ensure(u.size() * 8) && d_drafts_.ensure(k * 4 + 4) &&
+                        d_vout_.ensure((6 + k + 1) * 4) && (mask_words == nullptr || d_mask_.ensure((k + 1) * mw * 4));
+        if (!ok) {
+            rng.restore(ck);
+            return R(oom());
+        }
+        cudaMemcpyAsync(d_params_.p, &pr, sizeof pr, cudaMemcpyHostToDevice, stream_);
+        if (!context_tokens.empty())
+            cudaMemcpyAsync(d_hist_.p, context_tokens.data(), context_tokens.size() * 4, cudaMemcpyHostToDevice,
+                            stream_);
+        cudaMemcpyAsync(d_hoff_.p, hoff, sizeof hoff, cudaMemcpyHostToDevice, stream_);
+        cudaMemcpyAsync(d_u_.p, u.data(), u.size() * 8, cudaMemcpyHostToDevice, stream_);
+        if (k > 0) cudaMemcpyAsync(d_drafts_.p, drafts.data(), k * 4, cudaMemcpyHostToDevice, stream_);
+        if (mask_words != nullptr)
+            cudaMemcpyAsync(d_mask_.p, mask_words, (k + 1) * mw * 4, cudaMemcpyHostToDevice, stream_);
+        int32_t* o = d_vout_.as<int32_t>();  // accepted, n_tokens, first_reject, used, status, tokens[k+1]
+        const int32_t rc = sixi_smp_verify(h_, &rows, d_q, d_drafts_.as<int32_t>(), nullptr, 1,
+                                           static_cast<uint32_t>(k), d_params_.as<sixi_smp_params>(),
+                                           mask_words ? d_mask_.as<uint32_t>() : nullptr, d_hist_.as<int32_t>(),
+                                           d_hoff_.as<int64_t>(), d_u_.as<double>(), 0, o, o + 5, o + 1, o + 2,
+                                           o + 3, o + 4, stream_);
+        std::vector<int32_t> h(5 + k + 1, 0);
+        if (rc == SIXI_OK) {
+            cudaMemcpyAsync(h.data(), o, h.size() * 4, cudaMemcpyDeviceToHost, stream_);
+            if (cudaStreamSynchronize(stream_) != cudaSuccess) h[4] = SIXI_BACKEND_ERROR;
+        } else {
+            h[4] = rc;
+        }
+        rng.restore(ck);
+        if (h[4] != SIXI_OK) return R(detail::status_of(h[4], "verify"));
+        for (int32_t i = 0; i < h[3]; ++i) rng.next_uniform01();
+        VerifyResult res;
+        res.proposed_k = static_cast<uint32_t>(k);
+        res.accepted_draft_count = static_cast<uint32_t>(h[0]);
+        res.first_rejected_position = h[2];
+        res.uniforms_used = static_cast<uint32_t>(h[3]);
+        res.committed_tokens.assign(h.begin() + 5, h.begin() + 5 + h[1]);
+        return R(std::move(res));
+    }
+
     Status check_row(const float* logits, uint64_t vocab_size) const {
         if (logits == nullptr || vocab_size == 0)
             return Status::Error(ErrorCode::InvalidArgument, "logits must be non-null with vocab_size > 0");
@@ -543,9 +606,9 @@ private:
                                stream_) == cudaSuccess;
     }
 
-    Status stage_row(const float* logits, uint64_t vocab_size, const sixi_smp_params& p,
-                     const std::vector<int32_t>& hist, const uint32_t* mask_words, const double* u) {
-        if (!stage_logits(logits, 1, vocab_size)) return oom();
+    // params, history, mask and uniform of one row to the device staging buffers
+    Status stage_inputs(const sixi_smp_params& p, const std::vector<int32_t>& hist, const uint32_t* mask_words,
+                        const double* u) {
         const size_t mw = sixi_smp_mask_words(h_);
         const int64_t hoff[2] = {0, static_cast<int64_t>(hist.size())};
         if (!d_params_.ensure(sizeof p) || !d_hist_.ensure(hist.size() * 4 + 4) || !d_hoff_.ensure(sizeof hoff) ||

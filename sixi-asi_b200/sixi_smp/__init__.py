@@ -97,6 +97,7 @@ SIGNATURES = {
     "sixi_smp_status_string": (ctypes.c_char_p, [_I32]),
     "sixi_smp_sample": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _P, _P, _U64, _P, _P, _P]),
     "sixi_smp_sample_host": (_I32, [_P, _P, _U32, _U32, _U64, _P, _P, _P, _P, _P, _U64, _P, _P, _P]),
+    "sixi_smp_sample_host_async": (_I32, [_P, _P, _U32, _U32, _U64, _P, _P, _P, _P, _P, _U64, _P, _P, _P]),
     "sixi_smp_greedy_argmax": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _P]),
     "sixi_smp_candidates": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _P, _U32, _P, _P, _P, _P, _P]),
     "sixi_smp_verify": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32, _P, _P, _P, _P, _P,
@@ -391,8 +392,10 @@ class Sampler:
 
     # -- host-buffer entry point ---------------------------------------------------------------
     def sample_host(self, logits: np.ndarray, params: np.ndarray, masks=None, hist=None, hist_off=None,
-                    uniforms=None, step=0, out_tokens=None, out_status=None, stream=None):
-        """logits: host array [n, stride] (float32, or uint16 holding bf16)."""
+                    uniforms=None, step=0, out_tokens=None, out_status=None, stream=None, wait: bool = True):
+        """logits: host array [n, stride] (float32, or uint16 holding bf16). With wait=False the call
+        is sixi_smp_sample_host_async: it returns once the work is queued, and the outputs are valid
+        after `stream` is synchronised (host buffers pinned and kept unchanged until then)."""
         n = logits.shape[0]
         dt = BF16 if logits.dtype == np.uint16 else F32
         if out_tokens is None:
@@ -403,10 +406,10 @@ class Sampler:
         def hp(a):
             return 0 if a is None else a.ctypes.data
 
-        st = _lib().sixi_smp_sample_host(self.h, hp(logits), dt, n, logits.shape[1], hp(params), hp(masks),
-                                      hp(hist), hp(hist_off), hp(uniforms), step, hp(out_tokens),
-                                      hp(out_status), self._stream(stream) if stream is not None else 0)
-        _check("sixi_smp_sample_host", st)
+        fn = _lib().sixi_smp_sample_host if wait else _lib().sixi_smp_sample_host_async
+        st = fn(self.h, hp(logits), dt, n, logits.shape[1], hp(params), hp(masks), hp(hist), hp(hist_off),
+                hp(uniforms), step, hp(out_tokens), hp(out_status), self._stream(stream) if stream is not None else 0)
+        _check("sixi_smp_sample_host" if wait else "sixi_smp_sample_host_async", st)
         return out_tokens, out_status
 
 

@@ -20,6 +20,10 @@
 //                           tests/test_routing_and_numerics.cpp:415-460, and a 151,936-wide row)
 //   suffix_drafter          suffix_propose / suffix_propose_anchored vs orc_suffix_draft (match
 //                           length, drafts, one-hot draft_probs)
+//   device_rows             a fake backend that keeps its logits in device memory (fp32 rows with a
+//                           padded stride, and bf16 rows): sample_token, sample_greedy_argmax and
+//                           verify on its device rows equal the host-row calls on the same values,
+//                           tokens and RNG state alike
 // Exit status 0 when every check passes. Needs a CUDA device.
 #include <algorithm>
 #include <cmath>
@@ -524,6 +528,122 @@ bool suffix_drafter() {
     return true;
 }
 
+// A backend whose output logits stay in device memory (the device-resident hand-off): a
+// [positions][stride] buffer, fp32 or bf16, with a view of any run of rows.
+struct FakeDeviceBackend {
+    void* d = nullptr;
+    uint32_t dtype = SIXI_SMP_F32;
+    uint64_t V = 0, stride = 0;
+    uint32_t n = 0;
+    FakeDeviceBackend(const std::vector<float>& rows, uint64_t vocab, uint64_t row_stride, uint32_t n_rows, bool bf16)
+        : dtype(bf16 ? SIXI_SMP_BF16 : SIXI_SMP_F32), V(vocab), stride(row_stride), n(n_rows) {
+        if (bf16) {
+            std::vector<uint16_t> h(static_cast<size_t>(n_rows) * row_stride, 0);
+            for (uint32_t r = 0; r < n_rows; ++r)
+                for (uint64_t i = 0; i < vocab; ++i) {
+                    uint32_t u;
+                    std::memcpy(&u, &rows[r * vocab + i], 4);
+                    h[r * row_stride + i] = static_cast<uint16_t>(u >> 16);  // rows are bf16 values already
+                }
+            cudaMalloc(&d, h.size() * 2);
+            cudaMemcpy(d, h.data(), h.size() * 2, cudaMemcpyHostToDevice);
+        } else {
+            std::vector<float> h(static_cast<size_t>(n_rows) * row_stride, 0.0f);
+            for (uint32_t r = 0; r < n_rows; ++r)
+                std::copy(rows.begin() + r * vocab, rows.begin() + (r + 1) * vocab, h.begin() + r * row_stride);
+            cudaMalloc(&d, h.size() * 4);
+            cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice);
+        }
+    }
+    ~FakeDeviceBackend() { cudaFree(d); }
+    sixi_smp_rows rows(uint32_t first, uint32_t count) const {
+        const size_t esz = dtype == SIXI_SMP_BF16 ? 2 : 4;
+        return sixi_smp_rows{static_cast<char*>(d) + first * stride * esz, dtype, count, stride};
+    }
+};
+
+float to_bf16_value(float x) {  // truncating conversion: the value a bf16 buffer holds exactly
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    u &= 0xFFFF0000u;
+    std::memcpy(&x, &u, 4);
+    return x;
+}
+
+bool device_rows() {
+    const uint64_t V = 151936;
+    const uint32_t k = 6;
+    TestRng gen(99);
+    auto made = DeviceSampler::create(0, 32, V);
+    CHECK(made.ok());
+    DeviceSampler& s = *made.value();
+    for (int it = 0; it < 6; ++it) {
+        const bool bf16 = it % 2 == 1;
+        std::vector<float> rows((k + 1) * V);
+        for (uint32_t r = 0; r <= k; ++r) {
+            auto x = normal_row(gen, V, 3.0f);
+            for (uint64_t i = 0; i < V; ++i) rows[r * V + i] = bf16 ? to_bf16_value(x[i]) : x[i];
+        }
+        std::vector<float> q(k * V);
+        std::vector<int32_t> drafts(k);
+        for (uint32_t i = 0; i < k; ++i) {
+            double z = 0.0, m = -1e300;
+            for (uint64_t j = 0; j < V; ++j) m = std::max(m, static_cast<double>(rows[i * V + j]));
+            for (uint64_t j = 0; j < V; ++j) z += std::exp(rows[i * V + j] - m);
+            int32_t best = 0;
+            for (uint64_t j = 0; j < V; ++j) {
+                q[i * V + j] = static_cast<float>(std::exp(rows[i * V + j] - m) / z);
+                if (rows[i * V + j] > rows[i * V + best]) best = static_cast<int32_t>(j);
+            }
+            drafts[i] = (i + static_cast<uint32_t>(it)) % 3 == 0 ? static_cast<int32_t>(gen.next_u64() % V) : best;
+        }
+        const FakeDeviceBackend be(rows, V, V + 64 * (it % 3), k + 1, bf16);
+        float* dq = nullptr;
+        CHECK(cudaMalloc(&dq, q.size() * 4) == cudaSuccess);
+        cudaMemcpy(dq, q.data(), q.size() * 4, cudaMemcpyHostToDevice);
+        SamplingParams p;
+        p.temperature = it == 4 ? 0.0f : 0.8f;
+        p.top_k = it % 3 == 0 ? 0 : 40;
+        p.top_p = 0.9f;
+        p.repetition_penalty = 1.15f;
+        p.mode = ExecutionMode::Adaptive;
+        std::vector<int32_t> ctx(300);
+        for (auto& c : ctx) c = static_cast<int32_t>(gen.next_u64() % V);
+        // sample_token and the raw argmax, row by row
+        for (uint32_t r = 0; r <= k; ++r) {
+            TestRng a(1000 + r), b(1000 + r);
+            auto th = s.sample_token(&rows[r * V], V, p, a, ctx);
+            auto td = s.sample_token(be.rows(r, 1), p, b, ctx);
+            CHECK(th.ok() && td.ok());
+            CHECK(th.value() == td.value());
+            CHECK(a.checkpoint() == b.checkpoint());
+            CHECK(s.sample_greedy_argmax(&rows[r * V], V) == s.sample_greedy_argmax(be.rows(r, 1)));
+        }
+        // verify: dense q and one-hot
+        for (int dense = 0; dense < 2; ++dense) {
+            TestRng a(55 + it), b(55 + it);
+            auto vh = s.verify(rows.data(), dense ? q.data() : nullptr, drafts, p, a, ctx);
+            auto vd = s.verify(be.rows(0, k + 1), dense ? dq : nullptr, drafts, p, b, ctx);
+            CHECK(vh.ok() && vd.ok());
+            CHECK(vh.value().committed_tokens == vd.value().committed_tokens);
+            CHECK(vh.value().accepted_draft_count == vd.value().accepted_draft_count);
+            CHECK(vh.value().first_rejected_position == vd.value().first_rejected_position);
+            CHECK(a.checkpoint() == b.checkpoint());
+        }
+        cudaFree(dq);
+    }
+    // wrong shapes are refused without touching the RNG
+    TestRng r(5);
+    const uint64_t before = r.checkpoint();
+    SamplingParams p;
+    p.temperature = 0.7f;
+    CHECK(!s.sample_token(sixi_smp_rows{nullptr, SIXI_SMP_F32, 1, V}, p, r).ok());
+    CHECK(!s.verify(sixi_smp_rows{reinterpret_cast<void*>(16), SIXI_SMP_F32, 3, V}, nullptr,
+                    std::vector<int32_t>{1, 2, 3}, p, r, {}).ok());
+    CHECK(r.checkpoint() == before);
+    return true;
+}
+
 int main() {
     struct {
         const char* name;
@@ -536,7 +656,8 @@ int main() {
                  {"verify_forced_rejection", verify_forced_rejection},
                  {"json_constrained", json_constrained},
                  {"numeric_policy", numeric_policy},
-                 {"suffix_drafter", suffix_drafter}};
+                 {"suffix_drafter", suffix_drafter},
+                 {"device_rows", device_rows}};
     int passed = 0, n = 0;
     for (auto& t : tests) {
         ++n;

@@ -458,3 +458,27 @@ def test_topp_cut_position_on_mass_path(port, seed):
             excused += 1
     print(f"top-p cuts: {rows} rows, {excused} within 1e-6 of top_p and moved, smallest gap {min(gaps):.2e}")
     assert excused <= max_excused(rows)
+
+
+def test_sample_host_async_pipelined_batches(port):
+    """sixi_smp_sample_host_async: five config-2 batches queued back to back (two staging slots, so
+    batch i+1's copy overlaps batch i's kernel), one synchronisation at the end; every batch's
+    tokens and statuses equal the blocking host call's and the oracle's."""
+    rows = 16
+    smp = S.Sampler(0, 64, W.QWEN_VOCAB)
+    stream = torch.cuda.Stream(device=DEV)
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()  # noqa: E731
+    ds = [W.config2(rows=rows, seed=900 + i) for i in range(5)]
+    us = [np.random.default_rng(900 + i).random(rows) for i in range(5)]
+    ins = [(pin(d["logits"]), pin(d["params"].view(np.uint8)).view(S.PARAMS_DTYPE), pin(d["hist"]),
+            pin(d["hist_off"]), pin(u)) for d, u in zip(ds, us)]
+    outs = [(pin(np.full(rows, -7, np.int32)), pin(np.full(rows, -7, np.int32))) for _ in ds]
+    for (lg, prm, h, ho, u), (tok, st) in zip(ins, outs):
+        smp.sample_host(lg, prm, hist=h, hist_off=ho, uniforms=u, out_tokens=tok, out_status=st, stream=stream,
+                        wait=False)
+    stream.synchronize()
+    for (lg, prm, h, ho, u), (tok, st), d in zip(ins, outs, ds):
+        t2, s2 = smp.sample_host(lg, prm, hist=h, hist_off=ho, uniforms=u, stream=stream)
+        assert np.array_equal(tok, t2) and np.array_equal(st, s2)
+        check_against_oracle(port, d, u, tok, st)
+    smp.close()

@@ -765,16 +765,12 @@ def run_config5_sharded(args) -> int:
         mark("exchange")
         tok, sts = smp.merge_shards(gc, gs, params, uniforms=u, step=i, stream=cs)
         mark("stage2")
-        rows = (sts == 2).nonzero().flatten()
+        rows = (sts == 2).nonzero().flatten().to(torch.int32)
         if rows.numel():
-            fr = torch.cat(slices, dim=1)[rows].contiguous()
-            p = params.view(B, -1)[rows].contiguous()
-            from sixi_smp.sharded import _subset_csr
-
-            h, ho = _subset_csr(hist, hoff, rows)
-            t2, s2 = smp.sample(fr, p, hist=h, hist_off=ho, uniforms=u[rows].contiguous(), step=i, stream=cs)
-            tok[rows] = t2
-            sts[rows] = s2
+            fr = torch.empty((rows.numel(), VOCAB), dtype=torch.float32, device=dev)
+            for r in range(n_shards):  # each slice's flagged rows into its columns of the rebuilt rows
+                smp.gather_rows(slices[r], rows, lay.width(r), out=fr[:, lay.offset(r):], stream=cs)
+            smp.sample_indexed(fr, rows, params, tok, sts, hist=hist, hist_off=hoff, uniforms=u, step=i, stream=cs)
         mark("round2")
         return tok, sts
 

@@ -114,6 +114,28 @@ SIXI_SMP_API int32_t sixi_smp_sample(sixi_smp* h, const sixi_smp_rows* rows, con
                         int32_t* out_tokens, int32_t* out_status, void* stream);
 
 /*
+ * sixi_smp_sample over rows picked out of a batch (no counterpart in the engine): row j of `rows`
+ * is sampled with the parameters, mask, history and uniform of batch row row_map[j], and its token
+ * and status go to out_tokens[row_map[j]] and out_status[row_map[j]]; the other slots are left as
+ * they are. row_map: device memory, rows->n_rows distinct batch-row indices; params, mask_words,
+ * hist_*, uniforms and the outputs are the whole batch's arrays. The vocab-sharded mode's second
+ * round samples its rebuilt rows this way, without building subset arrays.
+ */
+SIXI_SMP_API int32_t sixi_smp_sample_indexed(sixi_smp* h, const sixi_smp_rows* rows, const uint32_t* row_map,
+                                            const sixi_smp_params* params, const uint32_t* mask_words,
+                                            const int32_t* hist_tokens, const int64_t* hist_offsets,
+                                            const double* uniforms, uint64_t step, int32_t* out_tokens,
+                                            int32_t* out_status, void* stream);
+
+/*
+ * Row gather on the device (no counterpart in the engine): dst row j = the first `width` elements
+ * of src row row_index[j], rows of src's dtype, dst rows dst_stride elements apart; n <= 65,535.
+ * Packs the rows of a batch that a second exchange round needs.
+ */
+SIXI_SMP_API int32_t sixi_smp_gather_rows(sixi_smp* h, const sixi_smp_rows* src, const int32_t* row_index,
+                                         uint32_t n, uint32_t width, void* dst, uint64_t dst_stride, void* stream);
+
+/*
  * Same as sixi_smp_sample with HOST inputs and outputs: copies the logits (pinned host memory
  * recommended), params, masks, histories and uniforms to handle-owned device staging, samples, and
  * copies tokens and statuses back, then synchronises `stream`. This is the engine-facing call

@@ -295,6 +295,42 @@ int32_t sixi_smp_sample(sixi_smp* h, const sixi_smp_rows* rows, const sixi_smp_p
                                             static_cast<cudaStream_t>(stream)));
 }
 
+int32_t sixi_smp_sample_indexed(sixi_smp* h, const sixi_smp_rows* rows, const uint32_t* row_map,
+                                const sixi_smp_params* params, const uint32_t* mask_words, const int32_t* hist_tokens,
+                                const int64_t* hist_offsets, const double* uniforms, uint64_t step,
+                                int32_t* out_tokens, int32_t* out_status, void* stream) {
+    if (h == nullptr || !rows_ok(h, rows) || row_map == nullptr || params == nullptr || out_tokens == nullptr ||
+        out_status == nullptr || (hist_tokens != nullptr && hist_offsets == nullptr))
+        return SIXI_INVALID_ARGUMENT;
+    if (rows->n_rows == 0) return SIXI_OK;
+    DeviceGuard g(h->device);
+    LaunchPlan plan{};
+    RowArgs a = base_args(h, rows, &plan);
+    a.params = params;
+    a.mask = mask_words;
+    a.hist = hist_tokens;
+    a.hist_off = hist_tokens ? hist_offsets : nullptr;
+    a.uniforms = uniforms;
+    a.step = step;
+    a.row_map = row_map;
+    a.out_tok = out_tokens;
+    a.out_status = out_status;
+    return from_cuda(sixi_b200::launch_rows(sixi_b200::kModeSample, a, plan, static_cast<cudaStream_t>(stream)));
+}
+
+int32_t sixi_smp_gather_rows(sixi_smp* h, const sixi_smp_rows* src, const int32_t* row_index, uint32_t n,
+                             uint32_t width, void* dst, uint64_t dst_stride, void* stream) {
+    if (h == nullptr || src == nullptr || (src->dtype != SIXI_SMP_F32 && src->dtype != SIXI_SMP_BF16) ||
+        width > src->row_stride || width > dst_stride || n > 65535u ||
+        (n > 0 && (src->data == nullptr || row_index == nullptr || dst == nullptr)))
+        return SIXI_INVALID_ARGUMENT;
+    if (n == 0 || width == 0) return SIXI_OK;
+    DeviceGuard g(h->device);
+    return from_cuda(sixi_b200::launch_gather_rows(src->data, src->row_stride, src->dtype == SIXI_SMP_BF16 ? 2u : 4u,
+                                                   row_index, n, width, dst, dst_stride,
+                                                   static_cast<cudaStream_t>(stream)));
+}
+
 int32_t sixi_smp_sample_host_async(sixi_smp* h, const void* host_logits, uint32_t dtype, uint32_t n_rows,
                                    uint64_t row_stride, const sixi_smp_params* host_params,
                                    const uint32_t* host_mask_words, const int32_t* host_hist_tokens,

@@ -53,6 +53,9 @@ struct RowArgs {
     const int64_t* hist_off;
     const double* uniforms;
     uint64_t step;
+    // sample mode: row j of `data` is sampled as row row_map[j] (its parameters, mask, history,
+    // uniform and output slots); nullptr = the identity
+    const uint32_t* row_map;
     // verify
     const float* q;            // dense draft probabilities [S*k][row_stride], or
     const void* qlog;          // draft logits [S*k][qlog_stride] (dtype qlog_dtype) with their
@@ -170,5 +173,7 @@ cudaError_t launch_full_distribution(const DistArgs& a, const LaunchPlan& plan, 
 cudaError_t prepare_full_distribution(int device);  // its launch attributes, once per device
 cudaError_t launch_shard_candidates(const ShardArgs& a, cudaStream_t stream);
 cudaError_t launch_merge_shards(const MergeArgs& a, cudaStream_t stream);
+cudaError_t launch_gather_rows(const void* src, uint64_t src_stride, uint32_t esz, const int32_t* index, uint32_t n,
+                               uint32_t width, void* dst, uint64_t dst_stride, cudaStream_t stream);
 
 }  // namespace sixi_b200

@@ -175,6 +175,7 @@ struct RowCtx {
     int32_t greedy;         // temperature <= 0 (or the raw-argmax entry)
     uint32_t stream;
     uint32_t vidx;          // verify: position i within the stream
+    uint32_t orow;          // row of the parameter, mask, history, uniform and output arrays
     double u_draw;          // uniform of the draw (sample/bonus) or of the residual (draft row)
     double u_accept;        // verify draft row: accept uniform
 };
@@ -225,17 +226,20 @@ __device__ RowCtx make_row_ctx(const RowArgs& a, uint32_t row) {
             }
         }
     } else {
+        const uint32_t orow = (MODE == kModeSample && a.row_map != nullptr) ? a.row_map[row] : row;
+        r.orow = orow;
         // the raw-argmax entry passes one default record for all rows
-        r.p = (MODE == kModeGreedy) ? a.params : &a.params[row];
+        r.p = (MODE == kModeGreedy) ? a.params : &a.params[orow];
         r.greedy = (MODE == kModeGreedy) ? 1 : (r.p->temperature <= 0.0f);
         if (a.hist && a.hist_off && MODE != kModeGreedy) {
-            r.hist = a.hist + a.hist_off[row];
-            r.nh = a.hist_off[row + 1] - a.hist_off[row];
+            r.hist = a.hist + a.hist_off[orow];
+            r.nh = a.hist_off[orow + 1] - a.hist_off[orow];
         }
-        if (MODE == kModeSample && !r.greedy) r.u_draw = row_uniform(a, r.p, row, 0);
+        if (MODE == kModeSample && !r.greedy) r.u_draw = row_uniform(a, r.p, orow, 0);
     }
+    if (MODE == kModeVerify) r.orow = row;
     if (a.mask != nullptr && (MODE == kModeGreedy || (r.p->flags & SIXI_SMP_ROW_MASKED))) {
-        r.mask = a.mask + static_cast<size_t>(row) * a.mask_words;
+        r.mask = a.mask + static_cast<size_t>(r.orow) * a.mask_words;
     } else {
         r.mask = nullptr;
     }
@@ -1744,8 +1748,8 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             }
         } else {
             const bool ok = res_status == SIXI_OK || (MODE == kModeGreedy && res_status == SIXI_NUMERIC_NAN_OR_INF);
-            a.out_tok[row] = ok ? res_token : -1;
-            a.out_status[row] = res_status;
+            a.out_tok[rc.orow] = ok ? res_token : -1;
+            a.out_status[rc.orow] = res_status;
         }
     };
 

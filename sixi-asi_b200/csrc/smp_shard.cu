@@ -477,4 +477,33 @@ cudaError_t launch_merge_shards(const MergeArgs& a, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
+namespace {
+
+// dst row j = the first `width` elements of src row index[j] (element size 2 or 4 bytes);
+// blockIdx.y picks the row, the x blocks stride over its elements
+template <typename T>
+__global__ void gather_rows_kernel(const T* __restrict__ src, uint64_t src_stride, const int32_t* __restrict__ index,
+                                   uint32_t width, T* __restrict__ dst, uint64_t dst_stride) {
+    const uint32_t j = blockIdx.y;
+    const T* s = src + static_cast<uint64_t>(index[j]) * src_stride;
+    T* d = dst + static_cast<uint64_t>(j) * dst_stride;
+    for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < width; e += gridDim.x * blockDim.x) d[e] = s[e];
+}
+
+}  // namespace
+
+cudaError_t launch_gather_rows(const void* src, uint64_t src_stride, uint32_t esz, const int32_t* index, uint32_t n,
+                               uint32_t width, void* dst, uint64_t dst_stride, cudaStream_t stream) {
+    if (n == 0 || width == 0) return cudaSuccess;
+    if (n > 65535u) return cudaErrorInvalidValue;  // one grid row per gathered row
+    const dim3 grid((width + 1023u) / 1024u < 32u ? (width + 1023u) / 1024u : 32u, n);
+    if (esz == 2)
+        gather_rows_kernel<uint16_t><<<grid, 256, 0, stream>>>(static_cast<const uint16_t*>(src), src_stride, index,
+                                                                width, static_cast<uint16_t*>(dst), dst_stride);
+    else
+        gather_rows_kernel<uint32_t><<<grid, 256, 0, stream>>>(static_cast<const uint32_t*>(src), src_stride, index,
+                                                                width, static_cast<uint32_t*>(dst), dst_stride);
+    return cudaGetLastError();
+}
+
 }  // namespace sixi_b200

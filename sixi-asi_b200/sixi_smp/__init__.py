@@ -98,6 +98,8 @@ SIGNATURES = {
     "sixi_smp_sample": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _P, _P, _U64, _P, _P, _P]),
     "sixi_smp_sample_host": (_I32, [_P, _P, _U32, _U32, _U64, _P, _P, _P, _P, _P, _U64, _P, _P, _P]),
     "sixi_smp_sample_host_async": (_I32, [_P, _P, _U32, _U32, _U64, _P, _P, _P, _P, _P, _U64, _P, _P, _P]),
+    "sixi_smp_sample_indexed": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _U64, _P, _P, _P]),
+    "sixi_smp_gather_rows": (_I32, [_P, _P, _P, _U32, _U32, _P, _U64, _P]),
     "sixi_smp_greedy_argmax": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _P]),
     "sixi_smp_candidates": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _P, _U32, _P, _P, _P, _P, _P]),
     "sixi_smp_verify": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _U32, _U32, _P, _P, _P, _P, _P,
@@ -239,6 +241,30 @@ class Sampler:
                                  _ptr(out_status), self._stream(stream))
         _check("sixi_smp_sample", st)
         return out_tokens, out_status
+
+    def sample_indexed(self, logits, row_map, params, out_tokens, out_status, masks=None, hist=None, hist_off=None,
+                       uniforms=None, step=0, stream=None):
+        """sixi_smp_sample_indexed: row j of `logits` sampled as batch row row_map[j] (int32 device
+        tensor); params / masks / hist / uniforms / outputs are the whole batch's."""
+        rows = self._rows(logits)
+        st = _lib().sixi_smp_sample_indexed(self.h, ctypes.byref(rows), _ptr(row_map), _ptr(params), _ptr(masks),
+                                            _ptr(hist), _ptr(hist_off), _ptr(uniforms), step, _ptr(out_tokens),
+                                            _ptr(out_status), self._stream(stream))
+        _check("sixi_smp_sample_indexed", st)
+        return out_tokens, out_status
+
+    def gather_rows(self, src, row_index, width: int, out=None, stream=None):
+        """sixi_smp_gather_rows: out[j, :width] = src[row_index[j], :width] (device tensors)."""
+        import torch
+
+        n = int(row_index.numel())
+        if out is None:
+            out = torch.empty((n, width), dtype=src.dtype, device=src.device)
+        rows = self._rows(src)
+        st = _lib().sixi_smp_gather_rows(self.h, ctypes.byref(rows), _ptr(row_index), n, width, _ptr(out),
+                                         out.stride(0), self._stream(stream))
+        _check("sixi_smp_gather_rows", st)
+        return out
 
     def greedy_argmax(self, logits, masks=None, stream=None):
         import torch

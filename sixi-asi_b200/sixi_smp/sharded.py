@@ -6,8 +6,8 @@ vocabulary of every row (logits produced vocab-parallel). One step is
   stage 2   sixi_smp_merge_shards, identical on every rank -> the token of every row
   round 2   only for rows whose kept set or draw reaches past the gathered candidates (stage 2
             reports SIXI_OUT_OF_BOUNDS, which can happen for top_k = 0 or top_k > top_n): their
-            slices are all-gathered, every rank rebuilds the full rows and samples them with
-            sixi_smp_sample
+            slices are packed (sixi_smp_gather_rows) and all-gathered, every rank rebuilds the full
+            rows and samples them with sixi_smp_sample_indexed (each as its batch row)
 
 so every rank ends with the same tokens, as sixi_smp_sample on the full rows draws them, for every
 row. The flagged rows are the same on every rank (stage 2 is deterministic on identical data), so
@@ -42,21 +42,6 @@ class ShardLayout:
 OUT_OF_BOUNDS = 2
 
 
-def _subset_csr(hist, hist_off, rows):
-    """The history lists of `rows` (device tensors): (tokens, offsets) of the subset."""
-    import torch
-
-    lens = (hist_off[1:] - hist_off[:-1])[rows]
-    off = torch.zeros(rows.numel() + 1, dtype=hist_off.dtype, device=hist_off.device)
-    off[1:] = torch.cumsum(lens, 0)
-    total = int(off[-1])
-    if total == 0:
-        return hist[:0], off
-    start = torch.repeat_interleave(hist_off[:-1][rows], lens)
-    within = torch.arange(total, device=hist.device, dtype=hist_off.dtype) - torch.repeat_interleave(off[:-1], lens)
-    return hist[start + within], off
-
-
 def sample_vocab_sharded(shard_logits, layout: ShardLayout, rank: int, params, *, top_n: int = 64,
                          masks=None, hist=None, hist_off=None, uniforms=None, step: int = 0,
                          stage1: Callable | None = None, stage2: Callable | None = None,
@@ -73,11 +58,14 @@ def sample_vocab_sharded(shard_logits, layout: ShardLayout, rank: int, params, *
 
     if full_rows is None:
         def full_rows(full, rows):
-            p = params.view(-1, params.numel() // shard_logits.shape[0])[rows].contiguous()
-            m = None if masks is None else masks[rows].contiguous()
-            h, ho = (None, None) if hist is None else _subset_csr(hist, hist_off, rows)
-            uu = None if uniforms is None else uniforms[rows].contiguous()
-            return sampler.sample(full, p, masks=m, hist=h, hist_off=ho, uniforms=uu, step=step, stream=stream)
+            # sixi_smp_sample_indexed: rebuilt row j is sampled as batch row rows[j], with the batch's
+            # own parameter, mask, history and uniform arrays
+            n = shard_logits.shape[0]
+            t = torch.empty(n, dtype=torch.int32, device=full.device)
+            st = torch.empty(n, dtype=torch.int32, device=full.device)
+            sampler.sample_indexed(full, rows.to(torch.int32), params, t, st, masks=masks, hist=hist,
+                                   hist_off=hist_off, uniforms=uniforms, step=step, stream=stream)
+            return t[rows], st[rows]
 
     if stage1 is None:
         def stage1(x, off, width):
@@ -108,7 +96,10 @@ def sample_vocab_sharded(shard_logits, layout: ShardLayout, rank: int, params, *
     if n_f:
         wmax = max(layout.width(r) for r in range(world))
         part = torch.zeros((n_f, wmax), dtype=shard_logits.dtype, device=shard_logits.device)
-        part[:, :layout.width(rank)] = shard_logits[rows.to(shard_logits.device)]
+        if sampler is not None:
+            sampler.gather_rows(shard_logits, rows.to(torch.int32), layout.width(rank), out=part, stream=stream)
+        else:
+            part[:, :layout.width(rank)] = shard_logits[rows.to(shard_logits.device)]
         g_rows = torch.empty((world * n_f, wmax), dtype=part.dtype, device=part.device)
         dist.all_gather_into_tensor(g_rows, part, group=group)
         g_rows = g_rows.view(world, n_f, wmax)

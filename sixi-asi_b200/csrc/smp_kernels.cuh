@@ -83,7 +83,7 @@ struct LaunchPlan {
 };
 
 // Launch plan for a vocabulary and batch: the smallest cluster whose chunk fits shared memory,
-// widened (up to 16 CTAs) while the batch leaves more than half of the device's `sms` SMs idle
+// widened (up to 8 CTAs) while the batch leaves more than half of the device's `sms` SMs idle
 // (sms = 0: no widening; the plan then only validates the vocabulary).
 bool plan_rows(uint32_t vocab, uint32_t n_rows, uint32_t sms, LaunchPlan* plan);
 // Streaming multiprocessors of `device` (queried once per device; 0 when the query fails).

@@ -434,8 +434,8 @@ public:
     }
 
     // verify on k + 1 device rows (`target.n_rows` == drafts.size() + 1: the rows of one stream's
-    // verify pass) with dense draft probabilities in device memory (`d_draft_probs` [k][row_stride]
-    // fp32) or none (one-hot rule).
+    // verify pass) with dense draft probabilities in device memory (`d_draft_probs`: k fp32 rows,
+    // target.row_stride elements apart, as the verifier reads them) or none (one-hot rule).
     template <class P, class Rng>
     Result<VerifyResult> verify(const sixi_smp_rows& target, const float* d_draft_probs,
                                 const std::vector<int32_t>& drafts, const P& params, Rng& rng,

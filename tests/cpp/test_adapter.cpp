@@ -598,9 +598,10 @@ bool device_rows() {
             drafts[i] = (i + static_cast<uint32_t>(it)) % 3 == 0 ? static_cast<int32_t>(gen.next_u64() % V) : best;
         }
         const FakeDeviceBackend be(rows, V, V + 64 * (it % 3), k + 1, bf16);
+        // q rows on the device are the target rows' stride apart, as the verifier reads them
         float* dq = nullptr;
-        CHECK(cudaMalloc(&dq, q.size() * 4) == cudaSuccess);
-        cudaMemcpy(dq, q.data(), q.size() * 4, cudaMemcpyHostToDevice);
+        CHECK(cudaMalloc(&dq, k * be.stride * 4) == cudaSuccess);
+        CHECK(cudaMemcpy2D(dq, be.stride * 4, q.data(), V * 4, V * 4, k, cudaMemcpyHostToDevice) == cudaSuccess);
         SamplingParams p;
         p.temperature = it == 4 ? 0.0f : 0.8f;
         p.top_k = it % 3 == 0 ? 0 : 40;

@@ -29,6 +29,7 @@ constexpr int kSh = 512;                 // threads of the shard and merge block
 constexpr int kShW = kSh / 32;
 constexpr uint32_t kCollectCap = 4096;   // candidates collected per row before ranking
 constexpr uint32_t kMaxMerge = 1024;     // n_shards * top_n handled by one merge block
+constexpr int kUnroll = 8;               // global loads in flight per thread in stage 1's loops
 
 struct ShardShared {
     unsigned long long red[kShW];
@@ -126,14 +127,23 @@ __global__ void __launch_bounds__(kSh, 1) shard_kernel(const ShardArgs a) {
         if (P.frequency_penalty != 0.0f && h1 - h0 > 65535) {
             if (tid == 0) sh->flags |= 2u;  // a count could pass 16 bits
         }
-        for (int64_t j = h0 + tid; j < h1; j += kSh) {
-            const int32_t t = a.hist[j];
-            if (t < static_cast<int32_t>(a.vocab_offset) ||
-                t >= static_cast<int32_t>(a.vocab_offset + a.shard_vocab) ||
-                !bit_allowed(mask, static_cast<uint32_t>(t)))
-                continue;
-            const uint32_t e = static_cast<uint32_t>(t) - a.vocab_offset;
-            atomicAdd(&cnt[e >> 1], 1u << (16u * (e & 1u)));
+        for (int64_t j0 = h0 + tid; j0 < h1; j0 += kUnroll * kSh) {  // kUnroll loads in flight
+            int32_t t8[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int64_t j = j0 + static_cast<int64_t>(u) * kSh;
+                t8[u] = j < h1 ? a.hist[j] : -1;
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int32_t t = t8[u];
+                if (t < static_cast<int32_t>(a.vocab_offset) ||
+                    t >= static_cast<int32_t>(a.vocab_offset + a.shard_vocab) ||
+                    !bit_allowed(mask, static_cast<uint32_t>(t)))
+                    continue;
+                const uint32_t e = static_cast<uint32_t>(t) - a.vocab_offset;
+                atomicAdd(&cnt[e >> 1], 1u << (16u * (e & 1u)));
+            }
         }
     }
     __syncthreads();
@@ -146,14 +156,24 @@ __global__ void __launch_bounds__(kSh, 1) shard_kernel(const ShardArgs a) {
     uint32_t n_al = 0u;
     unsigned long long best = 0ull;
     bool bad = false;
-    for (uint32_t e = tid; e < a.shard_vocab; e += kSh) {
-        const uint32_t gid = a.vocab_offset + e;
-        if (!bit_allowed(mask, gid)) continue;
-        const float raw = shard_logit(a, rowp, e);
-        bad |= !isfinite(raw);
-        ++n_al;
-        const unsigned long long c = comp_of(fkey(adjusted(e, raw)), gid);
-        best = c > best ? c : best;
+    for (uint32_t e0 = tid; e0 < a.shard_vocab; e0 += kUnroll * kSh) {  // kUnroll loads in flight
+        float x8[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const uint32_t e = e0 + u * kSh;
+            x8[u] = e < a.shard_vocab ? shard_logit(a, rowp, e) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const uint32_t e = e0 + u * kSh;
+            const uint32_t gid = a.vocab_offset + e;
+            if (e >= a.shard_vocab || !bit_allowed(mask, gid)) continue;
+            const float raw = x8[u];
+            bad |= !isfinite(raw);
+            ++n_al;
+            const unsigned long long c = comp_of(fkey(adjusted(e, raw)), gid);
+            best = c > best ? c : best;
+        }
     }
     tmax[tid] = best;
     const uint32_t n_allowed = blk_sum32(n_al, sh);
@@ -187,16 +207,26 @@ __global__ void __launch_bounds__(kSh, 1) shard_kernel(const ShardArgs a) {
     WeightCtx wc{};
     if (sampled) make_weight_ctx(P.temperature, xmax, 46.0f, wc);
     double se = 0.0;
-    for (uint32_t e = tid; e < a.shard_vocab; e += kSh) {
-        const uint32_t gid = a.vocab_offset + e;
-        if (!bit_allowed(mask, gid)) continue;
-        const float x = adjusted(e, shard_logit(a, rowp, e));
-        const unsigned long long c = comp_of(fkey(x), gid);
-        if (c >= theta) {
-            const uint32_t slot = atomicAdd(&sh->fill, 1u);
-            if (slot < kCollectCap) list[slot] = c;
+    for (uint32_t e0 = tid; e0 < a.shard_vocab; e0 += kUnroll * kSh) {  // kUnroll loads in flight
+        float x8[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const uint32_t e = e0 + u * kSh;
+            x8[u] = e < a.shard_vocab ? shard_logit(a, rowp, e) : 0.0f;
         }
-        if (sampled) se += static_cast<double>(fast_ex2(fminf(neg_log2w(x, wc), 0.0f)));
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const uint32_t e = e0 + u * kSh;
+            const uint32_t gid = a.vocab_offset + e;
+            if (e >= a.shard_vocab || !bit_allowed(mask, gid)) continue;
+            const float x = adjusted(e, x8[u]);
+            const unsigned long long c = comp_of(fkey(x), gid);
+            if (c >= theta) {
+                const uint32_t slot = atomicAdd(&sh->fill, 1u);
+                if (slot < kCollectCap) list[slot] = c;
+            }
+            if (sampled) se += static_cast<double>(fast_ex2(fminf(neg_log2w(x, wc), 0.0f)));
+        }
     }
     const double sum_exp = sampled ? blk_sumd(se, sh) : 0.0;
     uint32_t n_col = sh->fill;

@@ -59,7 +59,7 @@ def build(jobs: int | None = None, force: bool = False, verbose: bool = True) ->
         for dname, d in DTYPES.items():
             units.append((CSRC / "smp_inst.cu", BUILD / f"inst_{mname}_{dname}.o",
                           [f"-DSIXI_INST_MODE={m}", f"-DSIXI_INST_DT={d}"]))
-    for name in ("smp_launch", "smp_abi", "smp_shard", "smp_dist", "smp_json", "smp_numeric", "smp_suffix"):
+    for name in ("smp_launch", "smp_abi", "smp_shard", "smp_dist", "smp_json", "smp_numeric", "smp_suffix", "smp_schema"):
         units.append((CSRC / f"{name}.cu", BUILD / f"{name}.o", []))
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
         futs = [ex.submit(_compile, s, o, d, force) for s, o, d in units]

@@ -123,6 +123,15 @@ SIGNATURES = {
     "sixi_json_fill_masks": (_I32, [_P, _P, _U32, _P, _U64, _P]),
     "sixi_json_advance": (_I32, [_P, _P, _U32, _P, _U64, _P, _P, _P]),
     "sixi_json_expand_drafts": (_I32, [_P, _P, _U32, _P, _U32, _P, _P, _P]),
+    # json_schema grammar masks (include/sixi_schema.h)
+    "sixi_schema_compile": (_I32, [_I32, _P, ctypes.c_size_t, _P, _P, _U32, _P, _I32, _P, ctypes.c_size_t,
+                                   ctypes.POINTER(_P)]),
+    "sixi_schema_destroy": (None, [_P]),
+    "sixi_schema_vocab_size": (_U32, [_P]),
+    "sixi_schema_reset": (_I32, [_P, _P, _U32, _P]),
+    "sixi_schema_fill_masks": (_I32, [_P, _P, _U32, _P, _U64, _P]),
+    "sixi_schema_advance": (_I32, [_P, _P, _U32, _P, _U64, _P, _P, _P]),
+    "sixi_schema_check_text": (_I32, [_P, _P, ctypes.c_size_t]),
 }
 
 

@@ -21,14 +21,14 @@ def declared_symbols() -> list[str]:
     names = set()
     for h in HEADERS:
         text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
-        names |= set(re.findall(r"\b(sixi_(?:smp|json)_[a-z_]+)\s*\(", text))
+        names |= set(re.findall(r"\b(sixi_(?:smp|json|schema)_[a-z_]+)\s*\(", text))
     return sorted(names)
 
 
 def test_library_exports_every_declared_symbol():
     assert LIB.exists(), "build the library first (python sixi-asi_b200/build_lib.py)"
     out = subprocess.run(["nm", "-D", "--defined-only", str(LIB)], capture_output=True, text=True, check=True).stdout
-    exported = set(re.findall(r"\bT (sixi_(?:smp|json)_\w+)", out))
+    exported = set(re.findall(r"\bT (sixi_(?:smp|json|schema)_\w+)", out))
     missing = [s for s in declared_symbols() if s not in exported]
     assert not missing, missing
     # nothing else leaks from the library (kernels and helpers are hidden)

@@ -1314,13 +1314,16 @@ __global__ void schema_reset_kernel(State* s, uint32_t n, uint32_t root) {
 __global__ void __launch_bounds__(kMaskThreads) schema_mask_kernel(const Prog P, const SVocab V, const State* states,
                                                                    uint32_t* masks, uint64_t stride) {
     __shared__ State st;
+    __shared__ uint32_t st_ok;
     const uint32_t row = blockIdx.y;
     const uint32_t* src = reinterpret_cast<const uint32_t*>(&states[row]);
     for (uint32_t i = threadIdx.x; i < sizeof(State) / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(&st)[i] = src[i];
     __syncthreads();
+    if (threadIdx.x == 0) st_ok = state_ok(P, st) ? 1u : 0u;
+    __syncthreads();
     const uint32_t words = (V.vocab + 31u) / 32u;
     uint32_t* out = masks + static_cast<uint64_t>(row) * stride;
-    const bool dead = st.failed != 0u || st.depth == 0u;
+    const bool dead = st.failed != 0u || st.depth == 0u || st_ok == 0u;  // no token for a malformed state
     const uint32_t lane = threadIdx.x & 31u;
     for (uint32_t w = blockIdx.x * (kMaskThreads / 32) + threadIdx.x / 32; w < words;
          w += gridDim.x * (kMaskThreads / 32)) {
@@ -1377,6 +1380,13 @@ __global__ void schema_advance_kernel(const Prog P, const SVocab V, State* state
     State s = states[r];
     const int32_t n = n_tokens ? n_tokens[r] : 1;
     int32_t status = SIXI_OK;
+    if (!state_ok(P, s)) {  // a malformed state is frozen, not walked
+        s.failed = 1u;
+        if (s.depth > static_cast<uint32_t>(kMaxDepth)) s.depth = 0u;
+        states[r] = s;
+        if (out_status) out_status[r] = SIXI_INVALID_ARGUMENT;
+        return;
+    }
     for (int32_t j = 0; j < n; ++j) {
         if (!apply_token(P, V, s, tokens[static_cast<uint64_t>(r) * token_stride + j])) {
             s.failed = 1u;
@@ -1430,7 +1440,89 @@ struct sixi_schema {
         p.any_string = any_string;
         p.any_number = any_number;
         p.any_literal = any_literal;
+        p.n_nodes = static_cast<uint32_t>(nodes.size());
+        p.n_dfas = static_cast<uint32_t>(dfas.size());
         return p;
+    }
+
+    // Unions whose alternatives are unions (possible through a $ref to an anyOf) take their
+    // alternatives' alternatives instead, so that the automaton never nests unions. Their first
+    // characters were checked disjoint over the nested alternatives already.
+    void flatten_unions() {
+        for (size_t u = 0; u < nodes.size(); ++u) {
+            if (nodes[u].kind != N_UNION) continue;
+            std::vector<uint32_t> work(ids.begin() + nodes[u].first, ids.begin() + nodes[u].first + nodes[u].n), flat;
+            bool nested = false;
+            for (int guard = 0; !work.empty() && guard < 65536; ++guard) {
+                const uint32_t x = work.back();
+                work.pop_back();
+                if (x < nodes.size() && nodes[x].kind == N_UNION && x != u) {
+                    nested = true;
+                    for (uint32_t j = 0; j < nodes[x].n; ++j) work.push_back(ids[nodes[x].first + j]);
+                } else {
+                    flat.push_back(x);
+                }
+            }
+            if (!nested || flat.size() > 0xFFFFu) continue;
+            nodes[u].first = static_cast<uint32_t>(ids.size());
+            nodes[u].n = static_cast<uint16_t>(flat.size());
+            ids.insert(ids.end(), flat.begin(), flat.end());
+        }
+    }
+
+    // Every index the automaton follows lies inside its table (the device walks trust them).
+    bool tables_ok() const {
+        const size_t nn = nodes.size();
+        auto node_ok = [&](uint32_t x) { return x < nn; };
+        if (!node_ok(root) || !node_ok(any_object) || !node_ok(any_array) || !node_ok(any_string) ||
+            !node_ok(any_number) || !node_ok(any_literal))
+            return false;
+        for (const Dfa& d : dfas) {
+            if (d.n_states == 0) continue;  // the placeholder entry of a program without patterns
+            if (d.start >= d.n_states || static_cast<size_t>(d.next_off) + d.n_states * 128ull > next.size() ||
+                static_cast<size_t>(d.info_off) + d.n_states > info.size())
+                return false;
+            for (size_t i = 0; i < d.n_states * 128ull; ++i)
+                if (next[d.next_off + i] >= static_cast<int32_t>(d.n_states)) return false;
+        }
+        for (const Node& n : nodes) {
+            switch (n.kind) {
+                case N_ANY: break;
+                case N_OBJECT:
+                    if (static_cast<size_t>(n.first) + n.n > props.size() || (n.extra != kNone && !node_ok(n.extra)))
+                        return false;
+                    for (uint32_t i = 0; i < n.n; ++i) {
+                        const Prop& pr = props[n.first + i];
+                        if (!node_ok(pr.node) || static_cast<size_t>(pr.name_off) + pr.name_len > bytes.size()) return false;
+                    }
+                    break;
+                case N_ARRAY:
+                    if (static_cast<size_t>(n.first) + n.n > ids.size() || (n.extra != kNone && !node_ok(n.extra)))
+                        return false;
+                    for (uint32_t i = 0; i < n.n; ++i)
+                        if (!node_ok(ids[n.first + i])) return false;
+                    break;
+                case N_STRING:
+                    if (n.extra != kNone && (n.extra >= dfas.size() || dfas[n.extra].n_states == 0)) return false;
+                    break;
+                case N_INTEGER:
+                case N_NUMBER: break;
+                case N_ENUM:
+                    if (static_cast<size_t>(n.first) + n.n > lits.size() || n.n > 64) return false;
+                    for (uint32_t i = 0; i < n.n; ++i) {
+                        const Lit& l = lits[n.first + i];
+                        if (static_cast<size_t>(l.off) + l.len > bytes.size()) return false;
+                    }
+                    break;
+                case N_UNION:
+                    if (static_cast<size_t>(n.first) + n.n > ids.size()) return false;
+                    for (uint32_t i = 0; i < n.n; ++i)
+                        if (!node_ok(ids[n.first + i]) || nodes[ids[n.first + i]].kind == N_UNION) return false;
+                    break;
+                default: return false;
+            }
+        }
+        return true;
     }
     SVocab svocab() const { return SVocab{d_vbytes, d_voff, d_vflags, vocab}; }
 };
@@ -1521,6 +1613,11 @@ int32_t sixi_schema_compile(int32_t device, const char* schema_json, size_t sche
     if (g->dfas.empty()) g->dfas.push_back(Dfa{});
     if (g->next.empty()) g->next.push_back(-1);
     if (g->info.empty()) g->info.push_back(DfaInfo{});
+    g->flatten_unions();
+    if (!g->tables_ok()) {
+        set_err("JSON schema: internal error (inconsistent compiled program)");
+        return SIXI_BACKEND_ERROR;
+    }
     if (device >= 0) {  // device copies of the program and the vocabulary
         int n = 0;
         if (cudaGetDeviceCount(&n) != cudaSuccess || device >= n) {

@@ -62,6 +62,7 @@ struct Prog {  // device or host pointers
     const DfaInfo* info;
     uint32_t root;
     uint32_t any_object, any_array, any_string, any_number, any_literal;  // nodes of generic values
+    uint32_t n_nodes, n_dfas;  // table sizes the row-state check tests frames against
 };
 
 // frame kinds
@@ -92,10 +93,10 @@ static_assert(sizeof(Frame) == 24, "frame layout");
 struct State {                  // the row state of sixi_schema_state (800 bytes)
     uint32_t depth;             // frames in use
     uint32_t failed;
-    uint32_t pad[2];
+    uint32_t pad[6];
     Frame f[kMaxDepth];
 };
-static_assert(sizeof(State) <= 800, "state size");
+static_assert(sizeof(State) == 800, "state size: SIXI_SCHEMA_STATE_BYTES");
 
 __host__ __device__ inline bool is_ws(uint32_t c) { return c == ' ' || c == '\t' || c == '\n' || c == '\r'; }
 __host__ __device__ inline bool is_digit(uint32_t c) { return c >= '0' && c <= '9'; }
@@ -197,22 +198,33 @@ struct Machine {
     S& st;
     __host__ __device__ Machine(const Prog& p, S& s) : P(p), st(s) {}
 
+    // the generic node a value of any type that begins with c takes (for N_ANY), else nd
+    __host__ __device__ uint32_t concrete(uint32_t nd, uint32_t c) const {
+        if (P.nodes[nd].kind != N_ANY) return nd;
+        if (c == '{') return P.any_object;
+        if (c == '[') return P.any_array;
+        if (c == '"') return P.any_string;
+        if (c == '-' || is_digit(c)) return P.any_number;
+        return P.any_literal;
+    }
+
     // A value of node `nd` begins with byte c (not whitespace); the parent has already moved on
-    // to its after-value phase. Pushes the value's frame.
+    // to its after-value phase. Pushes the value's frame. Not recursive (device stacks are sized
+    // statically): a union's alternatives are never unions themselves (the compiler flattens
+    // them and checks it), and an N_ANY resolves to one generic node in one step.
     __host__ __device__ bool begin_value(uint32_t nd, uint32_t c) {
-        const Node& N = P.nodes[nd];
-        if (N.kind == N_UNION) {
-            for (uint32_t i = 0; i < N.n; ++i)  // alternatives begin with different characters
-                if (begin_value(P.ids[N.first + i], c)) return true;
+        const Node& U = P.nodes[nd];
+        if (U.kind == N_UNION) {
+            for (uint32_t i = 0; i < U.n; ++i)  // alternatives begin with different characters
+                if (begin_one(concrete(P.ids[U.first + i], c), c)) return true;
             return false;
         }
-        if (N.kind == N_ANY) {
-            if (c == '{') return begin_value(P.any_object, c);
-            if (c == '[') return begin_value(P.any_array, c);
-            if (c == '"') return begin_value(P.any_string, c);
-            if (c == '-' || is_digit(c)) return begin_value(P.any_number, c);
-            return begin_value(P.any_literal, c);
-        }
+        return begin_one(concrete(nd, c), c);
+    }
+
+    // begin_value for a node that is neither a union nor N_ANY
+    __host__ __device__ bool begin_one(uint32_t nd, uint32_t c) {
+        const Node& N = P.nodes[nd];
         Frame f{};
         f.node = nd;
         switch (N.kind) {
@@ -625,10 +637,34 @@ struct OverlayStack {
     }
 };
 
+// Whether a row state can be walked safely: its depth and every frame's node and kind lie in
+// range, and string frames under a pattern hold a state of their DFA. States made by
+// sixi_schema_reset / sixi_schema_advance always pass; the kernels treat any other as dead.
+__host__ __device__ inline bool state_ok(const Prog& P, const State& s) {
+    if (s.depth == 0u) return true;  // finished (or never started): nothing may follow
+    if (s.depth > static_cast<uint32_t>(kMaxDepth)) return false;
+    for (uint32_t i = 0; i < s.depth; ++i) {
+        const Frame& f = s.f[i];
+        if (f.node >= P.n_nodes || f.kind > F_LIT || (i == 0) != (f.kind == F_ROOT)) return false;
+        const Node& N = P.nodes[f.node];
+        if (f.kind == F_STR && N.kind == N_STRING && N.extra != kNone) {
+            if (N.extra >= P.n_dfas || ((f.b >> 8) & 0xFFFFu) >= P.dfas[N.extra].n_states) return false;
+        }
+        if ((f.kind == F_OBJ || f.kind == F_KEY) && N.kind != N_OBJECT) return false;
+        if (f.kind == F_KEY && (s.f[i - 1].kind != F_OBJ || s.f[i - 1].node != f.node)) return false;
+        if (f.kind == F_OBJ && f.a != 0xFFu && f.a >= N.n) return false;
+        if (f.kind == F_ARR && N.kind != N_ARRAY) return false;
+        if (f.kind == F_LIT && N.kind != N_ENUM) return false;
+        if (f.kind == F_NUM && N.kind != N_INTEGER && N.kind != N_NUMBER) return false;
+        if (f.kind == F_STR && N.kind != N_STRING) return false;
+    }
+    return true;
+}
+
 __host__ __device__ inline void start_state(State& s, uint32_t root) {
     s.depth = 1;
     s.failed = 0;
-    s.pad[0] = s.pad[1] = 0;
+    for (int i = 0; i < 6; ++i) s.pad[i] = 0;
     Frame r{};
     r.node = root;
     r.kind = F_ROOT;

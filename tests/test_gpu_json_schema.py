@@ -158,3 +158,21 @@ def test_constrained_decoding_produces_valid_documents(vocab):
                 assert g.check_text(text) != NOT_PREFIX
         assert ended.sum() >= rows // 2, (name, ended.sum())
         g.close()
+
+
+def test_malformed_states_are_frozen_not_walked(vocab):
+    toks, flags, eos, tk = vocab
+    g = SchemaGrammar(0, SCHEMAS["person"], toks, flags, eos)
+    st = g.new_states(4)
+    raw = st.cpu().numpy().copy()
+    words = raw.view(np.uint32)  # [4, 200]: depth, failed, pad[6], then 24-byte frames
+    words[1, 0] = 40             # deeper than SIXI_SCHEMA_MAX_DEPTH
+    words[2, 8] = 1_000_000      # the root frame's node past the program
+    words[3, 0] = 2              # a second frame of kind F_ROOT: only the bottom frame is a root
+    st.copy_(torch.from_numpy(raw))
+    masks = g.fill_masks(st).cpu().numpy()
+    assert masks[0].any() and not masks[1:].any()
+    tok = torch.tensor([tk.encode(b"{")[0]] * 4, dtype=torch.int32, device="cuda")
+    ast = g.advance(st, tok).cpu().numpy()
+    assert ast[0] == 0 and (ast[1:] != 0).all(), ast
+    g.close()

@@ -21,7 +21,7 @@ import random
 import pytest
 
 from oracle.schema_oracle import Validator
-from sixi_smp.json_schema import COMPLETE, NOT_PREFIX, SchemaError, SchemaGrammar
+from sixi_smp.json_schema import COMPLETE, NOT_PREFIX, PREFIX, SchemaError, SchemaGrammar
 
 PERSON = {
     "type": "object",
@@ -329,3 +329,20 @@ def test_annotations_have_no_effect():
     b = SchemaGrammar(-1, {"type": "integer"})
     for t in [b"1", b"-3", b"1.5", b'"x"', b"12"]:
         assert a.check_text(t) == b.check_text(t)
+
+
+def test_unions_reached_through_refs_stay_flat():
+    # a $ref to an anyOf, itself an alternative of an anyOf, and a recursive array of a union: the
+    # automaton walks them without nested unions (its device form is not recursive)
+    schema = {"$defs": {"opt": {"anyOf": [{"type": "string", "maxLength": 3}, {"type": "null"}]},
+                        "v": {"anyOf": [{"type": "integer", "minimum": 0}, {"type": "array", "items": {"$ref": "#/$defs/v"},
+                                                                             "maxItems": 2}]}},
+              "type": "object",
+              "properties": {"a": {"anyOf": [{"$ref": "#/$defs/opt"}, {"type": "boolean"}]}, "b": {"$ref": "#/$defs/v"}},
+              "additionalProperties": False}
+    g = SchemaGrammar(-1, schema)
+    v = Validator(schema)
+    for text in [b'{"a":"xy"}', b'{"a":null}', b'{"a":true}', b'{"a":"long"}', b'{"a":3}', b'{"b":[1,[2,[]]]}',
+                 b'{"b":[1,2,3]}', b'{"b":-1}', b'{"a":false,"b":7}', b'{"b":[[[[0]]]]}']:
+        assert (g.check_text(text) == COMPLETE) == v.accepts(text), text
+    assert g.check_text(b'{"a":n') == PREFIX and g.check_text(b'{"a":1') == NOT_PREFIX

@@ -178,8 +178,9 @@ __host__ __device__ inline bool int_viable(bool neg, uint64_t mag, bool more, in
         }
         if (vhi >= lo && vlo <= hi) return true;
         if (!more || mag == 0) return false;
+        if (a > cap / 10u) return false;  // one more digit passes every range (and must not wrap)
         a = a * 10u;
-        b = b * 10u + 9u;
+        b = b > cap / 10u ? cap + 1u : b * 10u + 9u;
     }
     return false;
 }

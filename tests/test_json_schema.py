@@ -346,3 +346,27 @@ def test_unions_reached_through_refs_stay_flat():
                  b'{"b":[1,2,3]}', b'{"b":-1}', b'{"a":false,"b":7}', b'{"b":[[[[0]]]]}']:
         assert (g.check_text(text) == COMPLETE) == v.accepts(text), text
     assert g.check_text(b'{"a":n') == PREFIX and g.check_text(b'{"a":1') == NOT_PREFIX
+
+
+def test_integers_near_the_64_bit_limits_end_cleanly():
+    # magnitudes whose next power of ten passes 2^64: a digit is allowed only while the value can
+    # still end inside the bounds, so no prefix is a dead end
+    for schema in [{"type": "integer"}, {"type": "integer", "minimum": -5, "maximum": 4_000_000_000_000_000_000},
+                   {"type": "array", "items": {"type": "integer"}}]:
+        g = SchemaGrammar(-1, schema)
+        v = Validator(schema)
+        pre = b"[" if schema.get("type") == "array" else b""
+        for digits in [b"409562218754484177", b"1152921504606846976", b"230584300921369395", b"9223372036854775807"]:
+            for sign in [b"", b"-"]:
+                text = pre + sign
+                for c in digits:
+                    nxt = text + bytes([c])
+                    if g.check_text(nxt) == NOT_PREFIX:
+                        break
+                    text = nxt
+                # what was accepted is no dead end: some byte follows, or the document is complete
+                assert g.check_text(text) == COMPLETE or any(
+                    g.check_text(text + bytes([b])) != NOT_PREFIX for b in range(256)), text
+                ends = [text + b"]"] if pre else [text]
+                for t in ends:
+                    assert (g.check_text(t) == COMPLETE) == v.accepts(t), t

@@ -232,3 +232,31 @@ def uniforms_for(params: np.ndarray, step: int = 0, slots: int = 1) -> np.ndarra
 __all__ = ["config1", "config2", "config3", "config4", "pack_mask", "unpack_mask", "run_mask",
            "mask_words", "f32_to_bf16_bits", "bf16_bits_to_f32", "softmax_rows", "uniforms_for",
            "PARAMS_DTYPE", "QWEN_VOCAB"]
+
+
+# A response_format json_schema of the kind an extraction request sends: nested objects, an array
+# of objects without an item bound (so that answers run long), integer bounds, enums, a pattern and
+# a format. Used by the json_schema bench line.
+RESPONSE_SCHEMA = {
+    "type": "object",
+    "properties": {
+        "order_id": {"type": "string", "pattern": "^[A-Z]{2}-[0-9]{6}$"},
+        "placed": {"type": "string", "format": "date"},
+        "status": {"enum": ["open", "shipped", "delivered", "cancelled"]},
+        "customer": {"type": "object",
+                     "properties": {"name": {"type": "string", "maxLength": 40},
+                                    "email": {"type": "string"},
+                                    "vip": {"type": "boolean"}},
+                     "required": ["name"], "additionalProperties": False},
+        "lines": {"type": "array",
+                  "items": {"type": "object",
+                            "properties": {"sku": {"type": "string"},
+                                           "qty": {"type": "integer", "minimum": 1, "maximum": 999},
+                                           "price": {"type": "number"},
+                                           "note": {"anyOf": [{"type": "string"}, {"type": "null"}]}},
+                            "required": ["sku", "qty"], "additionalProperties": False}},
+        "total": {"type": "number"},
+    },
+    "required": ["order_id", "status", "lines"],
+    "additionalProperties": False,
+}

@@ -11,9 +11,7 @@
  * the caller's CUDA stream (`stream` is a `cudaStream_t` passed as `void*`, NULL = legacy default
  * stream) and performs no host synchronisation. The handle owns device workspace only; it is not
  * thread-safe (one handle per host thread or external serialisation), matching the engine, where
- * device access is serialised by the batch leader (src/core/core_execution.cpp:1398-1530). Calls
- * on one handle share its workspace, so calls that could overlap in time (on different streams)
- * need ordering between them (one stream, or events).
+ * device access is serialised by the batch leader (src/core/core_execution.cpp:1398-1530).
  */
 #ifndef SIXI_SMP_H
 #define SIXI_SMP_H
@@ -109,20 +107,11 @@ SIXI_SMP_API const char* sixi_smp_status_string(int32_t status);
  *               hist_offsets[r+1]); hist_tokens may be NULL (no history)
  *   uniforms    [n_rows] in [0,1) or NULL (Philox slot 0); greedy rows consume none
  *   out_tokens  [n_rows] (-1 on error), out_status [n_rows]
- * Batches of at most 4 rows (see sixi_smp_set_split_rows) take a latency path for their greedy
- * rows and rows with 1 <= top_k <= 64: each row's vocabulary is split over 16 blocks and their
- * candidates merged, while the cluster path runs the batch's other rows on a second stream of
- * the handle (joined back into `stream` before the call's work ends; CUDA-graph capturable).
- * Tokens and statuses are the same either way.
  */
 SIXI_SMP_API int32_t sixi_smp_sample(sixi_smp* h, const sixi_smp_rows* rows, const sixi_smp_params* params,
                         const uint32_t* mask_words, const int32_t* hist_tokens,
                         const int64_t* hist_offsets, const double* uniforms, uint64_t step,
                         int32_t* out_tokens, int32_t* out_status, void* stream);
-
-/* The largest batch sixi_smp_sample sends to its small-batch latency path (default and maximum 4;
- * 0 turns it off). A tuning knob with no counterpart in the engine. */
-SIXI_SMP_API int32_t sixi_smp_set_split_rows(sixi_smp* h, uint32_t max_rows);
 
 /*
  * sixi_smp_sample over rows picked out of a batch (no counterpart in the engine): row j of `rows`

@@ -48,13 +48,6 @@ struct sixi_smp {
     HostSlot slot[2];
     uint32_t next_slot;
     cudaStream_t copy_stream;
-    // split path of sixi_smp_sample for batches of at most split_rows rows: stage-1 records of
-    // every (slice, row), and a second stream on which the cluster path takes the other rows
-    uint32_t split_rows;
-    sixi_b200::ShardCand* split_cand;   // [kSplitSlices][kSplitRows][kSplitTopN]
-    sixi_b200::ShardStats* split_stats; // [kSplitSlices][kSplitRows]
-    cudaStream_t side_stream;
-    cudaEvent_t ev_fork, ev_join;
 };
 
 namespace {
@@ -222,15 +215,6 @@ int32_t sixi_smp_create(int32_t device, uint32_t max_rows, uint32_t vocab, sixi_
     }
     if (e == cudaSuccess) e = sixi_b200::prepare_kernels(device);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking);
-    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->side_stream, cudaStreamNonBlocking);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->ev_fork, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->ev_join, cudaEventDisableTiming);
-    if (e == cudaSuccess)
-        e = cudaMalloc(&h->split_cand, sizeof(sixi_b200::ShardCand) * sixi_b200::kSplitSlices * sixi_b200::kSplitRows *
-                                           sixi_b200::kSplitTopN);
-    if (e == cudaSuccess)
-        e = cudaMalloc(&h->split_stats, sizeof(sixi_b200::ShardStats) * sixi_b200::kSplitSlices * sixi_b200::kSplitRows);
-    h->split_rows = sixi_b200::kSplitRows;
     for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
         e = cudaEventCreateWithFlags(&h->slot[i].copied, cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->slot[i].consumed, cudaEventDisableTiming);
@@ -261,14 +245,6 @@ int32_t sixi_smp_destroy(sixi_smp* h) {
         if (sl.consumed != nullptr) cudaEventDestroy(sl.consumed);
     }
     if (h->copy_stream != nullptr) cudaStreamDestroy(h->copy_stream);
-    if (h->side_stream != nullptr) {
-        cudaStreamSynchronize(h->side_stream);
-        cudaStreamDestroy(h->side_stream);
-    }
-    if (h->ev_fork != nullptr) cudaEventDestroy(h->ev_fork);
-    if (h->ev_join != nullptr) cudaEventDestroy(h->ev_join);
-    cudaFree(h->split_cand);
-    cudaFree(h->split_stats);
     cudaFree(h->ws);
     cudaFree(h->qstat);
     cudaFree(h->d_default);
@@ -315,62 +291,8 @@ int32_t sixi_smp_sample(sixi_smp* h, const sixi_smp_rows* rows, const sixi_smp_p
     a.step = step;
     a.out_tok = out_tokens;
     a.out_status = out_status;
-    const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (rows->n_rows > h->split_rows) return from_cuda(sixi_b200::launch_rows(sixi_b200::kModeSample, a, plan, st));
-    // Split path: the rows it certifies run as kSplitSlices blocks each (stage 1 of the sharded
-    // mode over the row's slices) and the merge, on the caller's stream; the cluster path takes
-    // the other rows on the side stream at the same time (its clusters of split rows leave at once).
-    const uint32_t V = h->vocab;
-    const uint32_t width = ((V + sixi_b200::kSplitSlices - 1) / sixi_b200::kSplitSlices + 31u) / 32u * 32u;
-    const uint32_t n_slices = (V + width - 1) / width;
-    sixi_b200::ShardArgs sa{};
-    sa.data = rows->data;
-    sa.row_stride = rows->row_stride;
-    sa.dtype = rows->dtype;
-    sa.shard_vocab = width;
-    sa.vocab_offset = 0;
-    sa.full_vocab = V;
-    sa.mask_words = h->mask_words;
-    sa.n_rows = rows->n_rows;
-    sa.top_n = sixi_b200::kSplitTopN;
-    sa.params = params;
-    sa.mask = mask_words;
-    sa.hist = hist_tokens;
-    sa.hist_off = hist_tokens ? hist_offsets : nullptr;
-    sa.out_cand = h->split_cand;
-    sa.out_stats = h->split_stats;
-    sa.slice_width = width;
-    sa.split_only = 1;
-    sixi_b200::MergeArgs ma{};
-    ma.n_rows = rows->n_rows;
-    ma.n_shards = n_slices;
-    ma.top_n = sixi_b200::kSplitTopN;
-    ma.cand = h->split_cand;
-    ma.stats = h->split_stats;
-    ma.params = params;
-    ma.uniforms = uniforms;
-    ma.step = step;
-    ma.out_tok = out_tokens;
-    ma.out_status = out_status;
-    ma.split_only = 1;
-    ma.hist_off = hist_tokens ? hist_offsets : nullptr;
-    a.skip_split = 1;
-    cudaError_t e = cudaEventRecord(h->ev_fork, st);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(h->side_stream, h->ev_fork, 0);
-    if (e == cudaSuccess) e = sixi_b200::launch_rows(sixi_b200::kModeSample, a, plan, h->side_stream);
-    if (e == cudaSuccess) e = sixi_b200::launch_shard_candidates(sa, st);
-    if (e == cudaSuccess) e = sixi_b200::launch_merge_shards(ma, st);
-    // the join is recorded whatever happened above, so that the side stream never runs ahead of
-    // a later call on the caller's stream
-    const cudaError_t ej = cudaEventRecord(h->ev_join, h->side_stream);
-    const cudaError_t ew = ej == cudaSuccess ? cudaStreamWaitEvent(st, h->ev_join, 0) : ej;
-    return from_cuda(e != cudaSuccess ? e : ew);
-}
-
-int32_t sixi_smp_set_split_rows(sixi_smp* h, uint32_t max_rows) {
-    if (h == nullptr || max_rows > sixi_b200::kSplitRows) return SIXI_INVALID_ARGUMENT;
-    h->split_rows = max_rows;
-    return SIXI_OK;
+    return from_cuda(sixi_b200::launch_rows(sixi_b200::kModeSample, a, plan,
+                                            static_cast<cudaStream_t>(stream)));
 }
 
 int32_t sixi_smp_sample_indexed(sixi_smp* h, const sixi_smp_rows* rows, const uint32_t* row_map,

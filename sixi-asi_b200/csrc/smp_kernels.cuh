@@ -73,8 +73,6 @@ struct RowArgs {
     int32_t* out_ids;
     double* out_probs;
     int32_t* out_count;
-    // sample mode: rows that are split_eligible (kSplitTopN) are left to the split path
-    uint32_t skip_split;
 };
 
 // Launch configuration chosen by the host for a vocabulary size.
@@ -129,21 +127,6 @@ constexpr uint32_t kMaxShards = 16;
 constexpr uint32_t kMaxShardTopN = 64;
 constexpr size_t kMaxShardSmem = 227 * 1024;
 
-// The split path of sixi_smp_sample for small batches (at most kSplitRows rows): each row's
-// vocabulary in kSplitSlices slices (stage 1 of the vocab-sharded mode on one device, one block per
-// slice), then the merge. It takes the rows the merge certifies whatever the data: greedy rows and
-// rows with 1 <= top_k <= kSplitTopN (every one of the row's top-k is among the best top_k of its
-// slice, so all of them are listed and at or above every truncated slice's worst listed entry),
-// except rows whose per-occurrence history counts could pass stage 1's 16-bit counters. The other
-// rows of the batch run on the cluster path, concurrently.
-constexpr uint32_t kSplitRows = 4;
-constexpr uint32_t kSplitSlices = 16;
-constexpr uint32_t kSplitTopN = 64;
-__host__ __device__ inline bool split_eligible(const sixi_smp_params& p, int64_t hist_len, uint32_t top_n) {
-    if (p.frequency_penalty != 0.0f && hist_len > 65535) return false;
-    return p.temperature <= 0.0f || (p.top_k >= 1 && static_cast<uint32_t>(p.top_k) <= top_n);
-}
-
 struct ShardArgs {
     const void* data;
     uint64_t row_stride;  // elements
@@ -160,11 +143,6 @@ struct ShardArgs {
     const int64_t* hist_off;
     ShardCand* out_cand;
     ShardStats* out_stats;
-    // split path: slice s = blockIdx.y covers ids [s * slice_width, ...) of full rows at `data`
-    // (0: one slice, the shard [vocab_offset, vocab_offset + shard_vocab) at `data`); outputs at
-    // [s][row]. split_only: rows that are not split_eligible are skipped.
-    uint32_t slice_width;
-    uint32_t split_only;
 };
 struct MergeArgs {
     uint32_t n_rows, n_shards, top_n;
@@ -175,8 +153,6 @@ struct MergeArgs {
     uint64_t step;
     int32_t* out_tok;
     int32_t* out_status;
-    uint32_t split_only;        // rows that are not split_eligible are left alone
-    const int64_t* hist_off;    // the rows' history offsets (split_only; nullable)
 };
 size_t shard_smem_bytes(uint32_t shard_vocab);
 

@@ -893,11 +893,6 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const Layout lay = make_layout(a.chunk, C);
-    if (MODE == kModeSample && a.skip_split) {  // the split path's row: every CTA of the cluster leaves
-        const uint32_t orow = a.row_map != nullptr ? a.row_map[row] : row;
-        const int64_t hl = a.hist != nullptr ? a.hist_off[orow + 1] - a.hist_off[orow] : 0;
-        if (split_eligible(a.params[orow], hl, kSplitTopN)) return;
-    }
 
     ClusterShared* cs = reinterpret_cast<ClusterShared*>(smem);
     LocalShared* ls = reinterpret_cast<LocalShared*>(smem + lay.off_ls);

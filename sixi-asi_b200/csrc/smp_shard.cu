@@ -93,8 +93,8 @@ __device__ __forceinline__ double blk_sumd(double v, ShardShared* sh) {
 }
 
 // ------------------------------------------------------------------------------------------ stage 1
-// One block per row (and per slice of it on the split path). Shared memory: per-id history counts
-// of the slice (16 bits each), the collected candidates and the per-thread maxima.
+// One block per row. Shared memory: per-id history counts of the slice (16 bits each), the
+// collected candidates and the per-thread maxima.
 __global__ void __launch_bounds__(kSh, 1) shard_kernel(const ShardArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     ShardShared* sh = reinterpret_cast<ShardShared*>(smem);
@@ -104,24 +104,17 @@ __global__ void __launch_bounds__(kSh, 1) shard_kernel(const ShardArgs a) {
     unsigned long long* tmax = list + kCollectCap;
     const int tid = threadIdx.x;
     const uint32_t row = blockIdx.x;
-    const uint32_t slice = blockIdx.y;
     const sixi_smp_params P = a.params[row];
+    const uint8_t* rowp = static_cast<const uint8_t*>(a.data) +
+                          static_cast<size_t>(row) * a.row_stride * (a.dtype == SIXI_SMP_BF16 ? 2 : 4);
+    const uint32_t* mask = (a.mask != nullptr && (P.flags & SIXI_SMP_ROW_MASKED))
+                               ? a.mask + static_cast<size_t>(row) * a.mask_words
+                               : nullptr;
     int64_t h0 = 0, h1 = 0;
     if (a.hist != nullptr) {
         h0 = a.hist_off[row];
         h1 = a.hist_off[row + 1];
     }
-    if (a.split_only && !split_eligible(P, h1 - h0, a.top_n)) return;  // the cluster path's row
-    // this block's ids: [voff, voff + sv) of the row, element e at rowp[e]
-    const uint32_t voff = a.vocab_offset + slice * a.slice_width;
-    const uint32_t sv = a.slice_width ? (a.full_vocab - voff < a.slice_width ? a.full_vocab - voff : a.slice_width)
-                                      : a.shard_vocab;
-    const size_t esz = a.dtype == SIXI_SMP_BF16 ? 2 : 4;
-    const uint8_t* rowp = static_cast<const uint8_t*>(a.data) +
-                          (static_cast<size_t>(row) * a.row_stride + static_cast<size_t>(slice) * a.slice_width) * esz;
-    const uint32_t* mask = (a.mask != nullptr && (P.flags & SIXI_SMP_ROW_MASKED))
-                               ? a.mask + static_cast<size_t>(row) * a.mask_words
-                               : nullptr;
     const bool pen = P.mode != SIXI_SMP_STRICT_REPLAY && h1 > h0 &&
                      (P.repetition_penalty != 1.0f || P.presence_penalty != 0.0f || P.frequency_penalty != 0.0f);
     if (tid == 0) {
@@ -144,11 +137,11 @@ __global__ void __launch_bounds__(kSh, 1) shard_kernel(const ShardArgs a) {
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u) {
                 const int32_t t = t8[u];
-                if (t < static_cast<int32_t>(voff) ||
-                    t >= static_cast<int32_t>(voff + sv) ||
+                if (t < static_cast<int32_t>(a.vocab_offset) ||
+                    t >= static_cast<int32_t>(a.vocab_offset + a.shard_vocab) ||
                     !bit_allowed(mask, static_cast<uint32_t>(t)))
                     continue;
-                const uint32_t e = static_cast<uint32_t>(t) - voff;
+                const uint32_t e = static_cast<uint32_t>(t) - a.vocab_offset;
                 atomicAdd(&cnt[e >> 1], 1u << (16u * (e & 1u)));
             }
         }
@@ -163,18 +156,18 @@ __global__ void __launch_bounds__(kSh, 1) shard_kernel(const ShardArgs a) {
     uint32_t n_al = 0u;
     unsigned long long best = 0ull;
     bool bad = false;
-    for (uint32_t e0 = tid; e0 < sv; e0 += kUnroll * kSh) {  // kUnroll loads in flight
+    for (uint32_t e0 = tid; e0 < a.shard_vocab; e0 += kUnroll * kSh) {  // kUnroll loads in flight
         float x8[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             const uint32_t e = e0 + u * kSh;
-            x8[u] = e < sv ? shard_logit(a, rowp, e) : 0.0f;
+            x8[u] = e < a.shard_vocab ? shard_logit(a, rowp, e) : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             const uint32_t e = e0 + u * kSh;
-            const uint32_t gid = voff + e;
-            if (e >= sv || !bit_allowed(mask, gid)) continue;
+            const uint32_t gid = a.vocab_offset + e;
+            if (e >= a.shard_vocab || !bit_allowed(mask, gid)) continue;
             const float raw = x8[u];
             bad |= !isfinite(raw);
             ++n_al;
@@ -190,53 +183,20 @@ __global__ void __launch_bounds__(kSh, 1) shard_kernel(const ShardArgs a) {
     if (sh->flags & 1u) status = SIXI_NUMERIC_NAN_OR_INF;
     else if (sh->flags & 2u) status = SIXI_OUT_OF_BOUNDS;
     const uint32_t top_n = a.top_n;
-    const size_t orec = static_cast<size_t>(slice) * a.n_rows + row;  // output record [slice][row]
-    ShardCand* outc = a.out_cand + orec * top_n;
+    ShardCand* outc = a.out_cand + static_cast<size_t>(row) * top_n;
     if (status != SIXI_OK || n_allowed == 0u) {
         for (uint32_t i = tid; i < top_n; i += kSh) outc[i] = ShardCand{-INFINITY, -1};
-        if (tid == 0) a.out_stats[orec] = ShardStats{-INFINITY, static_cast<int32_t>(n_allowed), 0.0, status, 0};
+        if (tid == 0) a.out_stats[row] = ShardStats{-INFINITY, static_cast<int32_t>(n_allowed), 0.0, status, 0};
         return;
     }
-    // threshold: the top_n-th largest per-thread maximum bounds the shard's top_n from below. Each
-    // warp sorts its 32 maxima (descending, bitonic over shuffles) into tmax[warp][lane]; a value's
-    // rank is its lane plus, in every other warp's sorted run, the count of larger values (a binary
-    // search). The maxima are distinct composites (key, id) or 0 (no entry), so ranks are exact.
+    // threshold: the top_n-th largest per-thread maximum bounds the shard's top_n from below
     unsigned long long theta = 1ull;
     {
         uint32_t nz = blk_sum32(best != 0ull ? 1u : 0u, sh);
         if (nz >= top_n) {
-            const int lane = tid & 31, w = tid >> 5;
-            unsigned long long v = best;
-#pragma unroll
-            for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-                for (int j = k >> 1; j > 0; j >>= 1) {
-                    const unsigned long long o = __shfl_xor_sync(0xFFFFFFFFu, v, j);
-                    // descending runs: the lower lane of a pair keeps the larger value when the
-                    // pair sits in a descending block of size k
-                    const bool desc = ((lane & k) == 0);
-                    const bool lower = ((lane & j) == 0);
-                    v = (lower == desc) ? (v > o ? v : o) : (v < o ? v : o);
-                }
-            }
-            __syncthreads();  // tmax is read below by every thread
-            tmax[tid] = v;
-            __syncthreads();
-            if (v != 0ull && static_cast<uint32_t>(lane) < top_n) {
-                uint32_t r = static_cast<uint32_t>(lane);
-                for (int o = 0; o < kShW && r < top_n; ++o) {
-                    if (o == w) continue;
-                    const unsigned long long* run = tmax + o * 32;
-                    int lo = 0, hi = 32;  // count of entries > v in a descending run
-                    while (lo < hi) {
-                        const int m = (lo + hi) >> 1;
-                        if (run[m] > v) lo = m + 1;
-                        else hi = m;
-                    }
-                    r += static_cast<uint32_t>(lo);
-                }
-                if (r == top_n - 1u) sh->bc[0] = v;
-            }
+            uint32_t r = 0u;
+            for (int j = 0; j < kSh; ++j) r += tmax[j] > best ? 1u : 0u;
+            if (best != 0ull && r == top_n - 1u) sh->bc[0] = best;
             __syncthreads();
             theta = sh->bc[0];
         }
@@ -247,18 +207,18 @@ __global__ void __launch_bounds__(kSh, 1) shard_kernel(const ShardArgs a) {
     WeightCtx wc{};
     if (sampled) make_weight_ctx(P.temperature, xmax, 46.0f, wc);
     double se = 0.0;
-    for (uint32_t e0 = tid; e0 < sv; e0 += kUnroll * kSh) {  // kUnroll loads in flight
+    for (uint32_t e0 = tid; e0 < a.shard_vocab; e0 += kUnroll * kSh) {  // kUnroll loads in flight
         float x8[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             const uint32_t e = e0 + u * kSh;
-            x8[u] = e < sv ? shard_logit(a, rowp, e) : 0.0f;
+            x8[u] = e < a.shard_vocab ? shard_logit(a, rowp, e) : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             const uint32_t e = e0 + u * kSh;
-            const uint32_t gid = voff + e;
-            if (e >= sv || !bit_allowed(mask, gid)) continue;
+            const uint32_t gid = a.vocab_offset + e;
+            if (e >= a.shard_vocab || !bit_allowed(mask, gid)) continue;
             const float x = adjusted(e, x8[u]);
             const unsigned long long c = comp_of(fkey(x), gid);
             if (c >= theta) {
@@ -280,8 +240,8 @@ __global__ void __launch_bounds__(kSh, 1) shard_kernel(const ShardArgs a) {
             __syncthreads();
             for (int i = tid; i < 256; i += kSh) dh[i] = 0u;
             __syncthreads();
-            for (uint32_t e = tid; e < sv; e += kSh) {
-                const uint32_t gid = voff + e;
+            for (uint32_t e = tid; e < a.shard_vocab; e += kSh) {
+                const uint32_t gid = a.vocab_offset + e;
                 if (!bit_allowed(mask, gid)) continue;
                 const unsigned long long c = comp_of(fkey(adjusted(e, shard_logit(a, rowp, e))), gid);
                 if ((c & pmask) == prefix) atomicAdd(&dh[(c >> shift) & 255u], 1u);
@@ -306,8 +266,8 @@ __global__ void __launch_bounds__(kSh, 1) shard_kernel(const ShardArgs a) {
         __syncthreads();
         if (tid == 0) sh->fill = 0u;
         __syncthreads();
-        for (uint32_t e = tid; e < sv; e += kSh) {
-            const uint32_t gid = voff + e;
+        for (uint32_t e = tid; e < a.shard_vocab; e += kSh) {
+            const uint32_t gid = a.vocab_offset + e;
             if (!bit_allowed(mask, gid)) continue;
             const unsigned long long c = comp_of(fkey(adjusted(e, shard_logit(a, rowp, e))), gid);
             if (c >= theta) list[atomicAdd(&sh->fill, 1u)] = c;  // exactly top_n entries
@@ -323,7 +283,7 @@ __global__ void __launch_bounds__(kSh, 1) shard_kernel(const ShardArgs a) {
         if (r < top_n) outc[r] = ShardCand{kval(comp_key(c)), static_cast<int32_t>(comp_id(c))};
     }
     for (uint32_t i = n_col + tid; i < top_n; i += kSh) outc[i] = ShardCand{-INFINITY, -1};
-    if (tid == 0) a.out_stats[orec] = ShardStats{xmax, static_cast<int32_t>(n_allowed), sum_exp, SIXI_OK, 0};
+    if (tid == 0) a.out_stats[row] = ShardStats{xmax, static_cast<int32_t>(n_allowed), sum_exp, SIXI_OK, 0};
 }
 
 // ------------------------------------------------------------------------------------------ stage 2
@@ -378,10 +338,6 @@ __global__ void __launch_bounds__(kSh, 1) merge_kernel(const MergeArgs a) {
     __shared__ unsigned long long M[kMaxMerge];   // merged, descending
     const int tid = threadIdx.x;
     const uint32_t row = blockIdx.x;
-    if (a.split_only) {  // the cluster path's row
-        const int64_t hl = a.hist_off != nullptr ? a.hist_off[row + 1] - a.hist_off[row] : 0;
-        if (!split_eligible(a.params[row], hl, a.top_n)) return;
-    }
     const uint32_t S = a.n_shards, n = a.top_n, tot = S * n;
     if (tid < static_cast<int>(S)) st[tid] = a.stats[static_cast<size_t>(tid) * a.n_rows + row];
     for (uint32_t i = tid; i < tot; i += kSh) {
@@ -542,9 +498,7 @@ cudaError_t launch_shard_candidates(const ShardArgs& a, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         ready.fetch_or(bit, std::memory_order_acq_rel);
     }
-    const uint32_t n_slices = a.slice_width ? (a.full_vocab - a.vocab_offset + a.slice_width - 1) / a.slice_width : 1u;
-    if (n_slices > 65535u) return cudaErrorInvalidValue;
-    shard_kernel<<<dim3(a.n_rows, n_slices), kSh, smem, stream>>>(a);
+    shard_kernel<<<a.n_rows, kSh, smem, stream>>>(a);
     return cudaGetLastError();
 }
 

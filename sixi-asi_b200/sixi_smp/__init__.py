@@ -99,7 +99,6 @@ SIGNATURES = {
     "sixi_smp_sample_host": (_I32, [_P, _P, _U32, _U32, _U64, _P, _P, _P, _P, _P, _U64, _P, _P, _P]),
     "sixi_smp_sample_host_async": (_I32, [_P, _P, _U32, _U32, _U64, _P, _P, _P, _P, _P, _U64, _P, _P, _P]),
     "sixi_smp_sample_indexed": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _U64, _P, _P, _P]),
-    "sixi_smp_set_split_rows": (_I32, [_P, _U32]),
     "sixi_smp_gather_rows": (_I32, [_P, _P, _P, _U32, _U32, _P, _U64, _P]),
     "sixi_smp_greedy_argmax": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _P]),
     "sixi_smp_candidates": (_I32, [_P, ctypes.POINTER(Rows), _P, _P, _P, _P, _U32, _P, _P, _P, _P, _P]),
@@ -212,10 +211,6 @@ class Sampler:
         if self.h:
             _lib().sixi_smp_destroy(self.h)
             self.h = None
-
-    def set_split_rows(self, max_rows: int) -> None:
-        """The largest batch `sample` sends to its small-batch latency path (0 turns it off)."""
-        _check("sixi_smp_set_split_rows", _lib().sixi_smp_set_split_rows(self.h, max_rows))
 
     def __del__(self):
         try:

@@ -1528,8 +1528,11 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             fl_n = 0;
         }
         // merge: rank of every pushed entry = its position + entries greater in the other lists
+        // entries list-minor (x -> list x % C, position x / C): for k <= kNT / C every thread
+        // merges at most one entry, instead of one entry of every list in turn
         for (uint32_t x = tid; fl_n > 0 && x < C * kKS; x += kNT) {
-            const uint32_t q = x / kKS, pidx = x % kKS;
+            const uint32_t q = x % C, pidx = x / C;
+            if (pidx >= fl_n) break;  // its rank is at least pidx: never among the first fl_n
             if (pidx >= cs->lcnt[q]) continue;
             const unsigned long long v = MA[q * kKS + pidx];
             uint32_t rank = pidx;

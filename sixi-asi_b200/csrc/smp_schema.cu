@@ -1300,9 +1300,27 @@ constexpr uint32_t kTokSpecial = 1u, kTokEos = 2u;
 struct SVocab {
     const uint8_t* bytes;
     const uint64_t* off;
-    const uint8_t* flags;  // kTokSpecial / kTokEos
+    const uint8_t* flags;   // kTokSpecial / kTokEos
+    const uint8_t* first;   // first byte of each token (0 for an empty one)
+    const uint16_t* plain;  // code points of a token that is a plain string body, else kNotPlain
     uint32_t vocab;
 };
+constexpr uint16_t kNotPlain = 0xFFFFu;
+
+// Code points of a token that a string in its plain state (no escape or UTF-8 sequence open)
+// takes whole and stays plain after: no quote, backslash or control byte, complete UTF-8 sequences.
+// kNotPlain otherwise (the token needs the full walk).
+uint16_t plain_code_points(const uint8_t* b, size_t n) {
+    if (n == 0) return kNotPlain;
+    uint32_t esc = 0, utf = 0, cp = 0;
+    for (size_t i = 0; i < n; ++i) {
+        if (b[i] == '\\') return kNotPlain;
+        bool starts = false;
+        if (str_byte(b[i], esc, utf, starts) != 1) return kNotPlain;
+        cp += starts ? 1u : 0u;
+    }
+    return (esc == 0u && (utf & 3u) == 0u && cp < kNotPlain) ? static_cast<uint16_t>(cp) : kNotPlain;
+}
 
 __global__ void schema_reset_kernel(State* s, uint32_t n, uint32_t root) {
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
@@ -1313,17 +1331,43 @@ __global__ void schema_reset_kernel(State* s, uint32_t n, uint32_t root) {
 // walked on an overlay of the stack, 32 verdicts per warp ballot written as a mask word.
 __global__ void __launch_bounds__(kMaskThreads) schema_mask_kernel(const Prog P, const SVocab V, const State* states,
                                                                    uint32_t* masks, uint64_t stride) {
+    static_assert(kMaskThreads >= 256, "one thread per first byte");
     __shared__ State st;
-    __shared__ uint32_t st_ok;
+    __shared__ uint32_t st_ok, eos_ok;
+    __shared__ int32_t str_room;   // a plain-string top frame: code points it may still take, else -1
+    __shared__ uint32_t first_ok[8];  // bytes the state takes as a token's first byte
     const uint32_t row = blockIdx.y;
     const uint32_t* src = reinterpret_cast<const uint32_t*>(&states[row]);
     for (uint32_t i = threadIdx.x; i < sizeof(State) / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(&st)[i] = src[i];
+    if (threadIdx.x < 8) first_ok[threadIdx.x] = 0u;
     __syncthreads();
     if (threadIdx.x == 0) st_ok = state_ok(P, st) ? 1u : 0u;
     __syncthreads();
     const uint32_t words = (V.vocab + 31u) / 32u;
     uint32_t* out = masks + static_cast<uint64_t>(row) * stride;
     const bool dead = st.failed != 0u || st.depth == 0u || st_ok == 0u;  // no token for a malformed state
+    if (!dead) {
+        // The first-byte table (one step of the automaton per byte) rejects most tokens of a state
+        // without a walk; it is exact for the first byte, so a token it passes is walked in full.
+        if (threadIdx.x < 256) {
+            OverlayStack<SIXI_SCHEMA_MASK_OPENS> ov(st);
+            Machine<OverlayStack<SIXI_SCHEMA_MASK_OPENS>> m(P, ov);
+            if (m.step(threadIdx.x)) atomicOr(&first_ok[threadIdx.x >> 5], 1u << (threadIdx.x & 31u));
+        }
+        if (threadIdx.x == 0) {
+            OverlayStack<SIXI_SCHEMA_MASK_OPENS> ov(st);
+            Machine<OverlayStack<SIXI_SCHEMA_MASK_OPENS>> m(P, ov);
+            eos_ok = m.complete() ? 1u : 0u;
+            // A string in its plain state without a pattern: a plain token of n code points is
+            // allowed exactly when the length bound admits n more (str_byte accepts every byte).
+            const Frame& t = st.f[st.depth - 1];
+            const Node& N = P.nodes[t.node];
+            const bool plain = t.kind == F_STR && N.extra == kNone && t.pos == 0u && (t.b & 0x1Fu) == 0u;
+            const int64_t room = N.hi - static_cast<int64_t>(t.a);
+            str_room = plain ? static_cast<int32_t>(room < 0 ? 0 : (room > 0x7FFFFFFF ? 0x7FFFFFFF : room)) : -1;
+        }
+    }
+    __syncthreads();
     const uint32_t lane = threadIdx.x & 31u;
     for (uint32_t w = blockIdx.x * (kMaskThreads / 32) + threadIdx.x / 32; w < words;
          w += gridDim.x * (kMaskThreads / 32)) {
@@ -1332,15 +1376,19 @@ __global__ void __launch_bounds__(kMaskThreads) schema_mask_kernel(const Prog P,
         if (!dead && id < V.vocab) {
             const uint8_t fl = V.flags[id];
             if (fl & kTokEos) {
-                OverlayStack<SIXI_SCHEMA_MASK_OPENS> ov(st);
-                Machine<OverlayStack<SIXI_SCHEMA_MASK_OPENS>> m(P, ov);
-                ok = m.complete();
+                ok = eos_ok != 0u;
             } else if (!(fl & kTokSpecial)) {
-                const uint64_t b0 = V.off[id], b1 = V.off[id + 1];
-                if (b1 > b0) {
+                const uint32_t c0 = V.first[id];
+                const uint16_t pc = V.plain[id];
+                if (!((first_ok[c0 >> 5] >> (c0 & 31u)) & 1u)) {
+                    ok = false;  // also every empty token (byte 0 is never a first byte)
+                } else if (str_room >= 0 && pc != kNotPlain) {
+                    ok = static_cast<int32_t>(pc) <= str_room;
+                } else {
+                    const uint64_t b0 = V.off[id], b1 = V.off[id + 1];
                     OverlayStack<SIXI_SCHEMA_MASK_OPENS> ov(st);
                     Machine<OverlayStack<SIXI_SCHEMA_MASK_OPENS>> m(P, ov);
-                    ok = true;
+                    ok = b1 > b0;
                     for (uint64_t j = b0; j < b1 && ok; ++j) ok = m.step(V.bytes[j]);
                 }
             }
@@ -1423,6 +1471,8 @@ struct sixi_schema {
     uint8_t* d_vbytes = nullptr;
     uint64_t* d_voff = nullptr;
     uint8_t* d_vflags = nullptr;
+    uint8_t* d_vfirst = nullptr;
+    uint16_t* d_vplain = nullptr;
 
     Prog host_prog() const {
         Prog p{};
@@ -1524,7 +1574,7 @@ struct sixi_schema {
         }
         return true;
     }
-    SVocab svocab() const { return SVocab{d_vbytes, d_voff, d_vflags, vocab}; }
+    SVocab svocab() const { return SVocab{d_vbytes, d_voff, d_vflags, d_vfirst, d_vplain, vocab}; }
 };
 
 namespace {
@@ -1659,6 +1709,20 @@ int32_t sixi_schema_compile(int32_t device, const char* schema_json, size_t sche
         if (e == cudaSuccess && nb) e = cudaMemcpy(g->d_vbytes, host_bytes, nb, cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMemcpy(g->d_voff, host_offsets, (static_cast<size_t>(vocab) + 1) * 8, cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMemcpy(g->d_vflags, fl.data(), vocab, cudaMemcpyHostToDevice);
+        // per token: its first byte and, for plain string bodies, its code points (mask filters)
+        std::vector<uint8_t> first(vocab + 1, 0);
+        std::vector<uint16_t> plain(vocab + 1, kNotPlain);
+        for (uint32_t i = 0; i < vocab; ++i) {
+            const uint64_t b0 = host_offsets[i], b1 = host_offsets[i + 1];
+            if (b1 > b0) {
+                first[i] = host_bytes[b0];
+                plain[i] = plain_code_points(host_bytes + b0, static_cast<size_t>(b1 - b0));
+            }
+        }
+        if (e == cudaSuccess) e = cudaMalloc(&g->d_vfirst, vocab + 16);
+        if (e == cudaSuccess) e = cudaMalloc(&g->d_vplain, 2ull * vocab + 16);
+        if (e == cudaSuccess) e = cudaMemcpy(g->d_vfirst, first.data(), vocab, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(g->d_vplain, plain.data(), 2ull * vocab, cudaMemcpyHostToDevice);
         if (e != cudaSuccess) {
             sixi_schema_destroy(g.release());
             set_err("device allocation failed");
@@ -1678,6 +1742,8 @@ void sixi_schema_destroy(sixi_schema* g) {
         cudaFree(g->d_vbytes);
         cudaFree(g->d_voff);
         cudaFree(g->d_vflags);
+        cudaFree(g->d_vfirst);
+        cudaFree(g->d_vplain);
     }
     delete g;
 }

@@ -1302,6 +1302,7 @@ struct SVocab {
     const uint64_t* off;
     const uint8_t* flags;   // kTokSpecial / kTokEos
     const uint8_t* first;   // first byte of each token (0 for an empty one)
+    const uint8_t* second;  // second byte of each token (0 for a shorter one)
     const uint16_t* plain;  // code points of a token that is a plain string body, else kNotPlain
     uint32_t vocab;
 };
@@ -1336,10 +1337,12 @@ __global__ void __launch_bounds__(kMaskThreads) schema_mask_kernel(const Prog P,
     __shared__ uint32_t st_ok, eos_ok;
     __shared__ int32_t str_room;   // a plain-string top frame: code points it may still take, else -1
     __shared__ uint32_t first_ok[8];  // bytes the state takes as a token's first byte
+    __shared__ uint32_t after_sp[8];  // bytes it takes after a space (most tokens start with one)
     const uint32_t row = blockIdx.y;
     const uint32_t* src = reinterpret_cast<const uint32_t*>(&states[row]);
     for (uint32_t i = threadIdx.x; i < sizeof(State) / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(&st)[i] = src[i];
     if (threadIdx.x < 8) first_ok[threadIdx.x] = 0u;
+    if (threadIdx.x >= 8 && threadIdx.x < 16) after_sp[threadIdx.x - 8] = 0u;
     __syncthreads();
     if (threadIdx.x == 0) st_ok = state_ok(P, st) ? 1u : 0u;
     __syncthreads();
@@ -1353,6 +1356,9 @@ __global__ void __launch_bounds__(kMaskThreads) schema_mask_kernel(const Prog P,
             OverlayStack<SIXI_SCHEMA_MASK_OPENS> ov(st);
             Machine<OverlayStack<SIXI_SCHEMA_MASK_OPENS>> m(P, ov);
             if (m.step(threadIdx.x)) atomicOr(&first_ok[threadIdx.x >> 5], 1u << (threadIdx.x & 31u));
+            OverlayStack<SIXI_SCHEMA_MASK_OPENS> ov2(st);
+            Machine<OverlayStack<SIXI_SCHEMA_MASK_OPENS>> m2(P, ov2);
+            if (m2.step(' ') && m2.step(threadIdx.x)) atomicOr(&after_sp[threadIdx.x >> 5], 1u << (threadIdx.x & 31u));
         }
         if (threadIdx.x == 0) {
             OverlayStack<SIXI_SCHEMA_MASK_OPENS> ov(st);
@@ -1380,8 +1386,12 @@ __global__ void __launch_bounds__(kMaskThreads) schema_mask_kernel(const Prog P,
             } else if (!(fl & kTokSpecial)) {
                 const uint32_t c0 = V.first[id];
                 const uint16_t pc = V.plain[id];
+                const uint32_t c1 = V.second[id];
                 if (!((first_ok[c0 >> 5] >> (c0 & 31u)) & 1u)) {
                     ok = false;  // also every empty token (byte 0 is never a first byte)
+                } else if (c0 == ' ' && c1 != 0u && !((after_sp[c1 >> 5] >> (c1 & 31u)) & 1u)) {
+                    ok = false;  // refused at its second byte (byte 0 is never taken, so c1 = 0
+                                 // means a one-byte token)
                 } else if (str_room >= 0 && pc != kNotPlain) {
                     ok = static_cast<int32_t>(pc) <= str_room;
                 } else {
@@ -1472,6 +1482,7 @@ struct sixi_schema {
     uint64_t* d_voff = nullptr;
     uint8_t* d_vflags = nullptr;
     uint8_t* d_vfirst = nullptr;
+    uint8_t* d_vsecond = nullptr;
     uint16_t* d_vplain = nullptr;
 
     Prog host_prog() const {
@@ -1574,7 +1585,7 @@ struct sixi_schema {
         }
         return true;
     }
-    SVocab svocab() const { return SVocab{d_vbytes, d_voff, d_vflags, d_vfirst, d_vplain, vocab}; }
+    SVocab svocab() const { return SVocab{d_vbytes, d_voff, d_vflags, d_vfirst, d_vsecond, d_vplain, vocab}; }
 };
 
 namespace {
@@ -1710,16 +1721,19 @@ int32_t sixi_schema_compile(int32_t device, const char* schema_json, size_t sche
         if (e == cudaSuccess) e = cudaMemcpy(g->d_voff, host_offsets, (static_cast<size_t>(vocab) + 1) * 8, cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMemcpy(g->d_vflags, fl.data(), vocab, cudaMemcpyHostToDevice);
         // per token: its first byte and, for plain string bodies, its code points (mask filters)
-        std::vector<uint8_t> first(vocab + 1, 0);
+        std::vector<uint8_t> first(vocab + 1, 0), second(vocab + 1, 0);
         std::vector<uint16_t> plain(vocab + 1, kNotPlain);
         for (uint32_t i = 0; i < vocab; ++i) {
             const uint64_t b0 = host_offsets[i], b1 = host_offsets[i + 1];
             if (b1 > b0) {
                 first[i] = host_bytes[b0];
+                if (b1 > b0 + 1) second[i] = host_bytes[b0 + 1];
                 plain[i] = plain_code_points(host_bytes + b0, static_cast<size_t>(b1 - b0));
             }
         }
         if (e == cudaSuccess) e = cudaMalloc(&g->d_vfirst, vocab + 16);
+        if (e == cudaSuccess) e = cudaMalloc(&g->d_vsecond, vocab + 16);
+        if (e == cudaSuccess) e = cudaMemcpy(g->d_vsecond, second.data(), vocab, cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMalloc(&g->d_vplain, 2ull * vocab + 16);
         if (e == cudaSuccess) e = cudaMemcpy(g->d_vfirst, first.data(), vocab, cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMemcpy(g->d_vplain, plain.data(), 2ull * vocab, cudaMemcpyHostToDevice);
@@ -1743,6 +1757,7 @@ void sixi_schema_destroy(sixi_schema* g) {
         cudaFree(g->d_voff);
         cudaFree(g->d_vflags);
         cudaFree(g->d_vfirst);
+        cudaFree(g->d_vsecond);
         cudaFree(g->d_vplain);
     }
     delete g;

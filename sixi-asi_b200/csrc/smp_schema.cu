@@ -1328,9 +1328,24 @@ __global__ void schema_reset_kernel(State* s, uint32_t n, uint32_t root) {
     if (r < n) start_state(s[r], root);
 }
 
-// One block per (row, vocabulary slice): the row's state in shared memory, one token per thread
-// walked on an overlay of the stack, 32 verdicts per warp ballot written as a mask word.
-__global__ void __launch_bounds__(kMaskThreads) schema_mask_kernel(const Prog P, const SVocab V, const State* states,
+constexpr uint32_t kTileWords = 256;   // mask words per tile of a block (8,192 tokens)
+constexpr uint32_t kQueueCap = 4096;   // queued walks per tile (more are walked in place)
+
+// Whether the row at state `st` takes token `id` (not EOS, not special): its bytes walked on an
+// overlay of the stack.
+__device__ __noinline__ bool walk_token(const Prog& P, const SVocab& V, const State& st, uint32_t id) {
+    const uint64_t b0 = V.off[id], b1 = V.off[id + 1];
+    OverlayStack<SIXI_SCHEMA_MASK_OPENS> ov(st);
+    Machine<OverlayStack<SIXI_SCHEMA_MASK_OPENS>> m(P, ov);
+    bool ok = b1 > b0;
+    for (uint64_t j = b0; j < b1 && ok; ++j) ok = m.step(V.bytes[j]);
+    return ok;
+}
+
+// One block per (row, vocabulary slice): the row's state in shared memory, per-state tables of
+// first bytes (and of bytes after a space), tokens decided by those tables or queued for a walk of
+// their bytes on an overlay of the stack, 32 verdicts per mask word.
+__global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog P, const SVocab V, const State* states,
                                                                    uint32_t* masks, uint64_t stride) {
     static_assert(kMaskThreads >= 256, "one thread per first byte");
     __shared__ State st;
@@ -1338,6 +1353,9 @@ __global__ void __launch_bounds__(kMaskThreads) schema_mask_kernel(const Prog P,
     __shared__ int32_t str_room;   // a plain-string top frame: code points it may still take, else -1
     __shared__ uint32_t first_ok[8];  // bytes the state takes as a token's first byte
     __shared__ uint32_t after_sp[8];  // bytes it takes after a space (most tokens start with one)
+    __shared__ uint32_t tile[kTileWords];  // mask words of the current tile
+    __shared__ uint32_t qid[kQueueCap];    // tokens of the tile that need a walk
+    __shared__ uint32_t qn;
     const uint32_t row = blockIdx.y;
     const uint32_t* src = reinterpret_cast<const uint32_t*>(&states[row]);
     for (uint32_t i = threadIdx.x; i < sizeof(State) / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(&st)[i] = src[i];
@@ -1374,37 +1392,60 @@ __global__ void __launch_bounds__(kMaskThreads) schema_mask_kernel(const Prog P,
         }
     }
     __syncthreads();
-    const uint32_t lane = threadIdx.x & 31u;
-    for (uint32_t w = blockIdx.x * (kMaskThreads / 32) + threadIdx.x / 32; w < words;
-         w += gridDim.x * (kMaskThreads / 32)) {
-        const uint32_t id = w * 32u + lane;
-        bool ok = false;
-        if (!dead && id < V.vocab) {
-            const uint8_t fl = V.flags[id];
-            if (fl & kTokEos) {
-                ok = eos_ok != 0u;
-            } else if (!(fl & kTokSpecial)) {
-                const uint32_t c0 = V.first[id];
-                const uint16_t pc = V.plain[id];
-                const uint32_t c1 = V.second[id];
-                if (!((first_ok[c0 >> 5] >> (c0 & 31u)) & 1u)) {
-                    ok = false;  // also every empty token (byte 0 is never a first byte)
-                } else if (c0 == ' ' && c1 != 0u && !((after_sp[c1 >> 5] >> (c1 & 31u)) & 1u)) {
-                    ok = false;  // refused at its second byte (byte 0 is never taken, so c1 = 0
-                                 // means a one-byte token)
-                } else if (str_room >= 0 && pc != kNotPlain) {
-                    ok = static_cast<int32_t>(pc) <= str_room;
-                } else {
-                    const uint64_t b0 = V.off[id], b1 = V.off[id + 1];
-                    OverlayStack<SIXI_SCHEMA_MASK_OPENS> ov(st);
-                    Machine<OverlayStack<SIXI_SCHEMA_MASK_OPENS>> m(P, ov);
-                    ok = b1 > b0;
-                    for (uint64_t j = b0; j < b1 && ok; ++j) ok = m.step(V.bytes[j]);
+    // Tiles of kTileWords mask words of this block's contiguous range: the table tests decide most
+    // tokens at once; the rest are queued and walked by the whole block together, so that a walk
+    // does not hold up a warp of decided tokens; the tile's words are written once at the end.
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t wpb = (words + gridDim.x - 1u) / gridDim.x;
+    const uint32_t w_begin = blockIdx.x * wpb;
+    const uint32_t w_end = w_begin + wpb < words ? w_begin + wpb : words;
+    for (uint32_t t0 = w_begin; t0 < w_end; t0 += kTileWords) {
+        const uint32_t nw = w_end - t0 < kTileWords ? w_end - t0 : kTileWords;
+        if (threadIdx.x == 0) qn = 0u;
+        __syncthreads();
+        for (uint32_t wi = warp; wi < nw; wi += kMaskThreads / 32) {
+            const uint32_t id = (t0 + wi) * 32u + lane;
+            bool ok = false, walk = false;
+            if (!dead && id < V.vocab) {
+                const uint8_t fl = V.flags[id];
+                if (fl & kTokEos) {
+                    ok = eos_ok != 0u;
+                } else if (!(fl & kTokSpecial)) {
+                    const uint32_t c0 = V.first[id];
+                    const uint32_t c1 = V.second[id];
+                    const uint16_t pc = V.plain[id];
+                    if (!((first_ok[c0 >> 5] >> (c0 & 31u)) & 1u)) {
+                        ok = false;  // also every empty token (byte 0 is never a first byte)
+                    } else if (c0 == ' ' && c1 != 0u && !((after_sp[c1 >> 5] >> (c1 & 31u)) & 1u)) {
+                        ok = false;  // refused at its second byte (c1 = 0: a one-byte token)
+                    } else if (str_room >= 0 && pc != kNotPlain) {
+                        ok = static_cast<int32_t>(pc) <= str_room;
+                    } else {
+                        walk = true;
+                    }
                 }
             }
+            const unsigned wm = __ballot_sync(0xFFFFFFFFu, walk);
+            uint32_t base = 0u;
+            if (lane == 0 && wm != 0u) base = atomicAdd(&qn, static_cast<uint32_t>(__popc(wm)));
+            base = __shfl_sync(0xFFFFFFFFu, base, 0);
+            if (walk) {
+                const uint32_t slot = base + static_cast<uint32_t>(__popc(wm & ((1u << lane) - 1u)));
+                if (slot < kQueueCap) qid[slot] = id;
+                else ok = walk_token(P, V, st, id);  // queue full: walk it here
+            }
+            const unsigned word = __ballot_sync(0xFFFFFFFFu, ok);
+            if (lane == 0) tile[wi] = word;
         }
-        const uint32_t word = __ballot_sync(0xFFFFFFFFu, ok);
-        if (lane == 0) out[w] = word;
+        __syncthreads();
+        const uint32_t nq = qn < kQueueCap ? qn : kQueueCap;
+        for (uint32_t i = threadIdx.x; i < nq; i += kMaskThreads) {
+            const uint32_t id = qid[i];
+            if (walk_token(P, V, st, id)) atomicOr(&tile[id / 32u - t0], 1u << (id & 31u));
+        }
+        __syncthreads();
+        for (uint32_t wi = threadIdx.x; wi < nw; wi += kMaskThreads) out[t0 + wi] = tile[wi];
+        __syncthreads();
     }
     for (uint32_t w = words + blockIdx.x * blockDim.x + threadIdx.x; w < stride && blockIdx.x == 0; w += blockDim.x)
         out[w] = 0u;

@@ -1297,13 +1297,20 @@ struct Compiler {
 constexpr int kMaskThreads = 256;
 constexpr uint32_t kTokSpecial = 1u, kTokEos = 2u;
 
+struct TokInfo {       // what the mask tables test of a token, in one 8-byte load
+    uint8_t flags;     // kTokSpecial / kTokEos
+    uint8_t first;     // first byte (0 for an empty token)
+    uint8_t second;    // second byte (0 for a shorter token)
+    uint8_t pad;
+    uint16_t plain;    // code points of a token that is a plain string body, else kNotPlain
+    uint16_t pad2;
+};
+static_assert(sizeof(TokInfo) == 8, "token record");
 struct SVocab {
     const uint8_t* bytes;
     const uint64_t* off;
     const uint8_t* flags;   // kTokSpecial / kTokEos
-    const uint8_t* first;   // first byte of each token (0 for an empty one)
-    const uint8_t* second;  // second byte of each token (0 for a shorter one)
-    const uint16_t* plain;  // code points of a token that is a plain string body, else kNotPlain
+    const TokInfo* info;
     uint32_t vocab;
 };
 constexpr uint16_t kNotPlain = 0xFFFFu;
@@ -1330,6 +1337,7 @@ __global__ void schema_reset_kernel(State* s, uint32_t n, uint32_t root) {
 
 constexpr uint32_t kTileWords = 256;   // mask words per tile of a block (8,192 tokens)
 constexpr uint32_t kQueueCap = 4096;   // queued walks per tile (more are walked in place)
+constexpr uint32_t kWordsPerIter = 4;  // mask words a warp tests per iteration
 
 // Whether the row at state `st` takes token `id` (not EOS, not special): its bytes walked on an
 // overlay of the stack.
@@ -1403,39 +1411,48 @@ __global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog
         const uint32_t nw = w_end - t0 < kTileWords ? w_end - t0 : kTileWords;
         if (threadIdx.x == 0) qn = 0u;
         __syncthreads();
-        for (uint32_t wi = warp; wi < nw; wi += kMaskThreads / 32) {
-            const uint32_t id = (t0 + wi) * 32u + lane;
-            bool ok = false, walk = false;
-            if (!dead && id < V.vocab) {
-                const uint8_t fl = V.flags[id];
-                if (fl & kTokEos) {
-                    ok = eos_ok != 0u;
-                } else if (!(fl & kTokSpecial)) {
-                    const uint32_t c0 = V.first[id];
-                    const uint32_t c1 = V.second[id];
-                    const uint16_t pc = V.plain[id];
-                    if (!((first_ok[c0 >> 5] >> (c0 & 31u)) & 1u)) {
+        // each warp takes kWordsPerIter words at a time, their records loaded together
+        for (uint32_t wi0 = warp * kWordsPerIter; wi0 < nw; wi0 += kWordsPerIter * (kMaskThreads / 32)) {
+            TokInfo ti[kWordsPerIter];
+#pragma unroll
+            for (uint32_t u = 0; u < kWordsPerIter; ++u) {
+                const uint32_t id = (t0 + wi0 + u) * 32u + lane;
+                ti[u] = (wi0 + u < nw && id < V.vocab) ? V.info[id] : TokInfo{kTokSpecial, 0, 0, 0, kNotPlain, 0};
+            }
+#pragma unroll
+            for (uint32_t u = 0; u < kWordsPerIter; ++u) {
+                const uint32_t wi = wi0 + u;
+                if (wi >= nw) break;  // warp-uniform
+                const uint32_t id = (t0 + wi) * 32u + lane;
+                bool ok = false, walk = false;
+                if (!dead) {
+                    const uint32_t c0 = ti[u].first, c1 = ti[u].second;
+                    if (ti[u].flags & kTokEos) {
+                        ok = eos_ok != 0u;
+                    } else if (ti[u].flags & kTokSpecial) {
+                        ok = false;  // also ids past the vocabulary
+                    } else if (!((first_ok[c0 >> 5] >> (c0 & 31u)) & 1u)) {
                         ok = false;  // also every empty token (byte 0 is never a first byte)
                     } else if (c0 == ' ' && c1 != 0u && !((after_sp[c1 >> 5] >> (c1 & 31u)) & 1u)) {
                         ok = false;  // refused at its second byte (c1 = 0: a one-byte token)
-                    } else if (str_room >= 0 && pc != kNotPlain) {
-                        ok = static_cast<int32_t>(pc) <= str_room;
+                    } else if (str_room >= 0 && ti[u].plain != kNotPlain) {
+                        ok = static_cast<int32_t>(ti[u].plain) <= str_room;
                     } else {
                         walk = true;
                     }
                 }
+                const unsigned wm = __ballot_sync(0xFFFFFFFFu, walk);
+                uint32_t base = 0u;
+                if (lane == 0 && wm != 0u) base = atomicAdd(&qn, static_cast<uint32_t>(__popc(wm)));
+                base = __shfl_sync(0xFFFFFFFFu, base, 0);
+                if (walk) {
+                    const uint32_t slot = base + static_cast<uint32_t>(__popc(wm & ((1u << lane) - 1u)));
+                    if (slot < kQueueCap) qid[slot] = id;
+                    else ok = walk_token(P, V, st, id);  // queue full: walk it here
+                }
+                const unsigned word = __ballot_sync(0xFFFFFFFFu, ok);
+                if (lane == 0) tile[wi] = word;
             }
-            const unsigned wm = __ballot_sync(0xFFFFFFFFu, walk);
-            uint32_t base = 0u;
-            if (lane == 0 && wm != 0u) base = atomicAdd(&qn, static_cast<uint32_t>(__popc(wm)));
-            base = __shfl_sync(0xFFFFFFFFu, base, 0);
-            if (walk) {
-                const uint32_t slot = base + static_cast<uint32_t>(__popc(wm & ((1u << lane) - 1u)));
-                if (slot < kQueueCap) qid[slot] = id;
-                else ok = walk_token(P, V, st, id);  // queue full: walk it here
-            }
-            const unsigned word = __ballot_sync(0xFFFFFFFFu, ok);
-            if (lane == 0) tile[wi] = word;
         }
         __syncthreads();
         const uint32_t nq = qn < kQueueCap ? qn : kQueueCap;
@@ -1522,9 +1539,7 @@ struct sixi_schema {
     uint8_t* d_vbytes = nullptr;
     uint64_t* d_voff = nullptr;
     uint8_t* d_vflags = nullptr;
-    uint8_t* d_vfirst = nullptr;
-    uint8_t* d_vsecond = nullptr;
-    uint16_t* d_vplain = nullptr;
+    TokInfo* d_vinfo = nullptr;
 
     Prog host_prog() const {
         Prog p{};
@@ -1626,7 +1641,7 @@ struct sixi_schema {
         }
         return true;
     }
-    SVocab svocab() const { return SVocab{d_vbytes, d_voff, d_vflags, d_vfirst, d_vsecond, d_vplain, vocab}; }
+    SVocab svocab() const { return SVocab{d_vbytes, d_voff, d_vflags, d_vinfo, vocab}; }
 };
 
 namespace {
@@ -1761,23 +1776,19 @@ int32_t sixi_schema_compile(int32_t device, const char* schema_json, size_t sche
         if (e == cudaSuccess && nb) e = cudaMemcpy(g->d_vbytes, host_bytes, nb, cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMemcpy(g->d_voff, host_offsets, (static_cast<size_t>(vocab) + 1) * 8, cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMemcpy(g->d_vflags, fl.data(), vocab, cudaMemcpyHostToDevice);
-        // per token: its first byte and, for plain string bodies, its code points (mask filters)
-        std::vector<uint8_t> first(vocab + 1, 0), second(vocab + 1, 0);
-        std::vector<uint16_t> plain(vocab + 1, kNotPlain);
+        // per token: flags, first two bytes and, for plain string bodies, code points (mask tables)
+        std::vector<TokInfo> info(vocab + 1, TokInfo{0, 0, 0, 0, kNotPlain, 0});
         for (uint32_t i = 0; i < vocab; ++i) {
             const uint64_t b0 = host_offsets[i], b1 = host_offsets[i + 1];
+            info[i].flags = fl[i];
             if (b1 > b0) {
-                first[i] = host_bytes[b0];
-                if (b1 > b0 + 1) second[i] = host_bytes[b0 + 1];
-                plain[i] = plain_code_points(host_bytes + b0, static_cast<size_t>(b1 - b0));
+                info[i].first = host_bytes[b0];
+                if (b1 > b0 + 1) info[i].second = host_bytes[b0 + 1];
+                info[i].plain = plain_code_points(host_bytes + b0, static_cast<size_t>(b1 - b0));
             }
         }
-        if (e == cudaSuccess) e = cudaMalloc(&g->d_vfirst, vocab + 16);
-        if (e == cudaSuccess) e = cudaMalloc(&g->d_vsecond, vocab + 16);
-        if (e == cudaSuccess) e = cudaMemcpy(g->d_vsecond, second.data(), vocab, cudaMemcpyHostToDevice);
-        if (e == cudaSuccess) e = cudaMalloc(&g->d_vplain, 2ull * vocab + 16);
-        if (e == cudaSuccess) e = cudaMemcpy(g->d_vfirst, first.data(), vocab, cudaMemcpyHostToDevice);
-        if (e == cudaSuccess) e = cudaMemcpy(g->d_vplain, plain.data(), 2ull * vocab, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMalloc(&g->d_vinfo, sizeof(TokInfo) * (static_cast<size_t>(vocab) + 1));
+        if (e == cudaSuccess) e = cudaMemcpy(g->d_vinfo, info.data(), sizeof(TokInfo) * vocab, cudaMemcpyHostToDevice);
         if (e != cudaSuccess) {
             sixi_schema_destroy(g.release());
             set_err("device allocation failed");
@@ -1797,9 +1808,7 @@ void sixi_schema_destroy(sixi_schema* g) {
         cudaFree(g->d_vbytes);
         cudaFree(g->d_voff);
         cudaFree(g->d_vflags);
-        cudaFree(g->d_vfirst);
-        cudaFree(g->d_vsecond);
-        cudaFree(g->d_vplain);
+        cudaFree(g->d_vinfo);
     }
     delete g;
 }

@@ -1301,9 +1301,9 @@ struct TokInfo {       // what the mask tables test of a token, in one 8-byte lo
     uint8_t flags;     // kTokSpecial / kTokEos
     uint8_t first;     // first byte (0 for an empty token)
     uint8_t second;    // second byte (0 for a shorter token)
-    uint8_t after_q;   // the byte after the quote of a quoted token (0: the quote ends it)
+    uint8_t pad;
     uint16_t plain;    // code points of a token that is a plain string body, else kNotPlain
-    uint16_t quoted;   // a plain body then a quote: the body's code points, else kNotPlain
+    uint16_t pad2;
 };
 static_assert(sizeof(TokInfo) == 8, "token record");
 struct SVocab {
@@ -1359,8 +1359,6 @@ __global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog
     __shared__ State st;
     __shared__ uint32_t st_ok, eos_ok;
     __shared__ int32_t str_room;   // a plain-string top frame: code points it may still take, else -1
-    __shared__ int32_t str_need;   // ... and the code points it needs before it may close
-    __shared__ uint32_t after_close[8];  // bytes its container takes once it closes
     __shared__ uint32_t first_ok[8];  // bytes the state takes as a token's first byte
     __shared__ uint32_t after_sp[8];  // bytes it takes after a space (most tokens start with one)
     __shared__ uint32_t tile[kTileWords];  // mask words of the current tile
@@ -1371,7 +1369,6 @@ __global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog
     for (uint32_t i = threadIdx.x; i < sizeof(State) / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(&st)[i] = src[i];
     if (threadIdx.x < 8) first_ok[threadIdx.x] = 0u;
     if (threadIdx.x >= 8 && threadIdx.x < 16) after_sp[threadIdx.x - 8] = 0u;
-    if (threadIdx.x >= 16 && threadIdx.x < 24) after_close[threadIdx.x - 16] = 0u;
     __syncthreads();
     if (threadIdx.x == 0) st_ok = state_ok(P, st) ? 1u : 0u;
     __syncthreads();
@@ -1399,21 +1396,8 @@ __global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog
             const Node& N = P.nodes[t.node];
             const bool plain = t.kind == F_STR && N.extra == kNone && t.pos == 0u && (t.b & 0x1Fu) == 0u;
             const int64_t room = N.hi - static_cast<int64_t>(t.a);
-            const int64_t need = N.lo - static_cast<int64_t>(t.a);
             str_room = plain ? static_cast<int32_t>(room < 0 ? 0 : (room > 0x7FFFFFFF ? 0x7FFFFFFF : room)) : -1;
-            str_need = static_cast<int32_t>(need < 0 ? 0 : (need > 0x7FFFFFFF ? 0x7FFFFFFF : need));
         }
-    }
-    __syncthreads();
-    if (!dead && str_room >= 0 && threadIdx.x < 256) {
-        // The string's container after the closing quote does not depend on the string's text:
-        // close it at a length its bounds admit, then try each byte.
-        OverlayStack<SIXI_SCHEMA_MASK_OPENS> ov(st);
-        Machine<OverlayStack<SIXI_SCHEMA_MASK_OPENS>> m(P, ov);
-        Frame& f = ov.mut();
-        const Node& N = P.nodes[f.node];
-        if (static_cast<int64_t>(f.a) < N.lo) f.a = static_cast<uint32_t>(N.lo);
-        if (m.step('"') && m.step(threadIdx.x)) atomicOr(&after_close[threadIdx.x >> 5], 1u << (threadIdx.x & 31u));
     }
     __syncthreads();
     // Tiles of kTileWords mask words of this block's contiguous range: the table tests decide most
@@ -1433,7 +1417,7 @@ __global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog
 #pragma unroll
             for (uint32_t u = 0; u < kWordsPerIter; ++u) {
                 const uint32_t id = (t0 + wi0 + u) * 32u + lane;
-                ti[u] = (wi0 + u < nw && id < V.vocab) ? V.info[id] : TokInfo{kTokSpecial, 0, 0, 0, kNotPlain, kNotPlain};
+                ti[u] = (wi0 + u < nw && id < V.vocab) ? V.info[id] : TokInfo{kTokSpecial, 0, 0, 0, kNotPlain, 0};
             }
 #pragma unroll
             for (uint32_t u = 0; u < kWordsPerIter; ++u) {
@@ -1453,14 +1437,6 @@ __global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog
                         ok = false;  // refused at its second byte (c1 = 0: a one-byte token)
                     } else if (str_room >= 0 && ti[u].plain != kNotPlain) {
                         ok = static_cast<int32_t>(ti[u].plain) <= str_room;
-                    } else if (str_room >= 0 && ti[u].quoted != kNotPlain &&
-                               (static_cast<int32_t>(ti[u].quoted) > str_room ||
-                                static_cast<int32_t>(ti[u].quoted) < str_need ||
-                                (ti[u].after_q != 0u &&
-                                 !((after_close[ti[u].after_q >> 5] >> (ti[u].after_q & 31u)) & 1u)))) {
-                        ok = false;  // its body overruns the bounds, or its container refuses what follows
-                    } else if (str_room >= 0 && ti[u].quoted != kNotPlain && ti[u].after_q == 0u) {
-                        ok = true;   // a body within the bounds, then the closing quote
                     } else {
                         walk = true;
                     }
@@ -1801,7 +1777,7 @@ int32_t sixi_schema_compile(int32_t device, const char* schema_json, size_t sche
         if (e == cudaSuccess) e = cudaMemcpy(g->d_voff, host_offsets, (static_cast<size_t>(vocab) + 1) * 8, cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMemcpy(g->d_vflags, fl.data(), vocab, cudaMemcpyHostToDevice);
         // per token: flags, first two bytes and, for plain string bodies, code points (mask tables)
-        std::vector<TokInfo> info(vocab + 1, TokInfo{0, 0, 0, 0, kNotPlain, kNotPlain});
+        std::vector<TokInfo> info(vocab + 1, TokInfo{0, 0, 0, 0, kNotPlain, 0});
         for (uint32_t i = 0; i < vocab; ++i) {
             const uint64_t b0 = host_offsets[i], b1 = host_offsets[i + 1];
             info[i].flags = fl[i];
@@ -1809,16 +1785,6 @@ int32_t sixi_schema_compile(int32_t device, const char* schema_json, size_t sche
                 info[i].first = host_bytes[b0];
                 if (b1 > b0 + 1) info[i].second = host_bytes[b0 + 1];
                 info[i].plain = plain_code_points(host_bytes + b0, static_cast<size_t>(b1 - b0));
-                // a plain body (possibly empty) then a quote: what the mask needs to close a string
-                for (uint64_t q = b0; q < b1; ++q) {
-                    if (host_bytes[q] != '"') continue;
-                    const uint16_t cp = q == b0 ? 0 : plain_code_points(host_bytes + b0, static_cast<size_t>(q - b0));
-                    if (cp != kNotPlain) {
-                        info[i].quoted = cp;
-                        info[i].after_q = q + 1 < b1 ? host_bytes[q + 1] : 0u;
-                    }
-                    break;
-                }
             }
         }
         if (e == cudaSuccess) e = cudaMalloc(&g->d_vinfo, sizeof(TokInfo) * (static_cast<size_t>(vocab) + 1));

@@ -1335,8 +1335,9 @@ __global__ void schema_reset_kernel(State* s, uint32_t n, uint32_t root) {
     if (r < n) start_state(s[r], root);
 }
 
-constexpr uint32_t kTileWords = 256;   // mask words per tile of a block (8,192 tokens)
-constexpr uint32_t kQueueCap = 4096;   // queued walks per tile (more are walked in place)
+constexpr uint32_t kTileWords = 128;   // mask words per tile of a block (4,096 tokens)
+constexpr uint32_t kQueueCap = kTileWords * 32;  // a queue slot for every token of a tile
+constexpr uint32_t kProgSmem = 48 * 1024;  // programs up to this size are walked from shared memory
 constexpr uint32_t kWordsPerIter = 4;  // mask words a warp tests per iteration
 
 // Whether the row at state `st` takes token `id` (not EOS, not special): its bytes walked on an
@@ -1353,8 +1354,17 @@ __device__ __noinline__ bool walk_token(const Prog& P, const SVocab& V, const St
 // One block per (row, vocabulary slice): the row's state in shared memory, per-state tables of
 // first bytes (and of bytes after a space), tokens decided by those tables or queued for a walk of
 // their bytes on an overlay of the stack, 32 verdicts per mask word.
-__global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog P, const SVocab V, const State* states,
-                                                                   uint32_t* masks, uint64_t stride) {
+__global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog PG, const SVocab V, const State* states,
+                                                                   uint32_t* masks, uint64_t stride, uint32_t prog_in_smem) {
+    // The automaton's tables are read by every step of every walk, in dependent chains: a copy in
+    // shared memory keeps them off the global-memory latency (the program is a few KB for a
+    // typical schema; larger ones are walked from global memory).
+    extern __shared__ __align__(16) uint8_t sprog[];
+    if (prog_in_smem) {
+        const uint4* src4 = reinterpret_cast<const uint4*>(PG.base);
+        for (uint32_t i = threadIdx.x; i < PG.bytes / 16u; i += blockDim.x) reinterpret_cast<uint4*>(sprog)[i] = src4[i];
+    }
+    const Prog P = prog_in_smem ? rebase(PG, sprog) : PG;
     static_assert(kMaskThreads >= 256, "one thread per first byte");
     __shared__ State st;
     __shared__ uint32_t st_ok, eos_ok;
@@ -1445,17 +1455,13 @@ __global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog
                 uint32_t base = 0u;
                 if (lane == 0 && wm != 0u) base = atomicAdd(&qn, static_cast<uint32_t>(__popc(wm)));
                 base = __shfl_sync(0xFFFFFFFFu, base, 0);
-                if (walk) {
-                    const uint32_t slot = base + static_cast<uint32_t>(__popc(wm & ((1u << lane) - 1u)));
-                    if (slot < kQueueCap) qid[slot] = id;
-                    else ok = walk_token(P, V, st, id);  // queue full: walk it here
-                }
+                if (walk) qid[base + static_cast<uint32_t>(__popc(wm & ((1u << lane) - 1u)))] = id;  // < kQueueCap
                 const unsigned word = __ballot_sync(0xFFFFFFFFu, ok);
                 if (lane == 0) tile[wi] = word;
             }
         }
         __syncthreads();
-        const uint32_t nq = qn < kQueueCap ? qn : kQueueCap;
+        const uint32_t nq = qn;
         for (uint32_t i = threadIdx.x; i < nq; i += kMaskThreads) {
             const uint32_t id = qid[i];
             if (walk_token(P, V, st, id)) atomicOr(&tile[id / 32u - t0], 1u << (id & 31u));
@@ -1765,7 +1771,12 @@ int32_t sixi_schema_compile(int32_t device, const char* schema_json, size_t sche
             dp.next = static_cast<const int16_t*>(put(g->next.data(), g->next.size() * 2, table_bytes(g->next)));
             dp.info = static_cast<const DfaInfo*>(put(g->info.data(), g->info.size() * sizeof(DfaInfo), table_bytes(g->info)));
         }
+        dp.base = static_cast<const uint8_t*>(g->d_prog);
+        dp.bytes = static_cast<uint32_t>(o);
         g->dprog = dp;
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(schema_mask_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kProgSmem));
         std::vector<uint8_t> fl(vocab + 1, 0);
         for (uint32_t i = 0; i < vocab; ++i) fl[i] = host_flags && (host_flags[i] & 1u) ? kTokSpecial : 0;
         if (eos_id >= 0) fl[static_cast<uint32_t>(eos_id)] = kTokEos;
@@ -1835,8 +1846,10 @@ int32_t sixi_schema_fill_masks(const sixi_schema* g, const sixi_schema_state* st
     uint32_t bx = (words + (kMaskThreads / 32) - 1) / (kMaskThreads / 32);
     const uint32_t want = std::max(1u, 592u / n_rows);  // about four blocks per SM over the batch
     bx = std::min(bx, want);
-    schema_mask_kernel<<<dim3(bx, n_rows), kMaskThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        g->dprog, g->svocab(), reinterpret_cast<const State*>(states), mask_words, mask_stride);
+    const uint32_t in_smem = g->dprog.bytes <= kProgSmem ? 1u : 0u;
+    schema_mask_kernel<<<dim3(bx, n_rows), kMaskThreads, in_smem ? g->dprog.bytes : 0u,
+                         static_cast<cudaStream_t>(stream)>>>(g->dprog, g->svocab(), reinterpret_cast<const State*>(states),
+                                                              mask_words, mask_stride, in_smem);
     return from_cuda(cudaGetLastError());
 }
 

@@ -63,7 +63,26 @@ struct Prog {  // device or host pointers
     uint32_t root;
     uint32_t any_object, any_array, any_string, any_number, any_literal;  // nodes of generic values
     uint32_t n_nodes, n_dfas;  // table sizes the row-state check tests frames against
+    const uint8_t* base;       // device: the one allocation holding every table (nullptr on the host)
+    uint32_t bytes;            // its size
 };
+
+// The same program with every table pointer moved from `P.base` to `to` (a copy of the
+// allocation, e.g. in shared memory).
+__host__ __device__ inline Prog rebase(const Prog& P, const uint8_t* to) {
+    Prog Q = P;
+    auto mv = [&](const void* p) { return to + (static_cast<const uint8_t*>(p) - P.base); };
+    Q.nodes = reinterpret_cast<const Node*>(mv(P.nodes));
+    Q.props = reinterpret_cast<const Prop*>(mv(P.props));
+    Q.ids = reinterpret_cast<const uint32_t*>(mv(P.ids));
+    Q.lits = reinterpret_cast<const Lit*>(mv(P.lits));
+    Q.bytes = mv(P.bytes);
+    Q.dfas = reinterpret_cast<const Dfa*>(mv(P.dfas));
+    Q.next = reinterpret_cast<const int16_t*>(mv(P.next));
+    Q.info = reinterpret_cast<const DfaInfo*>(mv(P.info));
+    Q.base = to;
+    return Q;
+}
 
 // frame kinds
 enum : uint8_t { F_ROOT = 0, F_OBJ, F_KEY, F_ARR, F_STR, F_NUM, F_LIT };

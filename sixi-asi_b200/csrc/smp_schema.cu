@@ -1362,7 +1362,7 @@ __global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog
     extern __shared__ __align__(16) uint8_t sprog[];
     if (prog_in_smem) {
         const uint4* src4 = reinterpret_cast<const uint4*>(PG.base);
-        for (uint32_t i = threadIdx.x; i < PG.bytes / 16u; i += blockDim.x) reinterpret_cast<uint4*>(sprog)[i] = src4[i];
+        for (uint32_t i = threadIdx.x; i < PG.base_bytes / 16u; i += blockDim.x) reinterpret_cast<uint4*>(sprog)[i] = src4[i];
     }
     const Prog P = prog_in_smem ? rebase(PG, sprog) : PG;
     static_assert(kMaskThreads >= 256, "one thread per first byte");
@@ -1772,7 +1772,7 @@ int32_t sixi_schema_compile(int32_t device, const char* schema_json, size_t sche
             dp.info = static_cast<const DfaInfo*>(put(g->info.data(), g->info.size() * sizeof(DfaInfo), table_bytes(g->info)));
         }
         dp.base = static_cast<const uint8_t*>(g->d_prog);
-        dp.bytes = static_cast<uint32_t>(o);
+        dp.base_bytes = static_cast<uint32_t>(o);
         g->dprog = dp;
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(schema_mask_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1846,8 +1846,8 @@ int32_t sixi_schema_fill_masks(const sixi_schema* g, const sixi_schema_state* st
     uint32_t bx = (words + (kMaskThreads / 32) - 1) / (kMaskThreads / 32);
     const uint32_t want = std::max(1u, 592u / n_rows);  // about four blocks per SM over the batch
     bx = std::min(bx, want);
-    const uint32_t in_smem = g->dprog.bytes <= kProgSmem ? 1u : 0u;
-    schema_mask_kernel<<<dim3(bx, n_rows), kMaskThreads, in_smem ? g->dprog.bytes : 0u,
+    const uint32_t in_smem = g->dprog.base_bytes <= kProgSmem ? 1u : 0u;
+    schema_mask_kernel<<<dim3(bx, n_rows), kMaskThreads, in_smem ? g->dprog.base_bytes : 0u,
                          static_cast<cudaStream_t>(stream)>>>(g->dprog, g->svocab(), reinterpret_cast<const State*>(states),
                                                               mask_words, mask_stride, in_smem);
     return from_cuda(cudaGetLastError());

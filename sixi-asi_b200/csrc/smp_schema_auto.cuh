@@ -64,7 +64,7 @@ struct Prog {  // device or host pointers
     uint32_t any_object, any_array, any_string, any_number, any_literal;  // nodes of generic values
     uint32_t n_nodes, n_dfas;  // table sizes the row-state check tests frames against
     const uint8_t* base;       // device: the one allocation holding every table (nullptr on the host)
-    uint32_t bytes;            // its size
+    uint32_t base_bytes;       // its size
 };
 
 // The same program with every table pointer moved from `P.base` to `to` (a copy of the

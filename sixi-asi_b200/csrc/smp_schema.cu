@@ -1335,8 +1335,8 @@ __global__ void schema_reset_kernel(State* s, uint32_t n, uint32_t root) {
     if (r < n) start_state(s[r], root);
 }
 
-constexpr uint32_t kTileWords = 128;   // mask words per tile of a block (4,096 tokens)
-constexpr uint32_t kQueueCap = kTileWords * 32;  // a queue slot for every token of a tile
+constexpr uint32_t kTileWords = 64;    // mask words per tile of a block (2,048 tokens)
+constexpr uint32_t kQueueCap = 8192;   // queued walks (a walk phase runs when a tile could overflow it)
 constexpr uint32_t kProgSmem = 48 * 1024;  // programs up to this size are walked from shared memory
 constexpr uint32_t kWordsPerIter = 4;  // mask words a warp tests per iteration
 
@@ -1371,7 +1371,6 @@ __global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog
     __shared__ int32_t str_room;   // a plain-string top frame: code points it may still take, else -1
     __shared__ uint32_t first_ok[8];  // bytes the state takes as a token's first byte
     __shared__ uint32_t after_sp[8];  // bytes it takes after a space (most tokens start with one)
-    __shared__ uint32_t tile[kTileWords];  // mask words of the current tile
     __shared__ uint32_t qid[kQueueCap];    // tokens of the tile that need a walk
     __shared__ uint32_t qn;
     const uint32_t row = blockIdx.y;
@@ -1417,11 +1416,27 @@ __global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog
     const uint32_t wpb = (words + gridDim.x - 1u) / gridDim.x;
     const uint32_t w_begin = blockIdx.x * wpb;
     const uint32_t w_end = w_begin + wpb < words ? w_begin + wpb : words;
-    for (uint32_t t0 = w_begin; t0 < w_end; t0 += kTileWords) {
-        const uint32_t nw = w_end - t0 < kTileWords ? w_end - t0 : kTileWords;
+    // Queued walks run once for the block's whole range (or when the queue could overflow): a
+    // walk phase leaves most threads waiting at the barrier, so there should be as few as can be.
+    auto walk_queue = [&]() {
+        const uint32_t nq = qn;
+        for (uint32_t i = threadIdx.x; i < nq; i += kMaskThreads) {
+            const uint32_t id = qid[i];
+            if (walk_token(P, V, st, id)) atomicOr(&out[id / 32u], 1u << (id & 31u));
+        }
+        __syncthreads();
         if (threadIdx.x == 0) qn = 0u;
         __syncthreads();
-        // each warp takes kWordsPerIter words at a time, their records loaded together
+    };
+    if (threadIdx.x == 0) qn = 0u;
+    __syncthreads();
+    for (uint32_t t0 = w_begin; t0 < w_end; t0 += kTileWords) {
+        const uint32_t nw = w_end - t0 < kTileWords ? w_end - t0 : kTileWords;
+        const uint32_t q_now = qn;  // every thread reads it before any thread adds to it again
+        __syncthreads();
+        if (q_now + kTileWords * 32u > kQueueCap) walk_queue();
+        // each warp takes kWordsPerIter words at a time, their records loaded together; the
+        // decided bits go out at once, the walks' bits are OR-ed in later
         for (uint32_t wi0 = warp * kWordsPerIter; wi0 < nw; wi0 += kWordsPerIter * (kMaskThreads / 32)) {
             TokInfo ti[kWordsPerIter];
 #pragma unroll
@@ -1457,19 +1472,12 @@ __global__ void __launch_bounds__(kMaskThreads, 3) schema_mask_kernel(const Prog
                 base = __shfl_sync(0xFFFFFFFFu, base, 0);
                 if (walk) qid[base + static_cast<uint32_t>(__popc(wm & ((1u << lane) - 1u)))] = id;  // < kQueueCap
                 const unsigned word = __ballot_sync(0xFFFFFFFFu, ok);
-                if (lane == 0) tile[wi] = word;
+                if (lane == 0) out[t0 + wi] = word;
             }
         }
         __syncthreads();
-        const uint32_t nq = qn;
-        for (uint32_t i = threadIdx.x; i < nq; i += kMaskThreads) {
-            const uint32_t id = qid[i];
-            if (walk_token(P, V, st, id)) atomicOr(&tile[id / 32u - t0], 1u << (id & 31u));
-        }
-        __syncthreads();
-        for (uint32_t wi = threadIdx.x; wi < nw; wi += kMaskThreads) out[t0 + wi] = tile[wi];
-        __syncthreads();
     }
+    walk_queue();
     for (uint32_t w = words + blockIdx.x * blockDim.x + threadIdx.x; w < stride && blockIdx.x == 0; w += blockDim.x)
         out[w] = 0u;
 }

@@ -179,3 +179,20 @@ def test_malformed_states_are_frozen_not_walked(vocab):
     ast = g.advance(st, tok).cpu().numpy()
     assert ast[0] == 0 and (ast[1:] != 0).all(), ast
     g.close()
+
+
+def test_large_batches_give_the_same_masks(vocab):
+    # 640 rows: one block per row, whose walk queue fills and is walked several times in the
+    # middle of the row; against the same states masked four rows at a time
+    toks, flags, eos, tk = vocab
+    for name in ("person", "formats"):
+        g = SchemaGrammar(0, SCHEMAS[name], toks, flags, eos)
+        pre, lens, _ = prefix_rows(name, tk, 64, seed=41)
+        st = g.new_states(64)
+        assert (g.advance(st, torch.from_numpy(pre).cuda(), torch.from_numpy(lens).cuda()).cpu().numpy() == 0).all()
+        big = st.repeat(10, 1)
+        m_big = g.fill_masks(big)
+        m_small = torch.cat([g.fill_masks(big[i:i + 4]) for i in range(0, big.shape[0], 4)])
+        torch.cuda.synchronize()
+        assert torch.equal(m_big, m_small), name
+        g.close()

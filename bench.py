@@ -125,14 +125,14 @@ def algorithmic_bytes(base: dict) -> int:
     return ROWS * VOCAB * 4 + 4 * int(base["hist_off"][-1])
 
 
-def profiled_traffic(name: str = "row_kernel_sample_config2.md") -> int | None:
+def profiled_traffic(name: str = "row_kernel_sample_config2.md", key: str = "traffic_bytes_per_launch") -> int | None:
     """DRAM bytes (read + write) per row_kernel launch of a workload from its committed ncu summary
-    (profiles/<name>), or None when it is absent."""
+    (profiles/<name>, the line `<key>: <bytes>`), or None when it is absent."""
     import re
 
     p = REPO / "profiles" / name
     try:
-        m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", p.read_text())
+        m = re.search(key + r":\s*(\d+)", p.read_text())
     except OSError:
         return None
     return int(m.group(1)) if m else None
@@ -760,6 +760,8 @@ def run_config5(args) -> int:
         del graph
         dist.barrier()
         dist.destroy_process_group()
+    t1024 = profiled_traffic("config5_sharded_splits.md", key="traffic_bytes_per_1024_rows")
+    traffic = int(t1024 * R / 1024) if t1024 else None
     if rank == 0:
         line = {
             "metric": "sampled rows/s, 8,192 rows x V=151,936 fp32 partitioned over N GPUs (config 5)",
@@ -771,8 +773,10 @@ def run_config5(args) -> int:
                        "vocab": VOCAB, "parallelism": f"rows partitioned, {world} GPU(s), no collective",
                        "l2": f"inputs larger than L2: {R * VOCAB * 4 / 1e6:.0f} MB of logits per GPU"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
-                         "bytes_per_launch": int(nbytes)},
+                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
+                         "bytes_per_launch": int(nbytes),
+                         "traffic_note": "ncu DRAM bytes of a 1,024-row launch of the same mix, scaled to this "
+                                         "rank's rows (profiles/config5_sharded_splits.md)"},
             "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": args.steps, "clocks": clk,
         }
         print(json.dumps(line), flush=True)

@@ -229,6 +229,10 @@ int main() {
         ++total;
         passed += sharded_case(2, 151936, 64, 8) ? 1 : 0;
     }
+    if (n_dev >= 4) {  // every GPU of the box, up to 8 slices
+        ++total;
+        passed += sharded_case(n_dev < 8 ? n_dev : 8, 151936, 64, 9) ? 1 : 0;
+    }
     std::printf("%d/%d sharded cases passed (%d GPUs)\n", passed, total, n_dev);
     return passed == total && g_fail == 0 ? 0 : 1;
 }

@@ -27,7 +27,7 @@ bool plan_rows(uint32_t vocab, uint32_t n_rows, uint32_t sms, LaunchPlan* plan) 
     while (c <= 16 && chunk_for(vocab, c) > kMaxChunk) c *= 2;
     if (c > 16) return false;
     // widen the cluster (up to 8 CTAs) while the batch would leave more than half of the SMs idle;
-    // 16-CTA clusters for a lone row measured slower (50.9 against 23.2 us per config-1 step)
+    // 16-CTA clusters for a lone row measured slower (18.1 against 16.4 us per config-1 step)
     while (c < 8 && n_rows > 0 && static_cast<uint64_t>(n_rows) * c * 2 <= sms && chunk_for(vocab, 2 * c) >= 2048) c *= 2;
     plan->cluster = c;
     plan->chunk = chunk_for(vocab, c);

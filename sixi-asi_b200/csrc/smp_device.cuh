@@ -62,8 +62,9 @@ __device__ __forceinline__ uint32_t fkey(float f) {
 }
 
 __device__ __forceinline__ float kval(uint32_t k) {
-    const uint32_t b = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
-    return __uint_as_float(b);
+    // (k & 0x80000000) ? (k & 0x7FFFFFFF) : ~k, as one shift and one three-input logic operation
+    const uint32_t s = static_cast<uint32_t>(static_cast<int32_t>(k) >> 31);
+    return __uint_as_float(k ^ (0x80000000u | ~s));
 }
 
 __device__ __forceinline__ uint64_t comp_of(uint32_t key, uint32_t id) {
@@ -334,6 +335,25 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// L2 policy for data read exactly once: evicted first, so that streaming a batch of logits through
+// L2 does not displace what the launch re-reads (its instructions among them: the serial phases of
+// the row engine run long straight-line code whose L2 misses go to HBM).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// bulk_g2s with an L2 cache policy (from l2_evict_first_policy)
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
 }
 

@@ -124,9 +124,11 @@ __host__ __device__ inline uint32_t umax(uint32_t a, uint32_t b) { return a > b 
 // Regions (lifetimes):
 //   K  keys (staging area of the bulk copies, then the keys of the chunk; live throughout)
 //   X  list path: MA, CTA 0's merge area (remote writes before CS1, read in phase B);
-//      mass path: H/HC local histograms (remote reads between CS2 and CS3), then CG/CGC
+//      mass path: the local weight histograms HB/HA/HLO (remote reads between CS2 and CS3), then
+//      CG/CGC
 //   Y  phase A: history bitmap + mask words (until P0 ends), then the local list LL;
-//      mass path: the two gather buffers
+//      mass path: the local counts HC (k-bound rows, remote reads between CS2 and CS3), then the
+//      two gather buffers
 //   Z  phase A: per-thread-maximum histogram; later the block-select digit histograms BH/BW
 //   R  reduced histogram segment (remote reads right after CS3), then the refine rounds
 //      double-buffered digit histograms (remote reads, first written two rounds after CS3)
@@ -475,23 +477,19 @@ __device__ __forceinline__ unsigned long long block_select(const unsigned long l
         for (uint32_t q = 0; q < C; ++q) total += cnt[q];
         if (total <= 4u) {
             // a handful of entries: every thread evaluates them (the same broadcast reads), so no
-            // exchange and no barrier is needed
+            // exchange and no barrier is needed. Each entry is inserted into four registers kept in
+            // descending order (no indexed array: that would live in local memory, whose L1 misses
+            // cost an L2 round trip each here).
             unsigned long long e4[4] = {0ull, 0ull, 0ull, 0ull};
-            uint32_t m = 0;
             for (uint32_t q = 0; q < C; ++q) {
-                for (uint32_t i = 0; i < cnt[q] && m < 4u; ++i) {
-                    const unsigned long long e = g[q * seg + i];
-                    e4[m++] = (e >= lowb && e != excl) ? e : 0ull;
-                }
-            }
+                for (uint32_t i = 0; i < cnt[q]; ++i) {
+                    unsigned long long e = g[q * seg + i];
+                    e = (e >= lowb && e != excl) ? e : 0ull;
 #pragma unroll
-            for (int i = 0; i < 3; ++i) {  // descending (a 4-element bubble network)
-#pragma unroll
-                for (int j = 0; j < 3 - i; ++j) {
-                    if (e4[j] < e4[j + 1]) {
-                        const unsigned long long t = e4[j];
-                        e4[j] = e4[j + 1];
-                        e4[j + 1] = t;
+                    for (int j = 0; j < 4; ++j) {  // insertion: e4 stays sorted, e carries the smaller
+                        const unsigned long long hi = e4[j] > e ? e4[j] : e;
+                        e = e4[j] > e ? e : e4[j];
+                        e4[j] = hi;
                     }
                 }
             }
@@ -808,18 +806,19 @@ __device__ __forceinline__ float q_of(const QView& v, uint32_t i) {
 // 32-bit parts, w = a * 2^32 + b * 2^16 + c (a < 2^12, b, c < 2^16): with at most 2^16 keys per
 // CTA none of the part sums can wrap, so the adds are fire-and-forget. Returns this thread's
 // share of the min-p prefix mass (keys >= x_minp) when use_minp. Kept out of line so that the
-// loop is scheduled with the whole register budget. The adds are predicated reductions (no
-// branches): on the key being valid and the part being non-zero; the b, a and count parts are
-// at fixed offsets from one address (HA = HB + kABins, HC = HB + 2 kABins).
+// loop is scheduled with the whole register budget. The pass is bound by integer issue, so the
+// per-key integer work is kept minimal: the adds are reductions predicated once per key (valid, and
+// a non-zero low word; a zero part adds nothing), and the b, a and c parts lie at fixed offsets from
+// one address (HA = HB + kABins, HLO = HB + 2 kABins); the counts (k-bound rows only) have their
+// own array HC.
+// (Measured at config 2, 38K keys per CTA: each integer operation added per key costs about
+// 0.6 us per pass; three fewer per key took the pass from 11.2-12.2 us to 8.9-10.8 us.)
 static __device__ __noinline__ unsigned long long mass_histogram(const uint32_t* K, int nq, const WeightCtx wc,
                                                           float x_minp, bool use_minp, bool need_counts,
-                                                          uint32_t* HLO, uint32_t* HB, uint32_t* HA,
-                                                          uint32_t* HC) {
+                                                          uint32_t* HB, uint32_t* HC) {
     static_assert(kABins * 4 == 8192, "part offsets below");
-    (void)HA;
-    (void)HC;
     const int tid = threadIdx.x;
-    const uint32_t lo_base = smem_u32(HLO), hi_base = smem_u32(HB);
+    const uint32_t hi_base = smem_u32(HB), hc_base = smem_u32(HC);
     unsigned long long wp = 0ull;
     const int nq8 = (nq + 1) >> 1;
     const int it8 = (nq8 + kNT - 1) / kNT;
@@ -838,29 +837,31 @@ static __device__ __noinline__ unsigned long long mass_histogram(const uint32_t*
             const float x = kval(k);
             const unsigned long long w = weight_of(x, wc);  // meaningless for k == 0 (never added)
             const uint32_t b = static_cast<uint32_t>(abin_of(x, wc));
-            const uint32_t c = static_cast<uint32_t>(w) & 0xFFFFu;
-            const uint32_t bm = static_cast<uint32_t>(w) >> 16;
-            const uint32_t alo = lo_base + 4u * b, ahi = hi_base + 4u * b;
-            am8[i] = k != 0u ? static_cast<uint32_t>(w >> 32) : 0u;
+            const uint32_t ahi = hi_base + 4u * b;
+            const bool valid = k != 0u;
+            am8[i] = valid ? static_cast<uint32_t>(w >> 32) : 0u;
             ah8[i] = ahi;
+            // The low parts are added when the key is valid and its low word is non-zero. Keys of
+            // zero weight (far below the maximum, all in the last bin) must add nothing: at low
+            // temperatures they are most of the row, and adds to one address serialise.
             asm volatile(
-                "{\n\t.reg .pred pk, p;\n\t"
+                "{\n\t.reg .pred pk;\n\t"
                 "setp.ne.u32 pk, %0, 0;\n\t"
-                "setp.ne.and.u32 p, %3, 0, pk;\n\t"
-                "@p red.shared.add.u32 [%1], %3;\n\t"
-                "setp.ne.and.u32 p, %4, 0, pk;\n\t"
-                "@p red.shared.add.u32 [%2], %4;\n\t}" ::"r"(k),
-                "r"(alo), "r"(ahi), "r"(c), "r"(bm)
+                "setp.ne.and.u32 pk, %2, 0, pk;\n\t"
+                "@pk red.shared.add.u32 [%1+16384], %3;\n\t"
+                "@pk red.shared.add.u32 [%1], %4;\n\t}" ::"r"(valid ? 1u : 0u),
+                "r"(ahi), "r"(static_cast<uint32_t>(w)), "r"(static_cast<uint32_t>(w) & 0xFFFFu),
+                "r"(static_cast<uint32_t>(w) >> 16)
                 : "memory");
             if (need_counts) {
                 asm volatile(
                     "{\n\t.reg .pred pk;\n\t"
                     "setp.ne.u32 pk, %0, 0;\n\t"
-                    "@pk red.shared.add.u32 [%1+16384], 1;\n\t}" ::"r"(k),
-                    "r"(ahi)
+                    "@pk red.shared.add.u32 [%1], 1;\n\t}" ::"r"(valid ? 1u : 0u),
+                    "r"(hc_base + 4u * b)
                     : "memory");
             }
-            if (use_minp) wp += (k != 0u && x >= x_minp) ? w : 0ull;
+            if (use_minp) wp += (valid && x >= x_minp) ? w : 0ull;
         }
         // The high parts are non-zero only for keys within 2^-11 of the row's largest weight, so
         // in nearly every warp all eight are zero: one vote skips their reductions.
@@ -903,17 +904,17 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     unsigned long long* MA = reinterpret_cast<unsigned long long*>(dyn + lay.off_x);
     uint32_t* HB = reinterpret_cast<uint32_t*>(dyn + lay.off_x);  // weight sums, bits 16..31 parts
     uint32_t* HA = HB + kABins;                                      // bits 32.. parts
-    uint32_t* HC = HB + 2 * kABins;                                  // counts
+    uint32_t* HLO = HB + 2 * kABins;                                 // bits 0..15 parts
     unsigned long long* CG = reinterpret_cast<unsigned long long*>(dyn + lay.off_x);  // HB/HA are dead
                                                                                       // once reduced
-    uint32_t* CGC = HC;
+    uint32_t* CGC = HB + 2 * kABins;  // HLO is dead once reduced
     // Y
     uint32_t* hb = reinterpret_cast<uint32_t*>(dyn + lay.off_y);
     uint32_t* mw = hb + (a.chunk / 32u + 2u);
     unsigned long long* LL = reinterpret_cast<unsigned long long*>(dyn + lay.off_y);
     unsigned long long* G0 = reinterpret_cast<unsigned long long*>(dyn + lay.off_y);
     unsigned long long* G1 = G0 + kGCap;
-    uint32_t* HLO = reinterpret_cast<uint32_t*>(dyn + lay.off_y);  // weight sums, bits 0..15 parts
+    uint32_t* HC = reinterpret_cast<uint32_t*>(dyn + lay.off_y);   // counts (k-bound rows)
     // Z
     uint32_t* H32 = reinterpret_cast<uint32_t*>(dyn + lay.off_z);
     uint32_t* BH = reinterpret_cast<uint32_t*>(dyn + lay.off_z);
@@ -945,13 +946,14 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
 #pragma unroll
         for (int s = 0; s < kStages; ++s) mbar_init(&ls->mbar[s], 1);
         fence_mbar_init();
+        const uint64_t pol = l2_evict_first_policy();  // the row is read once
         for (int s = 0; s < kStages; ++s) {
             const int32_t b0 = stage_vec(s) * 16, b1 = stage_vec(s + 1) * 16;
             if (b1 <= b0) continue;
             mbar_arrive_expect_tx(&ls->mbar[s], static_cast<uint32_t>(b1 - b0));
             for (int32_t off = b0; off < b1; off += 32768) {
                 const int32_t nb = (b1 - off) < 32768 ? (b1 - off) : 32768;
-                bulk_g2s(stg + off, gchunk + off, static_cast<uint32_t>(nb), &ls->mbar[s]);
+                bulk_g2s_hint(stg + off, gchunk + off, static_cast<uint32_t>(nb), &ls->mbar[s], pol);
             }
         }
         for (int q = 0; q < kCMax; ++q) {
@@ -1780,8 +1782,8 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             x_minp = static_cast<float>(static_cast<double>(M) +
                                         static_cast<double>(P->temperature) * log(static_cast<double>(P->min_p)));
         }
-        // Weight sums in three 32-bit parts (see mass_histogram). The c parts use region Y, which no
-        // CTA writes to before the third cluster barrier.
+        // Weight sums in three 32-bit parts (see mass_histogram), in region X. The counts use region
+        // Y, which no CTA writes to before the third cluster barrier.
         for (int i = tid; i < kABins; i += kNT) {
             HB[i] = 0u;
             HA[i] = 0u;
@@ -1792,7 +1794,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         // min-p prefix mass (only when min-p is set); the row mass Z is read off the assembled
         // cumulative histogram instead of being summed separately
         const bool use_minp = P->min_p > 0.0f;
-        unsigned long long wp = mass_histogram(K, nq, wc, x_minp, use_minp, need_counts, HLO, HB, HA, HC);
+        unsigned long long wp = mass_histogram(K, nq, wc, x_minp, use_minp, need_counts, HB, HC);
         if (use_minp) {
             wp = block_sum_u64<kNT>(wp, ls->red);
             if (tid < static_cast<int>(C)) cluster.map_shared_rank(cs, tid)->wmin[crank] = wp;
@@ -1801,16 +1803,18 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
 
     cluster.sync();  // ======================================================== CS2
 
-    // reduce histogram segment `crank` over all CTAs of the cluster
+    // reduce histogram segment `crank` over all CTAs of the cluster (the loads of the C sources
+    // are independent, so the unrolled loop keeps several remote round trips in flight)
     for (uint32_t i = tid; i < lay.seg; i += kNT) {
+        const uint32_t j = crank * lay.seg + i;
         unsigned long long s = 0ull;
         uint32_t sc = 0;
+#pragma unroll 4
         for (uint32_t q = 0; q < C; ++q) {
-            const uint32_t j = crank * lay.seg + i;
             s += (static_cast<unsigned long long>(cluster.map_shared_rank(HA, q)[j]) << 32) +
                  (static_cast<unsigned long long>(cluster.map_shared_rank(HB, q)[j]) << 16) +
                  cluster.map_shared_rank(HLO, q)[j];
-            if (need_counts) sc += cluster.map_shared_rank(HC, q)[crank * lay.seg + i];
+            if (need_counts) sc += cluster.map_shared_rank(HC, q)[j];
         }
         R[i] = s;
         RC[i] = sc;
@@ -2102,8 +2106,10 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     Refine rf{};
     // refine digit histograms (double-buffered) in region R: the reduced segments there are last
     // read remotely in the assembly above, at least one barrier before the first refine level
-    uint32_t* RH[2] = {reinterpret_cast<uint32_t*>(R), reinterpret_cast<uint32_t*>(R) + 256};
-    uint32_t* RW[2] = {reinterpret_cast<uint32_t*>(R + 256), reinterpret_cast<uint32_t*>(R + 512)};  // split
+    // (computed from the buffer index rather than held in a pointer array, which an indexed access
+    // would place in local memory)
+    auto RH = [&](int buf) -> uint32_t* { return reinterpret_cast<uint32_t*>(R) + 256 * buf; };
+    auto RW = [&](int buf) -> uint32_t* { return reinterpret_cast<uint32_t*>(R + 256) + 512 * buf; };  // split
 
     auto rf_match = [&](int e, uint32_t k) -> bool {
         if (k == 0u || (k & rf.pmask) != rf.prefix || xbin_g(k) != rf.bin) return false;
@@ -2112,17 +2118,17 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     };
     auto rf_build = [&](int buf) {  // local digit histogram of the refine level
         for (int i = tid; i < 256; i += kNT) {
-            RH[buf][i] = 0u;
-            RW[buf][i] = 0u;
-            RW[buf][256 + i] = 0u;
+            RH(buf)[i] = 0u;
+            RW(buf)[i] = 0u;
+            RW(buf)[256 + i] = 0u;
         }
         __syncthreads();
         for (int e = tid; e < len; e += kNT) {
             const uint32_t k = K[e];
             if (!rf_match(e, k)) continue;
             const uint32_t d = (k >> rf.shift) & ((1u << rf.width) - 1u);
-            atomicAdd(&RH[buf][d], 1u);
-            smem_add_split(&RW[buf][d], &RW[buf][256 + d], weight_of(kval(k), wc));
+            atomicAdd(&RH(buf)[d], 1u);
+            smem_add_split(&RW(buf)[d], &RW(buf)[256 + d], weight_of(kval(k), wc));
         }
         __syncthreads();
     };
@@ -2138,6 +2144,9 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         const int cur = round & 1;
         const int prev = cur ^ 1;
         bool read_buf = false;  // a gather buffer was read in this round
+        // Whether this round touched another CTA's shared memory (or let another CTA touch mine).
+        // The first round always counts: the histogram assembly before it read the peers' segments.
+        bool remote = round == 0;
         // a second pass runs only when the draw bin was gathered ahead of time (pending_kind 4)
 #pragma unroll 1
         for (int pass = 0; pass < 3; ++pass) {
@@ -2184,6 +2193,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 const unsigned long long h2 = block_max_u64<kNT>(hi, ls->red);
                 if (tid < static_cast<int>(C)) cluster.map_shared_rank(cs, tid)->mm[crank] = (l2 << 32) | h2;
                 st.pending_kind = 3;
+                remote = true;
             } else {
                 const unsigned long long* gp = gbuf ? G1 : G0;
                 sel = block_select(gp, gcn, C, gseg, st.target, wc, !cmode, lowb, ex, BH, ls, &cum_sel);
@@ -2206,6 +2216,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             }
             __syncthreads();
         } else if (st.pending_kind == 3) {
+            remote = true;
             if (rf.phase == 0) {
                 uint32_t klo = 0xFFFFFFFFu, khi = 0u;
                 for (uint32_t q = 0; q < C; ++q) {
@@ -2232,8 +2243,8 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 if (tid < 256) {
                     unsigned long long sc = 0ull, sw = 0ull;
                     for (uint32_t q = 0; q < C; ++q) {
-                        sc += cluster.map_shared_rank(RH[rf.buf], q)[tid];
-                        const uint32_t* rw = cluster.map_shared_rank(RW[rf.buf], q);
+                        sc += cluster.map_shared_rank(RH(rf.buf), q)[tid];
+                        const uint32_t* rw = cluster.map_shared_rank(RW(rf.buf), q);
                         sw += join_split(rw[tid], rw[256 + tid]);
                     }
                     BH[tid] = static_cast<uint32_t>(sc);
@@ -2384,6 +2395,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 }
             }
         } else if (st.pending_kind == 2) {
+            remote = true;
             if (st.stage == kStDSum) {
                 // dense residual: totals, then the owner CTA of the crossing finds the token
                 double rs = 0.0, ps = 0.0;
@@ -2553,6 +2565,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                     const unsigned long long tc = block_sum_u64<kNT>(c, ls->red);
                     if (tid < static_cast<int>(C)) cluster.map_shared_rank(cs, tid)->cnt[crank] = tc;
                     st.stage = kStCount;
+                    remote = true;
                     st.pending_kind = 2;
                 } else if (MODE == kModeVerify && rc.vrole == 0) {
                     const bool kept = dvalid && dcomp >= st.xcross && dcomp >= st.kbound && xd >= x_minp;
@@ -2593,6 +2606,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                                 dst->psum[crank] = psum;
                             }
                             st.stage = kStDSum;
+                            remote = true;
                             st.pending_kind = 2;
                         }
                     } else {
@@ -2652,9 +2666,16 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                 st.err = 4;
             }
         }
-        if (gq.bA >= 0) gather(gq.bA, gq.bufA, gq.bBlo, gq.bBhi, gq.bufB, gq.lowb);  // the one gather site
+        if (gq.bA >= 0) {
+            gather(gq.bA, gq.bufA, gq.bBlo, gq.bBhi, gq.bufB, gq.lowb);  // the one gather site
+            remote = true;
+        }
         if (st.pending_kind != 4) break;
         }  // pass
+        // A round that ends the row and neither read nor wrote a peer's shared memory needs no
+        // barrier: no CTA of the cluster touches another's memory again. The condition is
+        // cluster-uniform (the state advances identically in every CTA).
+        if ((st.stage == kStDone || st.err) && !remote) break;
         cluster.sync();  // ============================================ one barrier per round
         if (st.pending_kind == 5) {  // deferred draw gather (see kStDraw)
             st.pending_kind = 0;

@@ -338,9 +338,9 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
-// L2 policy for data read exactly once: evicted first, so that streaming a batch of logits through
-// L2 does not displace what the launch re-reads (its instructions among them: the serial phases of
-// the row engine run long straight-line code whose L2 misses go to HBM).
+// L2 policy for data read exactly once (a batch of logits): evicted first, so that streaming it
+// through L2 does not displace data that is read again (in an engine, the model's own working set).
+// At config 2 it measured neutral for the sampler itself.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t pol;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));

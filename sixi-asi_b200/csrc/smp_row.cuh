@@ -881,6 +881,85 @@ static __device__ __noinline__ unsigned long long mass_histogram(const uint32_t*
     return wp;
 }
 
+// The gather pass's scan (block-wide): pushes this CTA's keys of interval A (k - kloA < wA) and of
+// interval B as (key, id) composites >= lowb (lowb != 0: k-bound rows) into its segment of gather
+// buffers gA / gB in every CTA of the cluster; gfill[0..1] count them (above gseg: overfull). One
+// pass of 8 keys per iteration: per key only the interval tests (touch: one test against the
+// union); a warp reserves slots (local counter) only on the rare iterations where one of its lanes
+// holds a match, so the remote traffic is plain stores. Keys past the chunk read as 0, which no
+// interval contains. Kept out of line so that the loop is scheduled with the whole register budget
+// (inline, amid the round loop's live state, it measured 0.6 us slower per config-2 step).
+static __device__ __noinline__ void gather_scan(const uint32_t* K, int nq, uint32_t c0, uint32_t kloA, uint32_t wA,
+                                                uint32_t kloB, uint32_t wB, bool touch, uint32_t kloU, uint32_t wU,
+                                                unsigned long long lowb, unsigned long long* gA,
+                                                unsigned long long* gB, uint32_t gseg, uint32_t C,
+                                                unsigned int* gfill) {
+    cg::cluster_group cluster = cg::this_cluster();
+    const int tid = threadIdx.x;
+    const bool use_lowb = lowb != 0ull;
+    const int nq8 = (nq + 1) >> 1;
+    const int it8 = (nq8 + kNT - 1) / kNT;
+#pragma unroll 1
+    for (int m = 0; m < it8; ++m) {  // warp-uniform trip count
+        const int q = tid + m * kNT;
+        // groups q and q + nq8 (contiguous 16-byte loads across the warp); key i of the
+        // iteration is element 4 q + i (i < 4) or 4 (q + nq8) + i - 4
+        uint4 va = make_uint4(0u, 0u, 0u, 0u), vb = make_uint4(0u, 0u, 0u, 0u);
+        if (q < nq8) va = reinterpret_cast<const uint4*>(K)[q];
+        if (q < nq8 && q + nq8 < nq) vb = reinterpret_cast<const uint4*>(K)[q + nq8];
+        const uint32_t k8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+        bool hit = false;
+        if (touch) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) hit |= k8[i] - kloU < wU;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) hit |= (k8[i] - kloA < wA) | (k8[i] - kloB < wB);
+        }
+        if (__ballot_sync(0xFFFFFFFFu, hit) == 0u) continue;
+        uint32_t mA = 0u, mB = 0u;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            mA |= (k8[i] - kloA < wA) ? (1u << i) : 0u;
+            mB |= (k8[i] - kloB < wB) ? (1u << i) : 0u;
+        }
+        if (__ballot_sync(0xFFFFFFFFu, (mA | mB) != 0u) == 0u) continue;
+        if (use_lowb) {  // k-bound rows: drop entries below the composite bound
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int e = i < 4 ? 4 * q + i : 4 * (q + nq8) + i - 4;
+                if (comp_of(k8[i], c0 + static_cast<uint32_t>(e)) < lowb) {
+                    mA &= ~(1u << i);
+                    mB &= ~(1u << i);
+                }
+            }
+        }
+        uint32_t pA = warp_reserve(static_cast<uint32_t>(__popc(mA)), &gfill[0]);
+        uint32_t pB = warp_reserve(static_cast<uint32_t>(__popc(mB)), &gfill[1]);
+        uint32_t mk = mA | mB;
+        while (mk != 0u) {
+            const int i = __ffs(mk) - 1;
+            mk &= mk - 1u;
+            const int e = i < 4 ? 4 * q + i : 4 * (q + nq8) + i - 4;
+            const unsigned long long cp = comp_of(K[e], c0 + static_cast<uint32_t>(e));
+            if ((mA >> i) & 1u) {
+                if (pA < gseg) {
+#pragma unroll 1
+                    for (uint32_t dst = 0; dst < C; ++dst) cluster.map_shared_rank(gA, dst)[pA] = cp;
+                }
+                ++pA;
+            }
+            if ((mB >> i) & 1u) {
+                if (pB < gseg) {
+#pragma unroll 1
+                    for (uint32_t dst = 0; dst < C; ++dst) cluster.map_shared_rank(gB, dst)[pB] = cp;
+                }
+                ++pB;
+            }
+        }
+    }
+}
+
 template <int DT, int MODE>
 __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     constexpr int ESZ = (DT == SIXI_SMP_BF16) ? 2 : 4;
@@ -1046,7 +1125,10 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
     constexpr bool kRaw = (MODE == kModeGreedy) || (MODE == kModeVerify);
     const bool has_mask = rc.mask != nullptr;
     const bool use_pbits = rc.pen && !pen_smem;
-    uint32_t t_mk = 0u, t_mi = 0u, t_mn = 0xFFFFFFFFu, t_amax = 0u;
+    // t_mn1 tracks (smallest valid key) - 1 as an unsigned minimum, with invalid keys (0) wrapping
+    // to the neutral 0xFFFFFFFF: two integer operations per entry instead of three (P0 is bound
+    // by integer issue); t_mn is derived from it once P0 is done.
+    uint32_t t_mk = 0u, t_mi = 0u, t_mn = 0xFFFFFFFFu, t_mn1 = 0xFFFFFFFFu, t_amax = 0u;
     bool t_bad = false;  // an allowed raw logit is NaN or infinite (modes that do not track t_amax)
     // Entries of inactive rows are never allowed (MBIT is 0 for them). AMAX: track the largest
     // |bits| (raw-argmax modes, whose NaN keys are 0, and the frequency path); elsewhere a
@@ -1070,7 +1152,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             t_mk = ks_;                                                                      \
             t_mi = static_cast<uint32_t>(E);                                                 \
         }                                                                                    \
-        t_mn = (ks_ != 0u && ks_ < t_mn) ? ks_ : t_mn;                                       \
+        t_mn1 = min(t_mn1, ks_ - 1u);                                                        \
         (KOUT) = k_;                                                                         \
     }
     if (!pen_smem) {
@@ -1088,28 +1170,57 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
                     if (v < v1) raw4[m] = *reinterpret_cast<const uint4*>(stg + 16u * v);
                 }
                 __syncthreads();
+                // mb: the mask bits of the eight entries (all set for an active row without a mask,
+                // a case written out on its own so that no mask bit is tested)
+                auto admit8 = [&](const int32_t v, const uint4 r, const uint32_t mb, const bool plain) {
+                    const int32_t e0 = v * 8;
+                    const uint32_t pb = use_pbits ? (hb[e0 >> 5] >> (e0 & 31)) & 0xFFu : 0u;
+                    const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+                    uint32_t k8[8];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        SIXI_ADMIT(e0 + 2 * i, __uint_as_float(w4[i] << 16), plain ? 1u : (mb >> (2 * i)) & 1u,
+                                   (pb >> (2 * i)) & 1u, k8[2 * i], kRaw);
+                        SIXI_ADMIT(e0 + 2 * i + 1, __uint_as_float(w4[i] & 0xFFFF0000u),
+                                   plain ? 1u : (mb >> (2 * i + 1)) & 1u, (pb >> (2 * i + 1)) & 1u, k8[2 * i + 1], kRaw);
+                    }
+                    *reinterpret_cast<uint4*>(K + e0) = make_uint4(k8[0], k8[1], k8[2], k8[3]);
+                    *reinterpret_cast<uint4*>(K + e0 + 4) = make_uint4(k8[4], k8[5], k8[6], k8[7]);
+                };
+                if (!has_mask && len > 0) {
+#pragma unroll
+                    for (int m = 0; m < kVecMax; ++m) {
+                        const int32_t v = v0 + tid + m * kNT;
+                        if (v < v1) admit8(v, raw4[m], 0xFFu, true);
+                    }
+                } else {
+#pragma unroll
+                    for (int m = 0; m < kVecMax; ++m) {
+                        const int32_t v = v0 + tid + m * kNT;
+                        if (v < v1) {
+                            const uint32_t g = static_cast<uint32_t>(c0 + v * 8);
+                            admit8(v, raw4[m], (has_mask ? (mw[(g >> 5) - wbase] >> (g & 31)) & 0xFFu : 0xFFu) & act, false);
+                        }
+                    }
+                }
+                __syncthreads();
+            } else if (!has_mask && len > 0) {
+                // every entry allowed (no mask, active row): no mask bits to test
 #pragma unroll
                 for (int m = 0; m < kVecMax; ++m) {
                     const int32_t v = v0 + tid + m * kNT;
                     if (v < v1) {
-                        const int32_t e0 = v * 8;
-                        const uint32_t g = static_cast<uint32_t>(c0 + e0);
-                        const uint32_t mb = (has_mask ? (mw[(g >> 5) - wbase] >> (g & 31)) & 0xFFu : 0xFFu) & act;
-                        const uint32_t pb = use_pbits ? (hb[e0 >> 5] >> (e0 & 31)) & 0xFFu : 0u;
-                        const uint32_t w4[4] = {raw4[m].x, raw4[m].y, raw4[m].z, raw4[m].w};
-                        uint32_t k8[8];
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            SIXI_ADMIT(e0 + 2 * i, __uint_as_float(w4[i] << 16), (mb >> (2 * i)) & 1u,
-                                       (pb >> (2 * i)) & 1u, k8[2 * i], kRaw);
-                            SIXI_ADMIT(e0 + 2 * i + 1, __uint_as_float(w4[i] & 0xFFFF0000u), (mb >> (2 * i + 1)) & 1u,
-                                       (pb >> (2 * i + 1)) & 1u, k8[2 * i + 1], kRaw);
-                        }
-                        *reinterpret_cast<uint4*>(K + e0) = make_uint4(k8[0], k8[1], k8[2], k8[3]);
-                        *reinterpret_cast<uint4*>(K + e0 + 4) = make_uint4(k8[4], k8[5], k8[6], k8[7]);
+                        const float4 f = *reinterpret_cast<const float4*>(stg + 16u * v);
+                        const int32_t e0 = v * 4;
+                        const uint32_t pb = use_pbits ? (hb[e0 >> 5] >> (e0 & 31)) & 0xFu : 0u;
+                        uint32_t k0, k1, k2, k3;
+                        SIXI_ADMIT(e0 + 0, f.x, 1u, pb & 1u, k0, kRaw);
+                        SIXI_ADMIT(e0 + 1, f.y, 1u, (pb >> 1) & 1u, k1, kRaw);
+                        SIXI_ADMIT(e0 + 2, f.z, 1u, (pb >> 2) & 1u, k2, kRaw);
+                        SIXI_ADMIT(e0 + 3, f.w, 1u, (pb >> 3) & 1u, k3, kRaw);
+                        *reinterpret_cast<uint4*>(K + e0) = make_uint4(k0, k1, k2, k3);
                     }
                 }
-                __syncthreads();
             } else {
 #pragma unroll
                 for (int m = 0; m < kVecMax; ++m) {
@@ -1143,6 +1254,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             SIXI_ADMIT(e, x, mb, pb, k, kRaw);
             K[e] = k;
         }
+        t_mn = (t_mn1 == 0xFFFFFFFFu) ? 0xFFFFFFFFu : t_mn1 + 1u;
         // raw non-finite values of the entries seen so far (penalised entries are checked below,
         // on their raw keys, before a penalty could overflow them)
         if (!kRaw) t_bad = t_mk >= 0xFF800000u || t_mn <= 0x007FFFFFu;
@@ -1227,6 +1339,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             SIXI_ADMIT(e, KF[e], allowed(c0 + e) ? 1u : 0u, 0u, k, true);
             K[e] = k;
         }
+        t_mn = (t_mn1 == 0xFFFFFFFFu) ? 0xFFFFFFFFu : t_mn1 + 1u;
     }
 #undef SIXI_ADMIT
     // keys past the chunk end (up to a multiple of 4) are invalid
@@ -1942,71 +2055,8 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
         const uint32_t kloU = (wB != 0u && kloB < kloA) ? kloB : kloA;
         const unsigned long long khiU1 = (wB != 0u && khiB1 > khiA1) ? khiB1 : khiA1;
         const uint32_t wU = static_cast<uint32_t>(khiU1 - kloU);
-        const bool use_lowb = lowb != 0ull;
-        // One pass of 8 keys per iteration: per key only the interval tests; a warp reserves slots
-        // (local counter) only on the rare iterations where one of its lanes holds a match. Keys
-        // past the chunk read as 0, which no interval contains.
-        const int nq8 = (nq + 1) >> 1;
-        const int it8 = (nq8 + kNT - 1) / kNT;
-#pragma unroll 1
-        for (int m = 0; m < it8; ++m) {  // warp-uniform trip count
-            const int q = tid + m * kNT;
-            // groups q and q + nq8 (contiguous 16-byte loads across the warp); key i of the
-            // iteration is element 4 q + i (i < 4) or 4 (q + nq8) + i - 4
-            uint4 va = make_uint4(0u, 0u, 0u, 0u), vb = make_uint4(0u, 0u, 0u, 0u);
-            if (q < nq8) va = reinterpret_cast<const uint4*>(K)[q];
-            if (q < nq8 && q + nq8 < nq) vb = reinterpret_cast<const uint4*>(K)[q + nq8];
-            const uint32_t k8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
-            bool hit = false;
-            if (touch) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) hit |= k8[i] - kloU < wU;
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) hit |= (k8[i] - kloA < wA) | (k8[i] - kloB < wB);
-            }
-            if (__ballot_sync(0xFFFFFFFFu, hit) == 0u) continue;
-            uint32_t mA = 0u, mB = 0u;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                mA |= (k8[i] - kloA < wA) ? (1u << i) : 0u;
-                mB |= (k8[i] - kloB < wB) ? (1u << i) : 0u;
-            }
-            if (__ballot_sync(0xFFFFFFFFu, (mA | mB) != 0u) == 0u) continue;
-            if (use_lowb) {  // k-bound rows: drop entries below the composite bound
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int e = i < 4 ? 4 * q + i : 4 * (q + nq8) + i - 4;
-                    if (comp_of(k8[i], static_cast<uint32_t>(c0 + e)) < lowb) {
-                        mA &= ~(1u << i);
-                        mB &= ~(1u << i);
-                    }
-                }
-            }
-            uint32_t pA = warp_reserve(static_cast<uint32_t>(__popc(mA)), &ls->gfill[0]);
-            uint32_t pB = warp_reserve(static_cast<uint32_t>(__popc(mB)), &ls->gfill[1]);
-            uint32_t mk = mA | mB;
-            while (mk != 0u) {
-                const int i = __ffs(mk) - 1;
-                mk &= mk - 1u;
-                const int e = i < 4 ? 4 * q + i : 4 * (q + nq8) + i - 4;
-                const unsigned long long cp = comp_of(K[e], static_cast<uint32_t>(c0 + e));
-                if ((mA >> i) & 1u) {
-                    if (pA < gseg) {
-#pragma unroll 1
-                        for (uint32_t dst = 0; dst < C; ++dst) cluster.map_shared_rank(gA, dst)[pA] = cp;
-                    }
-                    ++pA;
-                }
-                if ((mB >> i) & 1u) {
-                    if (pB < gseg) {
-#pragma unroll 1
-                        for (uint32_t dst = 0; dst < C; ++dst) cluster.map_shared_rank(gB, dst)[pB] = cp;
-                    }
-                    ++pB;
-                }
-            }
-        }
+        gather_scan(K, nq, static_cast<uint32_t>(c0), kloA, wA, kloB, wB, touch, kloU, wU, lowb, gA, gB, gseg, C,
+                    ls->gfill);
         __syncthreads();
         const uint32_t tot = ls->gfill[0] | (ls->gfill[1] << 16);
         if (tid < static_cast<int>(C)) {  // publish my counts (above gseg: the bin is overfull)

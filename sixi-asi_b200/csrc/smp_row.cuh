@@ -881,6 +881,39 @@ static __device__ __noinline__ unsigned long long mass_histogram(const uint32_t*
     return wp;
 }
 
+// The list path's collect pass (block-wide): appends every key >= kthr of K[0, 4 * nq) as a
+// (key, id) composite to LL (unordered; slots past kLCap are counted in *lcount but not written).
+// Eight keys per iteration (two 16-byte loads, contiguous across the warp), slots reserved per
+// warp only where a lane holds a match; kept out of line so that the loop is scheduled with the
+// whole register budget. Keys past the chunk are 0, below every threshold (kthr >= 1).
+static __device__ __noinline__ void collect_scan(const uint32_t* K, int nq, uint32_t c0, uint32_t kthr,
+                                                 unsigned long long* LL, unsigned int* lcount) {
+    const int tid = threadIdx.x;
+    const int nq8 = (nq + 1) >> 1;
+    const int it8 = (nq8 + kNT - 1) / kNT;
+#pragma unroll 1
+    for (int m = 0; m < it8; ++m) {  // warp-uniform trip count
+        const int q = tid + m * kNT;
+        // key i of the iteration is element 4 q + i (i < 4) or 4 (q + nq8) + i - 4
+        uint4 va = make_uint4(0u, 0u, 0u, 0u), vb = make_uint4(0u, 0u, 0u, 0u);
+        if (q < nq8) va = reinterpret_cast<const uint4*>(K)[q];
+        if (q < nq8 && q + nq8 < nq) vb = reinterpret_cast<const uint4*>(K)[q + nq8];
+        const uint32_t k8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+        uint32_t mk = 0u;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mk |= (k8[i] >= kthr) ? (1u << i) : 0u;
+        if (__ballot_sync(0xFFFFFFFFu, mk != 0u) == 0u) continue;
+        uint32_t slot = warp_reserve(static_cast<uint32_t>(__popc(mk)), lcount);
+        while (mk != 0u) {
+            const int i = __ffs(mk) - 1;
+            mk &= mk - 1u;
+            const int e = i < 4 ? 4 * q + i : 4 * (q + nq8) + i - 4;
+            if (slot < static_cast<uint32_t>(kLCap)) LL[slot] = comp_of(K[e], c0 + static_cast<uint32_t>(e));
+            ++slot;
+        }
+    }
+}
+
 // The gather pass's scan (block-wide): pushes this CTA's keys of interval A (k - kloA < wA) and of
 // interval B as (key, id) composites >= lowb (lowb != 0: k-bound rows) into its segment of gather
 // buffers gA / gB in every CTA of the cluster; gfill[0..1] count them (above gseg: overfull). One
@@ -1460,24 +1493,7 @@ __global__ void __launch_bounds__(kNT, 1) row_kernel(const RowArgs a) {
             const uint32_t kthr = (tot < kl) ? 1u : static_cast<uint32_t>(
                 block_min_bc((t_mk != 0u && xbin(t_mk) <= b1) ? t_mk : 0xFFFFFFFFull, ls));
             // collect the superset into LL (unordered)
-            for (int m = 0; m < nq_iter; ++m) {
-                const int q = tid + m * kNT;
-                uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                if (q < nq) v = reinterpret_cast<const uint4*>(K)[q];
-                const uint32_t k4[4] = {v.x, v.y, v.z, v.w};
-                uint32_t c = 0;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) c += (k4[i] >= kthr) ? 1u : 0u;
-                if (__ballot_sync(0xFFFFFFFFu, c != 0u) == 0u) continue;
-                uint32_t slot = warp_reserve(c, &ls->lcount);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    if (k4[i] >= kthr) {
-                        if (slot < static_cast<uint32_t>(kLCap)) LL[slot] = comp_of(k4[i], static_cast<uint32_t>(c0 + 4 * q + i));
-                        ++slot;
-                    }
-                }
-            }
+            collect_scan(K, nq, static_cast<uint32_t>(c0), kthr, LL, &ls->lcount);
             __syncthreads();
             uint32_t ncand = ls->lcount;
             if (ncand > static_cast<uint32_t>(kLCap)) {

@@ -87,7 +87,7 @@ bool rows_ok(const sixi_smp* h, const sixi_smp_rows* rows) {
 RowArgs base_args(const sixi_smp* h, const sixi_smp_rows* rows, LaunchPlan* plan) {
     RowArgs a;
     std::memset(&a, 0, sizeof(a));
-    sixi_b200::plan_rows(h->vocab, rows->n_rows, sixi_b200::device_sm_count(h->device), plan);
+    sixi_b200::plan_rows(h->vocab, rows->n_rows, sixi_b200::device_sm_count(h->device), plan, h->device);
     a.data = rows->data;
     a.row_stride = rows->row_stride;
     a.dtype = rows->dtype;
@@ -214,6 +214,7 @@ int32_t sixi_smp_create(int32_t device, uint32_t max_rows, uint32_t vocab, sixi_
         e = cudaMemcpy(h->d_default, &p, sizeof(p), cudaMemcpyHostToDevice);
     }
     if (e == cudaSuccess) e = sixi_b200::prepare_kernels(device);
+    if (e == cudaSuccess) e = sixi_b200::prepare_plans(device, vocab);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking);
     for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
         e = cudaEventCreateWithFlags(&h->slot[i].copied, cudaEventDisableTiming);

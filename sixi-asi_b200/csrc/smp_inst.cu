@@ -67,4 +67,26 @@ cudaError_t prepare_mode_dt<SIXI_INST_MODE, SIXI_INST_DT>(int device) {
     return prepare_this(device);
 }
 
+#if SIXI_INST_MODE == 0 && SIXI_INST_DT == 0
+cudaError_t query_max_clusters(uint32_t cluster, size_t smem, int* n_clusters) {
+    auto kfn = row_kernel<SIXI_INST_DT, SIXI_INST_MODE>;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = prepare_this(dev);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cluster, 1, 1);
+    cfg.blockDim = dim3(kNT, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaOccupancyMaxActiveClusters(n_clusters, kfn, &cfg);
+}
+#endif
+
 }  // namespace sixi_b200

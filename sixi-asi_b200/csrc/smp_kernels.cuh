@@ -84,8 +84,17 @@ struct LaunchPlan {
 
 // Launch plan for a vocabulary and batch: the smallest cluster whose chunk fits shared memory,
 // widened (up to 8 CTAs) while the batch leaves more than half of the device's `sms` SMs idle
-// (sms = 0: no widening; the plan then only validates the vocabulary).
-bool plan_rows(uint32_t vocab, uint32_t n_rows, uint32_t sms, LaunchPlan* plan);
+// (sms = 0: no widening; the plan then only validates the vocabulary) and, when `device` >= 0 and
+// prepare_plans has run for it, while every cluster of the wider size is still resident at once
+// (clusters are placed whole within a GPC, so fewer of them fit than the SM count suggests).
+bool plan_rows(uint32_t vocab, uint32_t n_rows, uint32_t sms, LaunchPlan* plan, int device = -1);
+// Records, for `device` and the plans of `vocab`, how many clusters of each size the device holds
+// at once (cudaOccupancyMaxActiveClusters), for plan_rows. Call with `device` current, after
+// prepare_kernels, before any stream capture.
+cudaError_t prepare_plans(int device, uint32_t vocab);
+// Clusters of `cluster` CTAs with `smem` bytes of dynamic shared memory each that the current
+// device holds at once, for the row engine's launch shape (defined with the sample-mode instance).
+cudaError_t query_max_clusters(uint32_t cluster, size_t smem, int* n_clusters);
 // Streaming multiprocessors of `device` (queried once per device; 0 when the query fails).
 uint32_t device_sm_count(int device);
 cudaError_t launch_rows(int mode, const RowArgs& a, const LaunchPlan& plan, cudaStream_t stream);

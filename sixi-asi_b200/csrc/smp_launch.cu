@@ -21,14 +21,49 @@ uint32_t device_sm_count(int device) {
     return static_cast<uint32_t>(v);
 }
 
-bool plan_rows(uint32_t vocab, uint32_t n_rows, uint32_t sms, LaunchPlan* plan) {
+// Resident-cluster counts per device and cluster size (1, 2, 4, 8, 16), each packed as
+// (shared-memory bytes << 32) | clusters; 0 = not queried. plan_rows uses an entry only when its
+// shared-memory size is the plan's (the count depends on it).
+static std::atomic<uint64_t> g_max_clusters[64][5];
+
+static int cluster_slot(uint32_t c) { return c == 1 ? 0 : c == 2 ? 1 : c == 4 ? 2 : c == 8 ? 3 : c == 16 ? 4 : -1; }
+
+static uint32_t resident_clusters(int device, uint32_t c, size_t smem) {
+    const int s = cluster_slot(c);
+    if (device < 0 || device >= 64 || s < 0) return 0;
+    const uint64_t v = g_max_clusters[device][s].load(std::memory_order_relaxed);
+    return (v >> 32) == smem ? static_cast<uint32_t>(v & 0xFFFFFFFFu) : 0u;
+}
+
+cudaError_t prepare_plans(int device, uint32_t vocab) {
+    if (device < 0 || device >= 64 || vocab == 0) return cudaErrorInvalidValue;
+    for (uint32_t c = 1; c <= 16; c *= 2) {
+        if (chunk_for(vocab, c) > kMaxChunk) continue;
+        const size_t smem = make_layout(chunk_for(vocab, c), c).total;
+        if (smem > static_cast<size_t>(kMaxSmem)) continue;
+        int n = 0;
+        const cudaError_t e = query_max_clusters(c, smem, &n);
+        if (e != cudaSuccess) return e;
+        g_max_clusters[device][cluster_slot(c)].store((static_cast<uint64_t>(smem) << 32) | static_cast<uint32_t>(n),
+                                                      std::memory_order_relaxed);
+    }
+    return cudaSuccess;
+}
+
+bool plan_rows(uint32_t vocab, uint32_t n_rows, uint32_t sms, LaunchPlan* plan, int device) {
     if (vocab == 0) return false;
     uint32_t c = 1;
     while (c <= 16 && chunk_for(vocab, c) > kMaxChunk) c *= 2;
     if (c > 16) return false;
     // widen the cluster (up to 8 CTAs) while the batch would leave more than half of the SMs idle;
-    // 16-CTA clusters for a lone row measured slower (18.1 against 16.4 us per config-1 step)
-    while (c < 8 && n_rows > 0 && static_cast<uint64_t>(n_rows) * c * 2 <= sms && chunk_for(vocab, 2 * c) >= 2048) c *= 2;
+    // 16-CTA clusters for a lone row measured slower (18.1 against 16.4 us per config-1 step). A
+    // wider cluster must also leave every row resident at once: at 8 CTAs a B200 holds 16
+    // clusters, so 17 list rows took 32.7 us per step (two waves) against 24.8 us at 4 CTAs.
+    while (c < 8 && n_rows > 0 && static_cast<uint64_t>(n_rows) * c * 2 <= sms && chunk_for(vocab, 2 * c) >= 2048) {
+        const uint32_t held = resident_clusters(device, 2 * c, make_layout(chunk_for(vocab, 2 * c), 2 * c).total);
+        if (held != 0 && n_rows > held) break;
+        c *= 2;
+    }
     plan->cluster = c;
     plan->chunk = chunk_for(vocab, c);
     plan->smem = make_layout(plan->chunk, c).total;

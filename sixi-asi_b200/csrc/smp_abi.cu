@@ -214,7 +214,8 @@ int32_t sixi_smp_create(int32_t device, uint32_t max_rows, uint32_t vocab, sixi_
         e = cudaMemcpy(h->d_default, &p, sizeof(p), cudaMemcpyHostToDevice);
     }
     if (e == cudaSuccess) e = sixi_b200::prepare_kernels(device);
-    if (e == cudaSuccess) e = sixi_b200::prepare_plans(device, vocab);
+    // resident-cluster counts for the launch plans; without them the plans use the SM count alone
+    if (e == cudaSuccess && sixi_b200::prepare_plans(device, vocab) != cudaSuccess) (void)cudaGetLastError();
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking);
     for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
         e = cudaEventCreateWithFlags(&h->slot[i].copied, cudaEventDisableTiming);
